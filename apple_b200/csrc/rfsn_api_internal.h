@@ -1,0 +1,21 @@
+// rfsn_api_internal.h — host-side validation and error plumbing shared by the C-ABI entry points.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/rfsn_b200.h"
+
+namespace rfsn {
+
+// Records the CUDA error text for rfsn_last_cuda_error() and maps it to a status.
+int check_cuda(cudaError_t e);
+
+// Checks the quantizer description: shapes, codebook pointers and alignment.
+int validate_quantizer(const rfsn_quantizer* qz);
+
+// Checks a code store against the quantizer: pointers present for the enabled
+// fields, cap a multiple of 16, 16-byte aligned bases.
+int validate_store(const rfsn_code_store* s, const rfsn_quantizer* qz);
+
+}  // namespace rfsn

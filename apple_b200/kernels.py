@@ -1,0 +1,229 @@
+"""Tensor-level wrappers over the C ABI (include/rfsn_b200.h).
+
+Every function takes CUDA tensors, checks dtype/device/layout, builds the
+ABI structs and calls the library on the current torch stream.  Storage
+classes here own the device buffers of one code store or one quantizer.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+from typing import List, Optional, Sequence, Tuple
+
+import torch
+
+from . import _lib
+from ._lib import AttnArgs, CodeStore, DenseStore, Quantizer, Segment, call, lib
+
+STORE_HOT, STORE_WARM, STORE_COLD = 0, 1, 2
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def align16(n: int) -> int:
+    return (n + 15) // 16 * 16
+
+
+def _need_cuda(t: torch.Tensor, name: str) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (the RFSN B200 path has no CPU fallback)")
+
+
+@dataclass
+class QuantizerBuffers:
+    """Device codebooks of one HybridQuantizer plus the fields of ``rfsn_quantizer``."""
+    pq_codebooks: torch.Tensor           # fp16 [M, K, ds]
+    rvq_codebooks: Optional[torch.Tensor]  # fp16 [L, Kr, D] or None
+    threshold: float
+    sparse_topk: int = 0
+
+    def __post_init__(self):
+        _need_cuda(self.pq_codebooks, "pq_codebooks")
+        self.pq_codebooks = self.pq_codebooks.to(torch.float16).contiguous()
+        if self.rvq_codebooks is not None and self.rvq_codebooks.shape[0] == 0:
+            self.rvq_codebooks = None
+        if self.rvq_codebooks is not None:
+            self.rvq_codebooks = self.rvq_codebooks.to(torch.float16).contiguous()
+
+    @property
+    def M(self) -> int:
+        return self.pq_codebooks.shape[0]
+
+    @property
+    def K(self) -> int:
+        return self.pq_codebooks.shape[1]
+
+    @property
+    def ds(self) -> int:
+        return self.pq_codebooks.shape[2]
+
+    @property
+    def D(self) -> int:
+        return self.M * self.ds
+
+    @property
+    def L(self) -> int:
+        return 0 if self.rvq_codebooks is None else self.rvq_codebooks.shape[0]
+
+    @property
+    def Kr(self) -> int:
+        return 0 if self.rvq_codebooks is None else self.rvq_codebooks.shape[1]
+
+    @property
+    def rvq_code_dtype(self) -> torch.dtype:
+        return torch.uint8 if self.Kr <= 256 else torch.int16
+
+    def struct(self) -> Quantizer:
+        q = Quantizer()
+        q.pq_codebooks = _ptr(self.pq_codebooks)
+        q.rvq_codebooks = _ptr(self.rvq_codebooks)
+        q.head_dim, q.num_subspaces, q.subspace_dim, q.pq_codebook_size = self.D, self.M, self.ds, self.K
+        q.rvq_layers, q.rvq_codebook_size = self.L, self.Kr
+        q.rvq_threshold = float(self.threshold)
+        q.sparse_topk = int(self.sparse_topk)
+        return q
+
+
+class CodeStoreBuffers:
+    """Device arrays of an ``rfsn_code_store``: [slots, rows, cap, ...] per field."""
+
+    def __init__(self, qz: QuantizerBuffers, rows: int, cap: int, slots: int = 1,
+                 device: Optional[torch.device] = None, pin_memory: bool = False):
+        cap = align16(max(cap, 16))
+        dev = device if device is not None else qz.pq_codebooks.device
+        kw = dict(device="cpu", pin_memory=True) if pin_memory else dict(device=dev)
+        self.rows, self.cap, self.slots = rows, cap, slots
+        self.pq = torch.zeros((slots, rows, cap, qz.M), dtype=torch.uint8, **kw)
+        L = max(qz.L, 0)
+        self.rvq = torch.zeros((slots, rows, cap, L), dtype=qz.rvq_code_dtype, **kw) if L else None
+        self.mask = torch.zeros((slots, rows, cap), dtype=torch.uint8, **kw) if L else None
+        S = qz.sparse_topk
+        self.sp_idx = torch.zeros((slots, rows, cap, S), dtype=torch.uint8, **kw) if S else None
+        self.sp_val = torch.zeros((slots, rows, cap, S), dtype=torch.float16, **kw) if S else None
+
+    def fields(self) -> List[Optional[torch.Tensor]]:
+        return [self.pq, self.rvq, self.mask, self.sp_idx, self.sp_val]
+
+    def struct(self) -> CodeStore:
+        s = CodeStore()
+        s.pq, s.rvq, s.mask, s.sp_idx, s.sp_val = (_ptr(t) for t in self.fields())
+        s.cap, s.rows, s.slots = self.cap, self.rows, self.slots
+        return s
+
+    def nbytes_per_slot(self) -> int:
+        return sum(t[0].numel() * t.element_size() for t in self.fields() if t is not None)
+
+    def copy_slot_(self, dst_slot: int, src: "CodeStoreBuffers", src_slot: int, non_blocking: bool = True) -> None:
+        for d, s in zip(self.fields(), src.fields()):
+            if d is not None:
+                d[dst_slot].copy_(s[src_slot], non_blocking=non_blocking)
+
+    def grow(self, qz: QuantizerBuffers, new_cap: int) -> "CodeStoreBuffers":
+        new = CodeStoreBuffers(qz, self.rows, new_cap, self.slots, device=self.pq.device)
+        for d, s in zip(new.fields(), self.fields()):
+            if d is not None:
+                d[:, :, : self.cap].copy_(s)
+        return new
+
+
+def encode(qz: QuantizerBuffers, x: torch.Tensor, store: CodeStoreBuffers, slot: int, first: int,
+           residual_out: Optional[torch.Tensor] = None) -> None:
+    """Encode fp16 vectors x [B, T, H, D] (D contiguous) into rows b*H+h, tokens first..first+T."""
+    _need_cuda(x, "x")
+    if x.dtype != torch.float16 or x.dim() != 4 or x.shape[-1] != qz.D or x.stride(-1) != 1:
+        raise ValueError("x must be fp16 [B, T, H, D] with a contiguous last dim")
+    B, T, H, _ = x.shape
+    if residual_out is not None and residual_out.stride() != x.stride():
+        raise ValueError("residual_out must have the same strides as x")
+    q = qz.struct()
+    s = store.struct()
+    call("rfsn_encode", C.byref(q), _ptr(x), B, T, H, x.stride(0), x.stride(1), x.stride(2), C.byref(s),
+         slot, first, _ptr(residual_out), _stream())
+
+
+def decode_codes(qz: QuantizerBuffers, store: CodeStoreBuffers, slot: int, first: int, count: int,
+                 out: torch.Tensor) -> torch.Tensor:
+    """Exact fp16 decode of tokens [first, first+count) into out [B, count, H, D] (D contiguous)."""
+    _need_cuda(out, "out")
+    if out.dtype != torch.float16 or out.dim() != 4 or out.shape[1] != count or out.stride(-1) != 1:
+        raise ValueError("out must be fp16 [B, count, H, D]")
+    B, _, H, _ = out.shape
+    q = qz.struct()
+    s = store.struct()
+    call("rfsn_decode_codes", C.byref(q), C.byref(s), slot, first, count, B, H, _ptr(out), out.stride(0),
+         out.stride(1), out.stride(2), _stream())
+    return out
+
+
+_WORKSPACE: dict = {}
+
+
+def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
+    """Per-device scratch buffer for the split-K partials (grown on demand)."""
+    key = (device.type, device.index)
+    buf = _WORKSPACE.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _WORKSPACE[key] = buf
+    return buf
+
+
+def decode_attention(qz: QuantizerBuffers, q: torch.Tensor, out: torch.Tensor, segments: Sequence[Tuple],
+                     kv_heads: int, qpos: Optional[torch.Tensor] = None, causal: bool = True, scale: Optional[float] = None,
+                     hot: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
+                     warm: Optional[Tuple[CodeStoreBuffers, CodeStoreBuffers]] = None,
+                     cold: Optional[Tuple[CodeStoreBuffers, CodeStoreBuffers]] = None,
+                     num_ctas: int = 0, device_status: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Fused decode attention.  q/out fp16 [B, Q, Hq, D]; qpos int32 [B, Q, Hq] (global positions).
+
+    hot: (k, v) fp16 [rows, cap, D]; warm/cold: (k_store, v_store).
+    segments: (store, slot, first, count, pos0) tuples in window order.
+    """
+    _need_cuda(q, "q")
+    if q.dtype != torch.float16 or q.dim() != 4 or not q.is_contiguous():
+        raise ValueError("q must be contiguous fp16 [B, Q, Hq, D]")
+    if out.shape != q.shape or out.dtype != torch.float16 or not out.is_contiguous():
+        raise ValueError("out must be contiguous fp16 like q")
+    B, Qn, Hq, D = q.shape
+    if len(segments) > _lib.RFSN_MAX_SEGMENTS:
+        raise ValueError(f"at most {_lib.RFSN_MAX_SEGMENTS} segments per call")
+    a = AttnArgs()
+    a.q, a.out = _ptr(q), _ptr(out)
+    if causal:
+        if qpos is None or qpos.dtype != torch.int32 or tuple(qpos.shape) != (B, Qn, Hq) or not qpos.is_contiguous():
+            raise ValueError("causal attention needs contiguous int32 qpos [B, Q, Hq]")
+        a.qpos = _ptr(qpos)
+    a.batch, a.queries, a.q_heads, a.kv_heads = B, Qn, Hq, kv_heads
+    if hot is not None:
+        a.hot = DenseStore(_ptr(hot[0]), _ptr(hot[1]), hot[0].shape[1], hot[0].shape[0])
+    if warm is not None:
+        a.warm_k, a.warm_v = warm[0].struct(), warm[1].struct()
+    if cold is not None:
+        a.cold_k, a.cold_v = cold[0].struct(), cold[1].struct()
+    a.head_dim = D
+    a.causal = int(bool(causal))
+    a.scale = float(D ** -0.5 if scale is None else scale)
+    segs = (Segment * max(1, len(segments)))()
+    for i, (st, slot, first, count, pos0) in enumerate(segments):
+        segs[i].store, segs[i].slot, segs[i].first, segs[i].count, segs[i].pos0 = st, slot, first, count, pos0
+    a.segments = segs
+    a.num_segments = len(segments)
+    a.num_ctas = num_ctas
+    a.device_status = _ptr(device_status)
+    qs = qz.struct()
+    nbytes = C.c_size_t(0)
+    call("rfsn_attention_workspace_size", C.byref(a), C.byref(qs), C.byref(nbytes))
+    ws = workspace(nbytes.value, q.device)
+    a.workspace, a.workspace_bytes = _ptr(ws), ws.numel()
+    call("rfsn_decode_attention", C.byref(a), C.byref(qs), _stream())
+    return out
+
+
+def version() -> int:
+    return lib().rfsn_version()

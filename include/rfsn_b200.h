@@ -1,0 +1,174 @@
+/*
+ * rfsn_b200.h — C ABI of the B200-native RFSN compressed-KV decode path.
+ *
+ * The reference (dawsonblock/apple, RFSN v10.2) is pure Python on Apple MLX and
+ * has no FFI: its boundary is the Python class API (RFSNv10KVCacheMLX,
+ * HybridQuantizerMLX, RFSNHybridAttentionMLX, AsyncHierarchicalRouterMLX).
+ * Each entry point below replaces the MLX computation behind one of those
+ * methods; the comment on each names the reference lines (file:line, relative
+ * to the reference project root) whose behaviour it reproduces.
+ *
+ * Conventions
+ *   - Plain C: pointers, sizes, plain structs.  No C++ or torch types.
+ *   - Every device pointer is caller-owned; nothing is allocated inside the
+ *     library except CUDA's own launch resources.
+ *   - Every call is stream-ordered on the given cudaStream_t (passed as void*;
+ *     NULL = legacy default stream) and returns an int status (0 = RFSN_OK,
+ *     negative = error, see rfsn_status).  No exception crosses the ABI.
+ *   - fp16 tensors are passed as uint16_t* holding IEEE binary16 bits.
+ *   - A "row" is one (batch, kv-head) pair: row = b * num_kv_heads + h.
+ */
+#ifndef RFSN_B200_H
+#define RFSN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RFSN_ABI_VERSION 1
+#define RFSN_MAX_SEGMENTS 256   /* segments per attention call (hot/warm/cold pieces) */
+#define RFSN_MAX_ROWS_PER_KV 8  /* query rows (queries x GQA group) sharing one KV head */
+
+typedef enum rfsn_status {
+  RFSN_OK = 0,
+  RFSN_ERR_INVALID_ARGUMENT = -1,
+  RFSN_ERR_UNSUPPORTED = -2,
+  RFSN_ERR_CUDA = -3,
+  RFSN_ERR_WORKSPACE_TOO_SMALL = -4,
+  RFSN_ERR_DEVICE_TIMEOUT = -5, /* a bounded device-side wait expired; outputs are invalid */
+  RFSN_ERR_ALIGNMENT = -6
+} rfsn_status;
+
+/* Library version (RFSN_ABI_VERSION * 1000 + minor). */
+int rfsn_version(void);
+
+/* Human-readable text for a status code (static string). */
+const char* rfsn_status_string(int status);
+
+/* Last CUDA error text recorded by a call on this host thread ("" if none). */
+const char* rfsn_last_cuda_error(void);
+
+/* ------------------------------------------------------------------------ */
+/* Quantizer: the codebooks of HybridQuantizerMLX (quantization.py:296-319).  */
+/* ------------------------------------------------------------------------ */
+typedef struct rfsn_quantizer {
+  const uint16_t* pq_codebooks;  /* fp16 [M][K][ds]  (ProductQuantizerMLX.codebooks, quantization.py:109-115) */
+  const uint16_t* rvq_codebooks; /* fp16 [L][Kr][D]  (ResidualVQMLX.codebooks, quantization.py:189-197); NULL if L == 0 */
+  int32_t head_dim;              /* D = M * ds (storage.py:53-59) */
+  int32_t num_subspaces;         /* M */
+  int32_t subspace_dim;          /* ds */
+  int32_t pq_codebook_size;      /* K <= 256 (codes are uint8) */
+  int32_t rvq_layers;            /* L (0 = PQ only) */
+  int32_t rvq_codebook_size;     /* Kr; codes stored as uint8 when Kr <= 256, else uint16 */
+  float rvq_threshold;           /* token gets RVQ codes iff ||pq residual||_2 > threshold (quantization.py:216-218) */
+  int32_t sparse_topk;           /* S: extension, top-S |error| fp16 entries per token (0 = off) */
+} rfsn_quantizer;
+
+/* Compressed code store (the device form of CompressedTensorMLX, storage.py:75-98).
+ * Dense per-token layout: token t of row r in slot s lives at index
+ * (s * rows + r) * cap + t of every array.  RVQ codes are stored for every
+ * token (zero when inactive) next to a per-token activity byte, instead of the
+ * reference's (codes, offsets) pair; rvq[mask] and flatnonzero(mask) give the
+ * reference form back. */
+typedef struct rfsn_code_store {
+  uint8_t* pq;       /* uint8  [slots][rows][cap][M] */
+  void* rvq;         /* uint8 or uint16 [slots][rows][cap][L] */
+  uint8_t* mask;     /* uint8  [slots][rows][cap]  1 = RVQ active */
+  uint8_t* sp_idx;   /* uint8  [slots][rows][cap][S] */
+  uint16_t* sp_val;  /* fp16   [slots][rows][cap][S] */
+  int64_t cap;       /* tokens per row; multiple of 16 */
+  int64_t rows;      /* rows per slot (batch * kv heads) */
+  int64_t slots;     /* number of slots (1 for hot/warm stores; >1 for a cold chunk pool) */
+} rfsn_code_store;
+
+/* Dense fp16 store for exact (hot) tokens: [rows][cap][D]. */
+typedef struct rfsn_dense_store {
+  const uint16_t* k;
+  const uint16_t* v;
+  int64_t cap;   /* tokens per row */
+  int64_t rows;  /* rows in the store (>= batch * kv heads) */
+} rfsn_dense_store;
+
+/* Spill encoder — HybridQuantizerMLX.encode (quantization.py:305-308) =
+ * ProductQuantizerMLX.quantize (:124-144) + ResidualVQMLX.encode (:206-252),
+ * plus the top-S sparse residual extension; applied per token like
+ * _compress_tensor_sequence (:330-343) and written straight into a code store
+ * the way RFSNv10KVCacheMLX._add_to_warm / _add_to_cold append (cache.py:122-191).
+ *
+ * x: fp16, vector (b, t, h) at x[b*stride_b + t*stride_t + h*stride_h], D contiguous.
+ * Vector (b, t, h) is written to row b*heads + h, token dst_first + t of slot dst_slot.
+ * residual_out (optional, may be NULL): fp16 PQ residual in the same layout as x. */
+int rfsn_encode(const rfsn_quantizer* qz, const uint16_t* x, int64_t batch, int64_t tokens, int64_t heads,
+                int64_t stride_b, int64_t stride_t, int64_t stride_h, const rfsn_code_store* dst,
+                int64_t dst_slot, int64_t dst_first, uint16_t* residual_out, void* stream);
+
+/* Decode compressed tokens to dense fp16 — _decode_compressed_tensor (quantization.py:394-402),
+ * i.e. fp16(pq_decode + rvq_correction) (:319) plus the sparse residual added in fp32 and
+ * rounded once.  Tokens [first, first+count) of every row of slot `slot`; token i of row
+ * (b, h) goes to out[b*stride_b + i*stride_t + h*stride_h] (D contiguous).  This is what
+ * RFSNv10KVCacheMLX.materialize_window (cache.py:344-393) returns for warm/cold tokens. */
+int rfsn_decode_codes(const rfsn_quantizer* qz, const rfsn_code_store* src, int64_t slot, int64_t first,
+                      int64_t count, int64_t batch, int64_t heads, uint16_t* out, int64_t stride_b,
+                      int64_t stride_t, int64_t stride_h, void* stream);
+
+/* One contiguous run of window tokens in one store. */
+typedef struct rfsn_segment {
+  int32_t store;   /* 0 = hot dense store, 1 = warm code store, 2 = cold code pool */
+  int32_t slot;    /* slot in the store (cold pool) */
+  int32_t first;   /* first token index inside the row storage */
+  int32_t count;   /* number of tokens */
+  int32_t pos0;    /* global sequence position of token `first` (causal masking) */
+  int32_t reserved[3];
+} rfsn_segment;
+
+/* Fused decode attention — RFSNv10KVCacheMLX.attention_forward (cache.py:395-428) =
+ * materialize_window (:344-393) + _blockwise_exact_attention (attention.py:39-105),
+ * without materialising the window: PQ/RVQ/sparse codes are decoded inside a
+ * flash-decoding split-K kernel and partial (max, sum, acc) triples are merged by
+ * log-sum-exp.  Also covers RFSNHybridAttentionMLX.__call__ (attention.py:150-170).
+ *
+ * q / out: fp16 [batch][queries][q_heads][D]; query head hq reads KV head hq / (q_heads/kv_heads).
+ * qpos: int32 [batch][queries][q_heads] global positions; key at position p is visible
+ *       iff p <= qpos (causal); ignored when causal == 0.
+ * segments: host array in window (position) order; their token counts sum to the window.
+ * An empty window writes zeros (cache.py:417-418). */
+typedef struct rfsn_attn_args {
+  const uint16_t* q;
+  const int32_t* qpos;
+  uint16_t* out;
+  int32_t batch, queries, q_heads, kv_heads, head_dim;
+  int32_t causal;
+  float scale;                     /* head_dim ** -0.5 in the reference (cache.py:424) */
+  rfsn_dense_store hot;
+  rfsn_code_store warm_k, warm_v;
+  rfsn_code_store cold_k, cold_v;
+  const rfsn_segment* segments;
+  int32_t num_segments;
+  int32_t num_ctas;                /* 0 = one CTA per SM */
+  void* workspace;                 /* device scratch, >= rfsn_attention_workspace_size() bytes */
+  size_t workspace_bytes;
+  int32_t* device_status;          /* optional device int32: set non-zero by a kernel that hit a bounded-wait timeout */
+} rfsn_attn_args;
+
+/* Bytes of device workspace rfsn_decode_attention needs for these arguments. */
+int rfsn_attention_workspace_size(const rfsn_attn_args* args, const rfsn_quantizer* qz, size_t* bytes);
+
+int rfsn_decode_attention(const rfsn_attn_args* args, const rfsn_quantizer* qz, void* stream);
+
+/* Cold tier transfer — replaces load_compressed_chunk / np.load in the router's
+ * executor (storage.py:138-140, 226-234): one cudaMemcpyAsync of `bytes` from
+ * pinned host memory to device memory on `stream` (the router's side stream),
+ * followed by a record of `event` (a cudaEvent_t, may be NULL) on that stream. */
+int rfsn_cold_prefetch(void* dst_device, const void* src_pinned_host, size_t bytes, void* stream, void* event);
+
+/* Device-to-host counterpart used when warm chunks age out to the cold tier
+ * (save_compressed_chunk, storage.py:117-135). */
+int rfsn_cold_evict(void* dst_pinned_host, const void* src_device, size_t bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RFSN_B200_H */

@@ -1,0 +1,275 @@
+"""GPU parity of the C-ABI kernels against the CPU oracle and the reference's golden fixtures.
+
+Tolerances:
+* PQ/RVQ/sparse codes: bit-exact, except where the two best candidates tie to
+  fp32 rounding (checked in float64: |d_gpu - d_ref| <= 1e-5 * d_ref); RVQ and
+  sparse codes are compared on vectors whose PQ codes agree.
+* decoded K/V (rfsn_decode_codes): bit-exact fp16 (well inside 1e-3 absolute).
+* attention outputs: |out - ref| <= 2e-3 * |ref| + 2e-3 * rms(ref) element-wise
+  (fp32 accumulation; only summation order and one fp16 rounding of the
+  sparse-corrected value differ from the oracle).
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import restate as R
+from tests.conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+
+if torch.cuda.is_available():
+    from apple_b200 import kernels as K
+    from tests.gpu_util import codes_to_store, to_dev
+
+QUANT_CASES = ["quant_d128_m8x16_rvq3", "quant_d64_m16x4_rvq1_dense", "quant_d64_m8x8_rvq1", "quant_d64_m8x8_pqonly"]
+
+
+def assert_attn_close(out, ref, what=""):
+    out = np.asarray(out, np.float32)
+    ref = np.asarray(ref, np.float32)
+    rms = float(np.sqrt(np.mean(ref ** 2))) if ref.size else 0.0
+    err = np.abs(out - ref)
+    tol = 2e-3 * np.abs(ref) + 2e-3 * rms
+    bad = err > tol
+    assert not bad.any(), f"{what}: {int(bad.sum())} elements off, max err {err.max():.3e} (rms ref {rms:.3e})"
+
+
+def quantizer_from(g, sparse=0):
+    return K.QuantizerBuffers(to_dev(g["pq_codebooks"]), to_dev(g["rvq_codebooks"]), float(g["threshold"]), sparse)
+
+
+def pq_tie_ok(x, cb, got, want):
+    ds = cb.shape[2]
+    for n, m in zip(*np.nonzero(got != want)):
+        sub = x[n, m * ds:(m + 1) * ds].astype(np.float64)
+        d = ((cb[m].astype(np.float64) - sub) ** 2).sum(1)
+        a, b = d[got[n, m]], d[want[n, m]]
+        assert abs(a - b) <= 1e-5 * max(abs(b), 1e-3), (n, m, a, b)
+
+
+@pytest.mark.parametrize("name", QUANT_CASES)
+def test_encode_matches_reference_codes(name):
+    g = dict(np.load(GOLDEN / f"{name}.npz"))
+    qz = quantizer_from(g)
+    x = to_dev(g["x"])
+    N, D = x.shape
+    store = K.CodeStoreBuffers(qz, rows=1, cap=N)
+    res = torch.empty_like(x)
+    K.encode(qz, x.view(1, N, 1, D), store, 0, 0, residual_out=res.view(1, N, 1, D))
+    torch.cuda.synchronize()
+    pq = store.pq[0, 0, :N].cpu().numpy()
+    pq_tie_ok(g["x"], g["pq_codebooks"], pq, g["pq_codes"])
+    agree = (pq == g["pq_codes"]).all(axis=1)
+    assert agree.mean() > 0.99
+    np.testing.assert_array_equal(res.cpu().numpy()[agree].view(np.uint16), g["residual"][agree].view(np.uint16))
+    if qz.L:
+        mask = store.mask[0, 0, :N].cpu().numpy().astype(bool)
+        np.testing.assert_array_equal(mask[agree], g["rvq_mask"][agree])
+        dense = np.zeros((N, qz.L), np.int64)
+        dense[g["rvq_offsets"]] = g["rvq_codes"]
+        got = store.rvq[0, 0, :N].cpu().numpy().astype(np.int64)
+        sel = agree & g["rvq_mask"]
+        assert ((got[sel] == dense[sel]).all(axis=1)).mean() > 0.99
+
+
+@pytest.mark.parametrize("name", QUANT_CASES)
+def test_decode_codes_bit_exact(name):
+    g = dict(np.load(GOLDEN / f"{name}.npz"))
+    qz = quantizer_from(g)
+    N, D = g["x"].shape
+    dense = np.zeros((N, qz.L), np.uint16)
+    dense[g["rvq_offsets"]] = g["rvq_codes"]
+    codes = R.Codes(g["pq_codes"][:, None], dense[:, None], g["rvq_mask"][:, None],
+                    np.zeros((N, 1, 0), np.uint8), np.zeros((N, 1, 0), np.float16))
+    store = codes_to_store(qz, [R.Codes(codes.pq[:, 0], codes.rvq[:, 0], codes.mask[:, 0], codes.sp_idx[:, 0],
+                                        codes.sp_val[:, 0])], cap=N)
+    out = torch.empty((1, N, 1, D), dtype=torch.float16, device="cuda")
+    K.decode_codes(qz, store, 0, 0, N, out)
+    np.testing.assert_array_equal(out.cpu().numpy()[0, :, 0].view(np.uint16), g["decoded"].view(np.uint16))
+
+
+def test_sparse_encode_and_decode_match_oracle():
+    g = dict(np.load(GOLDEN / "quant_d64_m16x4_rvq1_dense.npz"))
+    S = 8
+    qz = quantizer_from(g, sparse=S)
+    oq = R.Quantizer(g["pq_codebooks"], g["rvq_codebooks"], float(g["threshold"]), sparse_topk=S)
+    x = g["x"]
+    N, D = x.shape
+    ref = oq.compress(x[:, None])
+    store = K.CodeStoreBuffers(qz, rows=1, cap=N)
+    K.encode(qz, to_dev(x).view(1, N, 1, D), store, 0, 0)
+    pq = store.pq[0, 0, :N].cpu().numpy()
+    agree = (pq == ref.pq[:, 0]).all(axis=1)
+    assert agree.mean() > 0.99
+    np.testing.assert_array_equal(store.sp_idx[0, 0, :N].cpu().numpy()[agree], ref.sp_idx[agree, 0])
+    np.testing.assert_array_equal(store.sp_val[0, 0, :N].cpu().numpy()[agree].view(np.uint16),
+                                  ref.sp_val[agree, 0].view(np.uint16))
+    # decode of the oracle's codes is bit-exact with the oracle decode
+    st2 = codes_to_store(qz, [R.Codes(ref.pq[:, 0], ref.rvq[:, 0], ref.mask[:, 0], ref.sp_idx[:, 0],
+                                      ref.sp_val[:, 0])], cap=N)
+    out = torch.empty((1, N, 1, D), dtype=torch.float16, device="cuda")
+    K.decode_codes(qz, st2, 0, 0, N, out)
+    np.testing.assert_array_equal(out.cpu().numpy()[0, :, 0].view(np.uint16), oq.decode(ref)[:, 0].view(np.uint16))
+
+
+def _qpos_global(adjusted, window_start, shape):
+    a = np.broadcast_to(np.asarray(adjusted, np.int32).reshape(shape[0], -1), shape[:2]).astype(np.int64)
+    return (np.maximum(a, -1) + window_start).astype(np.int32)
+
+
+def test_hybrid_attention_golden():
+    """RFSNHybridAttentionMLX case of the reference suite (rfsn_v10_mlx_ane_complete.py:418-446)."""
+    g = dict(np.load(GOLDEN / "attention_hybrid.npz"))
+    qz = quantizer_from(g)
+    oq = R.Quantizer(g["pq_codebooks"], g["rvq_codebooks"], float(g["threshold"]))
+    kc, vc = oq.compress(g["keys"]), oq.compress(g["values"])
+    H, T = 4, 24
+    per_row_k = [kc.slice(0, T) for _ in range(H)]
+    ks = codes_to_store(qz, [R.Codes(kc.pq[:, h], kc.rvq[:, h], kc.mask[:, h], kc.sp_idx[:, h], kc.sp_val[:, h])
+                             for h in range(H)], cap=T)
+    vs = codes_to_store(qz, [R.Codes(vc.pq[:, h], vc.rvq[:, h], vc.mask[:, h], vc.sp_idx[:, h], vc.sp_val[:, h])
+                             for h in range(H)], cap=T)
+    del per_row_k
+    q = to_dev(g["q"]).view(1, 2, H, 128)  # two queries against one sequence
+    out = torch.empty_like(q)
+    seg = [(K.STORE_WARM, 0, 0, T, 0)]
+    for key, causal, pos in (("out_causal", True, g["positions"]), ("out_plain", False, None),
+                             ("out_bh", True, g["positions_bh"])):
+        qpos = None
+        if causal:
+            qpos = to_dev(np.broadcast_to(np.asarray(pos, np.int32).reshape(2, -1), (2, H)).reshape(1, 2, H).copy())
+        K.decode_attention(qz, q, out, seg, kv_heads=H, qpos=qpos, causal=causal, warm=(ks, vs))
+        assert_attn_close(out.cpu().numpy()[0], g[key], key)
+
+
+def _oracle_cache_from_golden(g):
+    cfg = R.OracleConfig(hidden_dim=512, num_heads=4, head_dim=128, num_subspaces=8, subspace_dim=16,
+                         num_rvq_layers=3, rvq_codebook_size=256, rvq_sparsity_threshold=0.25,
+                         hot_capacity=16, warm_capacity=24, block_size_seq=16)
+    oq = R.Quantizer(g["pq_codebooks"], g["rvq_codebooks"], float(g["threshold"]))
+    c = R.OracleCache(cfg, oq, batch=1)
+    s = int(g["update_split"])
+    c.update(g["keys"][None, :s], g["values"][None, :s])
+    c.update(g["keys"][None, s:], g["values"][None, s:])
+    return c
+
+
+@pytest.mark.parametrize("num_ctas", [0, 1, 3, 37])
+def test_tiered_attention_golden(num_ctas):
+    """hot + warm + two cold chunks (cache.py tiering) vs the reference's outputs, all windows."""
+    g = dict(np.load(GOLDEN / "cache_tiers.npz"))
+    oc = _oracle_cache_from_golden(g)
+    qz = quantizer_from(g)
+    H, D = 4, 128
+    hot_k = to_dev(np.ascontiguousarray(g["keys"][:16].transpose(1, 0, 2)))
+    hot_v = to_dev(np.ascontiguousarray(g["values"][:16].transpose(1, 0, 2)))
+
+    def rows(c):
+        return [R.Codes(c.pq[:, h], c.rvq[:, h], c.mask[:, h], c.sp_idx[:, h], c.sp_val[:, h]) for h in range(H)]
+
+    wk = codes_to_store(qz, rows(oc.warm_k[0]), cap=32)
+    wv = codes_to_store(qz, rows(oc.warm_v[0]), cap=32)
+    ck = K.CodeStoreBuffers(qz, rows=H, cap=16, slots=len(oc.cold))
+    cv = K.CodeStoreBuffers(qz, rows=H, cap=16, slots=len(oc.cold))
+    for i, meta in enumerate(oc.cold):
+        codes_to_store(qz, rows(meta["k"][0]), cap=16, store=ck, slot=i)
+        codes_to_store(qz, rows(meta["v"][0]), cap=16, store=cv, slot=i)
+    q = to_dev(g["q"]).view(1, 1, H, D)
+    out = torch.empty_like(q)
+    spans = [(K.STORE_HOT, 0, 0, 16), (K.STORE_WARM, 0, 16, 24)] + \
+            [(K.STORE_COLD, i, m["start_token"], m["num_tokens"]) for i, m in enumerate(oc.cold)]
+    for i, (qpos, win) in enumerate(g["cases"]):
+        tag = f"q{i // 3}_w{i % 3}"
+        win = None if win < 0 else int(win)
+        start, end, adj = R.window_bounds(60, [int(qpos)], win, None)
+        segs = []
+        for st, slot, s0, n in spans:
+            a, b = max(start, s0), min(end, s0 + n)
+            if a < b:
+                segs.append((st, slot, a - s0, b - a, a))
+        qp = to_dev(_qpos_global(adj, start, (1, 1)).repeat(H).reshape(1, 1, H))
+        K.decode_attention(qz, q, out, segs, kv_heads=H, qpos=qp, causal=True, hot=(hot_k, hot_v),
+                           warm=(wk, wv), cold=(ck, cv), num_ctas=num_ctas)
+        assert_attn_close(out.cpu().numpy()[0], g[f"{tag}_out"], tag)
+
+
+def _make_cfg2_like(rng, B, Hkv, G, D, T_hot, T_warm, S=8, ds=4, L=1, thr=-1.0, outliers=4):
+    M = D // ds
+    pq_cb = (rng.standard_normal((M, 256, ds)) * np.sqrt(2.0 / ds)).astype(np.float16)
+    rvq_cb = (rng.standard_normal((L, 256, D)) * np.sqrt(2.0 / D)).astype(np.float16) if L else \
+        np.zeros((0, 256, D), np.float16)
+    if L:
+        rvq_cb[:, 0] = 0
+    T = T_hot + T_warm
+    k = rng.standard_normal((B, T, Hkv, D)).astype(np.float32)
+    if outliers:
+        k[..., rng.choice(D, outliers, replace=False)] *= 10
+    k = k.astype(np.float16)
+    v = rng.standard_normal((B, T, Hkv, D)).astype(np.float16)
+    return pq_cb, rvq_cb, k, v
+
+
+@pytest.mark.parametrize("B,Hkv,G,Qn,D,ds,L,S,thr,T_hot,T_warm,num_ctas", [
+    (2, 8, 4, 1, 64, 4, 1, 8, -1.0, 300, 2000, 0),     # config-2 shape (small T)
+    (2, 8, 4, 1, 64, 4, 1, 8, -1.0, 300, 2000, 5),
+    (1, 4, 2, 4, 64, 8, 2, 0, 0.5, 64, 700, 0),        # R = 8 query rows per KV head, gated RVQ
+    (3, 2, 1, 1, 64, 8, 0, 0, 0.0, 128, 1000, 11),     # PQ only, no GQA
+    (1, 2, 2, 1, 128, 16, 1, 4, -1.0, 50, 400, 0),     # D = 128
+])
+def test_fused_attention_vs_oracle(B, Hkv, G, Qn, D, ds, L, S, thr, T_hot, T_warm, num_ctas):
+    rng = np.random.default_rng(B * 1000 + Hkv * 10 + D + L)
+    pq_cb, rvq_cb, k, v = _make_cfg2_like(rng, B, Hkv, G, D, T_hot, T_warm, S=S, ds=ds, L=L, thr=thr)
+    oq = R.Quantizer(pq_cb, rvq_cb, thr, sparse_topk=S)
+    qz = K.QuantizerBuffers(to_dev(pq_cb), to_dev(rvq_cb) if L else None, thr, S)
+    # warm = oldest tokens (encoded), hot = newest (exact), like hot_policy="recent"
+    kc = [oq.compress(k[b, :T_warm]) for b in range(B)]
+    vc = [oq.compress(v[b, :T_warm]) for b in range(B)]
+
+    def rows(cs):
+        return [R.Codes(c.pq[:, h], c.rvq[:, h], c.mask[:, h], c.sp_idx[:, h], c.sp_val[:, h])
+                for c in cs for h in range(Hkv)]
+
+    wk = codes_to_store(qz, rows(kc), cap=T_warm)
+    wv = codes_to_store(qz, rows(vc), cap=T_warm)
+    hot_k = to_dev(np.ascontiguousarray(k[:, T_warm:].transpose(0, 2, 1, 3).reshape(B * Hkv, T_hot, D)))
+    hot_v = to_dev(np.ascontiguousarray(v[:, T_warm:].transpose(0, 2, 1, 3).reshape(B * Hkv, T_hot, D)))
+    Hq = Hkv * G
+    q = rng.standard_normal((B, Qn, Hq, D)).astype(np.float16)
+    T = T_hot + T_warm
+    pos = rng.integers(T // 2, T, size=(B, Qn, Hq)).astype(np.int32)
+    pos[:, 0, 0] = T - 1
+    segs = [(K.STORE_WARM, 0, 0, T_warm, 0), (K.STORE_HOT, 0, 0, T_hot, T_warm)]
+    out = torch.empty((B, Qn, Hq, D), dtype=torch.float16, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    K.decode_attention(qz, to_dev(q), out, segs, kv_heads=Hkv, qpos=to_dev(pos), causal=True,
+                       hot=(hot_k, hot_v), warm=(wk, wv), num_ctas=num_ctas, device_status=status)
+    got = out.cpu().numpy()
+    assert int(status.item()) == 0
+    for b in range(B):
+        kw = np.concatenate([oq.decode(kc[b]), k[b, T_warm:]], 0)
+        vw = np.concatenate([oq.decode(vc[b]), v[b, T_warm:]], 0)
+        ref = R.blockwise_exact_attention(q[b].reshape(Qn, Hq, D), kw, vw, D ** -0.5, 128, True, pos[b])
+        assert_attn_close(got[b], ref, f"batch {b}")
+
+
+def test_empty_window_writes_zeros():
+    rng = np.random.default_rng(0)
+    pq_cb = rng.standard_normal((8, 256, 8)).astype(np.float16)
+    qz = K.QuantizerBuffers(to_dev(pq_cb), None, 0.0)
+    q = torch.randn(1, 1, 4, 64, device="cuda").half()
+    out = torch.full_like(q, 7.0)
+    K.decode_attention(qz, q, out, [], kv_heads=4, qpos=torch.zeros(1, 1, 4, dtype=torch.int32, device="cuda"))
+    assert torch.count_nonzero(out).item() == 0
+
+
+def test_abi_rejects_out_of_range_segment():
+    rng = np.random.default_rng(1)
+    pq_cb = rng.standard_normal((8, 256, 8)).astype(np.float16)
+    qz = K.QuantizerBuffers(to_dev(pq_cb), None, 0.0)
+    st = K.CodeStoreBuffers(qz, rows=4, cap=32)
+    q = torch.randn(1, 1, 4, 64, device="cuda").half()
+    out = torch.empty_like(q)
+    from apple_b200 import RFSNError
+    with pytest.raises(RFSNError):
+        K.decode_attention(qz, q, out, [(K.STORE_WARM, 0, 20, 20, 0)], kv_heads=4, causal=False, warm=(st, st))
