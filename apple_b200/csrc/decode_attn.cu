@@ -39,6 +39,7 @@ constexpr int kStages = 3;
 constexpr int kStageBytes = 32 * 1024;
 constexpr int kNumFields = 10;  // k/v x {pq, rvq, mask, sp_idx, sp_val}
 constexpr int kChunk = 8;       // tokens per warp chunk (2 row-steps of 4 tokens)
+constexpr int64_t kMaxSmem = 227 * 1024;  // opt-in shared memory per CTA on sm_100
 
 struct SegDev {
   int store, slot, first, count, pos0, wstart;
@@ -674,18 +675,23 @@ static int make_plan(const rfsn_attn_args* a, const rfsn_quantizer* qz, Plan& pl
   pl.nw = consumer_warps(p.D, pl.rmax);
   const int64_t pq_bytes = (int64_t)p.M * p.K * p.ds * 2;
   const int64_t rvq_bytes = (int64_t)p.L * p.Kr * p.D * 2;
-  pl.rvq_smem = p.L > 0 && rvq_bytes <= 64 * 1024;
-  int64_t off = (int64_t)kStages * kStageBytes;
-  p.smem_pq = (int)off; off = align_up(off + pq_bytes, 128);
-  p.smem_rvq = (int)off; if (pl.rvq_smem) off = align_up(off + rvq_bytes, 128);
-  p.smem_qtab = (int)off; off = align_up(off + (int64_t)pl.nw * p.D * pl.rmax * 4, 128);
-  p.smem_vsp = (int)off; off = align_up(off + (int64_t)pl.nw * pl.rmax * p.D * 4, 128);
-  p.smem_ml = (int)off; off = align_up(off + (int64_t)pl.nw * pl.rmax * 2 * 4, 128);
-  p.smem_desc = (int)off; off = align_up(off + (int64_t)kStages * sizeof(TileDesc), 128);
-  p.smem_bar = (int)off; off = align_up(off + (2 * kStages + 1) * 8, 128);
-  p.smem_flag = (int)off; off = align_up(off + 16, 128);
-  pl.smem = off;
-  if (pl.smem > 227 * 1024) return RFSN_ERR_UNSUPPORTED;
+  // Shared-memory layout; the RVQ codebook is staged only if it fits (else it
+  // is read through L1/L2 from global memory).
+  for (int attempt = 0; attempt < 2; ++attempt) {
+    pl.rvq_smem = attempt == 0 && p.L > 0 && rvq_bytes <= 64 * 1024;
+    int64_t off = (int64_t)kStages * kStageBytes;
+    p.smem_pq = (int)off; off = align_up(off + pq_bytes, 128);
+    p.smem_rvq = (int)off; if (pl.rvq_smem) off = align_up(off + rvq_bytes, 128);
+    p.smem_qtab = (int)off; off = align_up(off + (int64_t)pl.nw * p.D * pl.rmax * 4, 128);
+    p.smem_vsp = (int)off; off = align_up(off + (int64_t)pl.nw * pl.rmax * p.D * 4, 128);
+    p.smem_ml = (int)off; off = align_up(off + (int64_t)pl.nw * pl.rmax * 2 * 4, 128);
+    p.smem_desc = (int)off; off = align_up(off + (int64_t)kStages * sizeof(TileDesc), 128);
+    p.smem_bar = (int)off; off = align_up(off + (2 * kStages + 1) * 8, 128);
+    p.smem_flag = (int)off; off = align_up(off + 16, 128);
+    pl.smem = off;
+    if (pl.smem <= kMaxSmem) break;
+  }
+  if (pl.smem > kMaxSmem) return RFSN_ERR_UNSUPPORTED;
 
   // work split: equal contiguous ranges of the flattened (row, token) space
   const int64_t total = p.rows * W;

@@ -1,0 +1,446 @@
+"""Config, compressed-tensor container, pinned-host cold tier and the async router.
+
+Mirrors storage.py of the reference (RFSNConfig storage.py:19-59,
+CompressedTensorMLX :75-98, chunk IO :113-151, AsyncHierarchicalRouterMLX
+:154-237).  The cold tier moves from zlib NPZ files on disk to pinned host
+memory: each chunk is a pinned code store (same codes the reference writes to
+``layer{L}_chunk{id}.npz``), copied into a device-resident chunk pool with
+``rfsn_cold_prefetch`` (cudaMemcpyAsync) — by the router on its side stream
+ahead of time, or by the cache on the compute stream on a miss.
+"""
+from __future__ import annotations
+
+import asyncio
+import logging
+import threading
+from collections import OrderedDict
+from dataclasses import dataclass, field
+from pathlib import Path
+from typing import Dict, List, Optional, Tuple
+
+import numpy as np
+import torch
+
+from . import kernels as K
+
+logger = logging.getLogger("RFSN_STORAGE")
+
+SUPPORTED_GROUP_SIZES = (128, 64, 32)
+MASK_FILL_VALUE = -1e30
+
+
+@dataclass
+class RFSNConfig:
+    """Hyperparameters (storage.py:19-59) plus the B200 build's extensions.
+
+    Extensions (all default to the reference behaviour):
+      num_kv_heads      KV heads (GQA); None = num_heads.
+      batch_size        independent sequences per cache (reference: 1).
+      hot_policy        "prefix" (reference: hot = first tokens) or "recent"
+                        (hot = newest tokens; older tokens spill hot->warm->cold).
+      sparse_topk       top-S |error| fp16 residual entries per token (0 = off).
+      cold_chunk_tokens cold chunk length (None = block_size_seq, as cache.py:144).
+      cold_pool_chunks  device-resident cold chunk slots (LRU).
+      device            CUDA device of the cache and quantizer.
+    """
+
+    hidden_dim: int = 4096
+    num_heads: int = 32
+    head_dim: int = 128
+    num_layers: int = 32
+
+    num_subspaces: int = 8
+    pq_bits: int = 8
+    subspace_dim: int = 16
+    pq_codebook_dtype: str = "float16"
+
+    num_rvq_layers: int = 4
+    rvq_codebook_size: int = 4096
+    rvq_sparsity_threshold: float = 0.005
+    max_rvq_sparse: int = 64
+
+    hot_capacity: int = 8192
+    warm_capacity: int = 65536
+    cold_capacity: int = 2_000_000
+
+    block_size_seq: int = 128
+
+    ane_quant_bits: int = 6
+    ane_group_size: int = 128
+
+    disk_cache_dir: str = "./rfsn_disk_cache"
+    max_open_files: int = 8
+    prefetch_throttle_s: float = 0.5
+
+    cpu_threads: int = 4
+
+    num_kv_heads: Optional[int] = None
+    batch_size: int = 1
+    hot_policy: str = "prefix"
+    sparse_topk: int = 0
+    cold_chunk_tokens: Optional[int] = None
+    cold_pool_chunks: int = 32
+    device: str = "cuda"
+
+    def __post_init__(self) -> None:
+        expected = self.num_subspaces * self.subspace_dim
+        if expected != self.head_dim:
+            raise ValueError(
+                "head_dim must equal num_subspaces * subspace_dim: "
+                f"{self.head_dim} != {expected}"
+            )
+        if self.hot_policy not in ("prefix", "recent"):
+            raise ValueError("hot_policy must be 'prefix' or 'recent'")
+        if self.num_kv_heads is not None and self.num_heads % self.num_kv_heads:
+            raise ValueError("num_heads must be a multiple of num_kv_heads")
+
+    @property
+    def kv_heads(self) -> int:
+        return self.num_kv_heads or self.num_heads
+
+    @property
+    def chunk_tokens(self) -> int:
+        return max(1, self.cold_chunk_tokens or self.block_size_seq)
+
+
+@dataclass
+class QuantizedMatrix:
+    """Affine-quantised 2-D tensor (storage.py:62-72).  Kept for API parity; the
+    Apple-specific 6-bit codebook path is not part of the B200 build."""
+    weights: torch.Tensor
+    scales: torch.Tensor
+    biases: torch.Tensor
+    bits: int
+    group_size: int
+    transposed: bool
+    original_shape: Tuple[int, ...]
+
+
+class CompressedTensorMLX:
+    """Compressed [T, H, D] tensor (storage.py:75-98) in the device layout.
+
+    Fields: pq_codes uint8 [T, H, M]; rvq uint8/int16 [T, H, L] for every token
+    (zero when inactive); rvq_mask bool [T, H]; sp_idx uint8 [T, H, S];
+    sp_val fp16 [T, H, S].  ``rvq_codes`` / ``rvq_offsets`` give the
+    reference's sparse (codes [A, L], flat offsets t*H+h [A]) form.
+    """
+
+    def __init__(self, pq_codes, rvq, rvq_mask, sp_idx, sp_val, num_heads: int):
+        self.pq_codes = pq_codes
+        self.rvq = rvq
+        self.rvq_mask = rvq_mask
+        self.sp_idx = sp_idx
+        self.sp_val = sp_val
+        self.num_heads = num_heads
+
+    @property
+    def num_tokens(self) -> int:
+        return int(self.pq_codes.shape[0])
+
+    @property
+    def rvq_offsets(self) -> torch.Tensor:
+        return torch.nonzero(self.rvq_mask.reshape(-1), as_tuple=False).reshape(-1).to(torch.int32)
+
+    @property
+    def rvq_codes(self) -> torch.Tensor:
+        L = self.rvq.shape[-1]
+        flat = self.rvq.reshape(-1, L)
+        return flat[self.rvq_mask.reshape(-1)].to(torch.int32) & 0xFFFF
+
+    @classmethod
+    def empty(cls, config: RFSNConfig, num_heads: Optional[int] = None) -> "CompressedTensorMLX":
+        heads = config.num_heads if num_heads is None else num_heads
+        dev = torch.device(config.device)
+        code_dtype = torch.uint8 if config.rvq_codebook_size <= 256 else torch.int16
+        return cls(torch.zeros((0, heads, config.num_subspaces), dtype=torch.uint8, device=dev),
+                   torch.zeros((0, heads, config.num_rvq_layers), dtype=code_dtype, device=dev),
+                   torch.zeros((0, heads), dtype=torch.bool, device=dev),
+                   torch.zeros((0, heads, config.sparse_topk), dtype=torch.uint8, device=dev),
+                   torch.zeros((0, heads, config.sparse_topk), dtype=torch.float16, device=dev), heads)
+
+    def to_store(self, qz: K.QuantizerBuffers) -> K.CodeStoreBuffers:
+        """Copy into a one-slot code store with rows = heads (for the kernels)."""
+        T, H = self.num_tokens, self.num_heads
+        st = K.CodeStoreBuffers(qz, rows=H, cap=max(T, 16), device=self.pq_codes.device)
+        if T:
+            st.pq[0, :, :T] = self.pq_codes.transpose(0, 1)
+            if st.rvq is not None:
+                st.rvq[0, :, :T] = self.rvq.transpose(0, 1).to(st.rvq.dtype)
+                st.mask[0, :, :T] = self.rvq_mask.transpose(0, 1).to(torch.uint8)
+            if st.sp_idx is not None:
+                st.sp_idx[0, :, :T] = self.sp_idx.transpose(0, 1)
+                st.sp_val[0, :, :T] = self.sp_val.transpose(0, 1)
+        return st
+
+
+def _concat0(lhs: torch.Tensor, rhs: torch.Tensor) -> torch.Tensor:
+    """storage.py:101-106."""
+    if lhs.shape[0] == 0:
+        return rhs
+    if rhs.shape[0] == 0:
+        return lhs
+    return torch.cat([lhs, rhs], dim=0)
+
+
+def _numpy_ints(values) -> np.ndarray:
+    """storage.py:109-110."""
+    if isinstance(values, torch.Tensor):
+        values = values.detach().cpu().numpy()
+    return np.asarray(values, dtype=np.int64)
+
+
+def chunk_file_path(root: Path, layer_idx: int, chunk_id: int) -> Path:
+    """storage.py:113-114 — name of a cold chunk (also its key in the pinned tier)."""
+    return Path(root) / f"layer{layer_idx}_chunk{chunk_id}.npz"
+
+
+# ---------------------------------------------------------------------------
+# Pinned-host cold tier
+# ---------------------------------------------------------------------------
+
+@dataclass
+class ColdChunk:
+    chunk_id: int
+    start_token: int
+    end_token: int
+    k: K.CodeStoreBuffers  # pinned host, one slot, rows x cap
+    v: K.CodeStoreBuffers
+    ready: Optional[torch.cuda.Event] = None  # D2H writes into k/v done
+    version: int = 0
+
+    @property
+    def num_tokens(self) -> int:
+        return self.end_token - self.start_token
+
+
+class ColdTier:
+    """Cold chunks in pinned host memory plus a device-resident LRU chunk pool.
+
+    ``chunks`` maps chunk id -> ColdChunk (codes for every row of the cache).
+    ``pool_k/pool_v`` are device code stores with ``slots`` chunk slots; a
+    chunk is resident when ``slot_of[chunk_id]`` exists.  Copies in either
+    direction go through the C ABI (rfsn_cold_prefetch / rfsn_cold_evict).
+    """
+
+    def __init__(self, qz: K.QuantizerBuffers, rows: int, chunk_tokens: int, slots: int, device):
+        self.qz = qz
+        self.rows = rows
+        self.chunk_tokens = chunk_tokens
+        self.device = torch.device(device)
+        self.chunks: "OrderedDict[int, ColdChunk]" = OrderedDict()
+        self.slots = max(1, slots)
+        self.pool_k = K.CodeStoreBuffers(qz, rows, chunk_tokens, self.slots, device=self.device)
+        self.pool_v = K.CodeStoreBuffers(qz, rows, chunk_tokens, self.slots, device=self.device)
+        self.slot_of: "OrderedDict[int, int]" = OrderedDict()  # chunk id -> slot (LRU order)
+        self.slot_version: Dict[int, int] = {}
+        self.slot_ready: Dict[int, torch.cuda.Event] = {}
+        self.pinned_by_router: set = set()
+        self.lock = threading.Lock()
+        self.h2d_bytes = 0
+
+    # -- host side -------------------------------------------------------
+    def new_chunk(self, chunk_id: int, start: int) -> ColdChunk:
+        c = ColdChunk(chunk_id, start, start,
+                      K.CodeStoreBuffers(self.qz, self.rows, self.chunk_tokens, 1, pin_memory=True),
+                      K.CodeStoreBuffers(self.qz, self.rows, self.chunk_tokens, 1, pin_memory=True))
+        self.chunks[chunk_id] = c
+        return c
+
+    def write_from_device(self, chunk: ColdChunk, offset: int, src_k: K.CodeStoreBuffers,
+                          src_v: K.CodeStoreBuffers, src_slot: int, src_first: int, count: int,
+                          stream: torch.cuda.Stream) -> None:
+        """D2H copy of tokens [src_first, +count) of every row into chunk tokens [offset, +count)."""
+        with torch.cuda.stream(stream):
+            for dst, src in ((chunk.k, src_k), (chunk.v, src_v)):
+                for d, s in zip(dst.fields(), src.fields()):
+                    if d is None:
+                        continue
+                    d[0, :, offset:offset + count].copy_(s[src_slot, : self.rows, src_first:src_first + count],
+                                                         non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(stream)
+        chunk.ready = ev
+        chunk.version += 1
+        self.invalidate(chunk.chunk_id)
+
+    def invalidate(self, chunk_id: int) -> None:
+        slot = self.slot_of.pop(chunk_id, None)
+        if slot is not None:
+            self.slot_version.pop(slot, None)
+            self.slot_ready.pop(slot, None)
+        self.pinned_by_router.discard(chunk_id)
+
+    # -- device pool ------------------------------------------------------
+    def _grow(self, need: int) -> None:
+        new_slots = max(need, self.slots * 2)
+        for name in ("pool_k", "pool_v"):
+            old = getattr(self, name)
+            new = K.CodeStoreBuffers(self.qz, self.rows, self.chunk_tokens, new_slots, device=self.device)
+            for d, s in zip(new.fields(), old.fields()):
+                if d is not None:
+                    d[: self.slots].copy_(s)
+            setattr(self, name, new)
+        self.slots = new_slots
+
+    def _free_slot(self, keep: set) -> int:
+        used = set(self.slot_of.values())
+        for s in range(self.slots):
+            if s not in used:
+                return s
+        for cid, s in self.slot_of.items():  # LRU order
+            if cid not in keep and cid not in self.pinned_by_router:
+                self.invalidate(cid)
+                return s
+        for cid, s in self.slot_of.items():
+            if cid not in keep:
+                self.invalidate(cid)
+                return s
+        self._grow(self.slots + 1)
+        return self._free_slot(keep)
+
+    def resident(self, chunk_id: int) -> bool:
+        c = self.chunks.get(chunk_id)
+        s = self.slot_of.get(chunk_id)
+        return c is not None and s is not None and self.slot_version.get(s) == c.version
+
+    def ensure_resident(self, chunk_id: int, stream: torch.cuda.Stream, keep: set = frozenset()) -> int:
+        """Make chunk resident (H2D on `stream` if needed); return its slot."""
+        with self.lock:
+            if self.resident(chunk_id):
+                self.slot_of.move_to_end(chunk_id)
+                return self.slot_of[chunk_id]
+            chunk = self.chunks[chunk_id]
+            slot = self._free_slot(set(keep) | {chunk_id})
+            if chunk.ready is not None:
+                stream.wait_event(chunk.ready)
+            sptr = stream.cuda_stream
+            for dst, src in ((self.pool_k, chunk.k), (self.pool_v, chunk.v)):
+                for d, s in zip(dst.fields(), src.fields()):
+                    if d is None:
+                        continue
+                    nbytes = s[0].numel() * s.element_size()
+                    K.call("rfsn_cold_prefetch", d[slot].data_ptr(), s[0].data_ptr(), nbytes, sptr, None)
+                    self.h2d_bytes += nbytes
+            ev = torch.cuda.Event()
+            ev.record(stream)
+            self.slot_of[chunk_id] = slot
+            self.slot_version[slot] = chunk.version
+            self.slot_ready[slot] = ev
+            return slot
+
+    def wait_ready(self, slot: int, stream: torch.cuda.Stream) -> None:
+        ev = self.slot_ready.get(slot)
+        if ev is not None:
+            stream.wait_event(ev)
+
+
+_COLD_REGISTRY: Dict[Tuple[str, int], ColdTier] = {}
+
+
+def register_cold_tier(root: Path, layer_idx: int, tier: ColdTier) -> None:
+    _COLD_REGISTRY[(str(Path(root).resolve()), int(layer_idx))] = tier
+
+
+def lookup_cold_tier(root: Path, layer_idx: int) -> Optional[ColdTier]:
+    return _COLD_REGISTRY.get((str(Path(root).resolve()), int(layer_idx)))
+
+
+def unregister_cold_tier(root: Path, layer_idx: int) -> None:
+    _COLD_REGISTRY.pop((str(Path(root).resolve()), int(layer_idx)), None)
+
+
+class AsyncHierarchicalRouterMLX:
+    """Cold-chunk prefetcher (storage.py:154-237) for the pinned-host tier.
+
+    Candidate selection is the reference's (storage.py:166-182): chunk ids in
+    [(p - w) // cs, (p + w) // cs] that exist, nearest first by |id*cs - p|,
+    the first ``top_k`` loaded.  "Loading" copies the chunk's codes into the
+    device pool with cudaMemcpyAsync on the router's own CUDA stream (the
+    reference reads an NPZ file in an executor thread); the cache's attention
+    waits on the copy's event before reading the slot.  The router keeps at
+    most 16 chunks (FIFO, storage.py:186-188), which the pool does not evict.
+    """
+
+    def __init__(self, config: RFSNConfig, layer_idx: int = 0):
+        self.config = config
+        self.layer_idx = layer_idx
+        self.disk_dir = Path(config.disk_cache_dir)
+        self.throttle = config.prefetch_throttle_s
+        self._cache: "OrderedDict[int, Dict[str, object]]" = OrderedDict()
+        self._max_cache_size = 16
+        self._pending_prefetch: set = set()
+        self._stream: Optional[torch.cuda.Stream] = None
+
+    def _tier(self) -> Optional[ColdTier]:
+        return lookup_cold_tier(self.disk_dir, self.layer_idx)
+
+    @property
+    def stream(self) -> torch.cuda.Stream:
+        if self._stream is None:
+            self._stream = torch.cuda.Stream(device=torch.device(self.config.device))
+        return self._stream
+
+    def candidates(self, current_position: int, context_window: int, top_k: int) -> List[int]:
+        tier = self._tier()
+        if tier is None:
+            return []
+        cs = max(self.config.chunk_tokens, 1)
+        start_chunk = max(0, (current_position - context_window) // cs)
+        end_chunk = max(start_chunk, (current_position + context_window) // cs)
+        cands = [c for c in range(start_chunk, end_chunk + 1) if c in tier.chunks]
+        cands.sort(key=lambda cid: abs(cid * cs - current_position))
+        return cands[:top_k]
+
+    async def predict_and_prefetch(self, current_position: int, context_window: int, top_k: int = 2) -> List[int]:
+        loaded: List[int] = []
+        for chunk_id in self.candidates(current_position, context_window, top_k):
+            entry = self._cache.get(chunk_id)
+            tier = self._tier()
+            if entry is not None and tier is not None and tier.resident(chunk_id):
+                loaded.append(chunk_id)
+                continue
+            if chunk_id in self._pending_prefetch:
+                continue
+            self._pending_prefetch.add(chunk_id)
+            await self._load_chunk(chunk_id)
+            self._pending_prefetch.discard(chunk_id)
+            loaded.append(chunk_id)
+            if self.throttle > 0:
+                await asyncio.sleep(self.throttle)
+        while len(self._cache) > self._max_cache_size:
+            old, _ = self._cache.popitem(last=False)
+            tier = self._tier()
+            if tier is not None:
+                tier.pinned_by_router.discard(old)
+        return loaded
+
+    def prefetch_sync(self, current_position: int, context_window: int, top_k: int = 2) -> List[int]:
+        try:
+            return asyncio.run(self.predict_and_prefetch(current_position, context_window, top_k))
+        except RuntimeError:
+            loop = asyncio.new_event_loop()
+            try:
+                return loop.run_until_complete(self.predict_and_prefetch(current_position, context_window, top_k))
+            finally:
+                loop.close()
+
+    async def _load_chunk(self, chunk_id: int) -> None:
+        self._cache[chunk_id] = self._load_chunk_sync(chunk_id)
+
+    def _load_chunk_sync(self, chunk_id: int) -> Dict[str, object]:
+        tier = self._tier()
+        if tier is None or chunk_id not in tier.chunks:
+            return {}
+        slot = tier.ensure_resident(chunk_id, self.stream)
+        tier.pinned_by_router.add(chunk_id)
+        c = tier.chunks[chunk_id]
+        return {"chunk_id": chunk_id, "slot": slot, "num_tokens": c.num_tokens, "start_token": c.start_token}
+
+    def get_chunk(self, chunk_id: int) -> Optional[Dict[str, object]]:
+        entry = self._cache.get(chunk_id)
+        if entry is None:
+            return None
+        tier = self._tier()
+        if tier is None or not tier.resident(chunk_id):
+            return None
+        return entry
