@@ -40,8 +40,7 @@ class Quantizer(C.Structure):
 
 
 class CodeStore(C.Structure):
-    _fields_ = [("pq", C.c_void_p), ("rvq", C.c_void_p), ("mask", C.c_void_p), ("sp_idx", C.c_void_p),
-                ("sp_val", C.c_void_p), ("cap", C.c_int64), ("rows", C.c_int64), ("slots", C.c_int64)]
+    _fields_ = [("data", C.c_void_p), ("cap", C.c_int64), ("rows", C.c_int64), ("slots", C.c_int64)]
 
 
 class DenseStore(C.Structure):
@@ -56,8 +55,8 @@ class Segment(C.Structure):
 class AttnArgs(C.Structure):
     _fields_ = [("q", C.c_void_p), ("qpos", C.c_void_p), ("out", C.c_void_p), ("batch", C.c_int32),
                 ("queries", C.c_int32), ("q_heads", C.c_int32), ("kv_heads", C.c_int32), ("head_dim", C.c_int32),
-                ("causal", C.c_int32), ("scale", C.c_float), ("hot", DenseStore), ("warm_k", CodeStore),
-                ("warm_v", CodeStore), ("cold_k", CodeStore), ("cold_v", CodeStore),
+                ("causal", C.c_int32), ("scale", C.c_float), ("hot", DenseStore), ("warm", CodeStore),
+                ("cold", CodeStore),
                 ("segments", C.POINTER(Segment)), ("num_segments", C.c_int32), ("num_ctas", C.c_int32),
                 ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t), ("device_status", C.c_void_p)]
 
@@ -67,12 +66,13 @@ SIGNATURES = {
     "rfsn_version": (C.c_int, []),
     "rfsn_status_string": (C.c_char_p, [C.c_int]),
     "rfsn_last_cuda_error": (C.c_char_p, []),
+    "rfsn_code_block_bytes": (C.c_int64, [C.POINTER(Quantizer)]),
     "rfsn_encode": (C.c_int, [C.POINTER(Quantizer), C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_int64,
-                              C.c_int64, C.c_int64, C.POINTER(CodeStore), C.c_int64, C.c_int64, C.c_void_p,
-                              C.c_void_p]),
-    "rfsn_decode_codes": (C.c_int, [C.POINTER(Quantizer), C.POINTER(CodeStore), C.c_int64, C.c_int64, C.c_int64,
-                                    C.c_int64, C.c_int64, C.c_void_p, C.c_int64, C.c_int64, C.c_int64,
-                                    C.c_void_p]),
+                              C.c_int64, C.c_int64, C.POINTER(CodeStore), C.c_int32, C.c_int64, C.c_int64,
+                              C.c_void_p, C.c_void_p]),
+    "rfsn_decode_codes": (C.c_int, [C.POINTER(Quantizer), C.POINTER(CodeStore), C.c_int32, C.c_int64, C.c_int64,
+                                    C.c_int64, C.c_int64, C.c_int64, C.c_void_p, C.c_int64, C.c_int64,
+                                    C.c_int64, C.c_void_p]),
     "rfsn_attention_workspace_size": (C.c_int, [C.POINTER(AttnArgs), C.POINTER(Quantizer),
                                                 C.POINTER(C.c_size_t)]),
     "rfsn_decode_attention": (C.c_int, [C.POINTER(AttnArgs), C.POINTER(Quantizer), C.c_void_p]),

@@ -3,6 +3,7 @@
 #include <string.h>
 
 #include "rfsn_api_internal.h"
+#include "rfsn_layout.h"
 
 namespace {
 thread_local char g_last_cuda_error[256] = "";
@@ -38,18 +39,15 @@ int validate_quantizer(const rfsn_quantizer* qz) {
 }
 
 int validate_store(const rfsn_code_store* s, const rfsn_quantizer* qz) {
-  if (!s || !s->pq || s->cap <= 0 || s->rows <= 0 || s->slots <= 0) return RFSN_ERR_INVALID_ARGUMENT;
-  if (s->cap % 16 != 0) return RFSN_ERR_ALIGNMENT;
-  if (!aligned16(s->pq)) return RFSN_ERR_ALIGNMENT;
-  if (qz->rvq_layers > 0) {
-    if (!s->rvq || !s->mask) return RFSN_ERR_INVALID_ARGUMENT;
-    if (!aligned16(s->rvq) || !aligned16(s->mask)) return RFSN_ERR_ALIGNMENT;
-  }
-  if (qz->sparse_topk > 0) {
-    if (!s->sp_idx || !s->sp_val) return RFSN_ERR_INVALID_ARGUMENT;
-    if (!aligned16(s->sp_idx) || !aligned16(s->sp_val)) return RFSN_ERR_ALIGNMENT;
-  }
+  (void)qz;
+  if (!s || !s->data || s->cap <= 0 || s->rows <= 0 || s->slots <= 0) return RFSN_ERR_INVALID_ARGUMENT;
+  if (s->cap % kBlockTokens != 0) return RFSN_ERR_ALIGNMENT;
+  if (!aligned16(s->data)) return RFSN_ERR_ALIGNMENT;
   return RFSN_OK;
+}
+
+BlockLayout layout_of(const rfsn_quantizer* qz) {
+  return make_block_layout(qz->num_subspaces, qz->rvq_layers, qz->rvq_codebook_size > 256, qz->sparse_topk);
 }
 
 }  // namespace rfsn
@@ -70,6 +68,11 @@ extern "C" const char* rfsn_status_string(int status) {
 }
 
 extern "C" const char* rfsn_last_cuda_error(void) { return g_last_cuda_error; }
+
+extern "C" int64_t rfsn_code_block_bytes(const rfsn_quantizer* qz) {
+  if (rfsn::validate_quantizer(qz) != RFSN_OK) return -1;
+  return rfsn::layout_of(qz).block_bytes;
+}
 
 extern "C" int rfsn_cold_prefetch(void* dst_device, const void* src_pinned_host, size_t bytes, void* stream,
                                   void* event) {

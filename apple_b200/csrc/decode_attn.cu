@@ -31,14 +31,15 @@
 #include <math.h>
 
 #include "rfsn_api_internal.h"
+#include "rfsn_attn_chunk.cuh"
+#include "rfsn_attn_util.cuh"
 #include "rfsn_decode.cuh"
 
 namespace rfsn {
 
-constexpr int kStages = 3;
-constexpr int kStageBytes = 32 * 1024;
-constexpr int kNumFields = 10;  // k/v x {pq, rvq, mask, sp_idx, sp_val}
-constexpr int kChunk = 8;       // tokens per warp chunk (2 row-steps of 4 tokens)
+constexpr int kMaxStages = 8;                // mbarrier slots reserved per CTA
+constexpr int kMaxStageBytes = 48 * 1024;    // upper bound of one ring stage
+constexpr int kChunk = 16;      // tokens per warp chunk (4 row-steps of 4 tokens)
 constexpr int64_t kMaxSmem = 227 * 1024;  // opt-in shared memory per CTA on sm_100
 
 struct SegDev {
@@ -46,7 +47,7 @@ struct SegDev {
 };
 
 struct StoreDev {
-  const uint8_t* f[5];  // pq, rvq, mask, sp_idx, sp_val
+  const uint8_t* data;  // packed 16-token blocks (rfsn_layout.h)
   int64_t cap, rows;
 };
 
@@ -61,24 +62,24 @@ struct AttnParams {
   const uint16_t* hot_k;
   const uint16_t* hot_v;
   int64_t hot_cap;
-  StoreDev sk[3], sv[3];  // index 1 = warm, 2 = cold pool
+  StoreDev st[3];  // index 1 = warm, 2 = cold pool
+  BlockLayout lay;
   const uint16_t* pq_cb;
   const uint16_t* rvq_cb;
-  int M, K, ds, L, Kr, S, rvq_u16, has_mask;
+  int M, K, ds, L, Kr, S, rvq_u16, has_mask, rvq_smem;
   int64_t rows, W, per_cta;
   int max_pieces;
-  int tile_codes, tile_dense;
-  int field_bpt[kNumFields];   // bytes per token of each field (0 = absent)
-  int field_base[kNumFields];  // byte offset of each field's region in a stage
+  int tile_blocks, tile_dense;  // code-tile length in 16-token blocks; dense-tile length in tokens
   int nseg;
   int smem_pq, smem_rvq, smem_qtab, smem_vsp, smem_ml, smem_desc, smem_bar, smem_flag;
+  int stages, stage_bytes, ring_off;  // ring depth, bytes per stage, ring offset in smem
   SegDev seg[RFSN_MAX_SEGMENTS];
 };
 
 struct TileDesc {
   int kind;  // 0 = dense, 1 = compressed, -1 = done
-  int n, pos0, row, first_of_piece, last_of_piece, piece, pad;
-  int off[kNumFields];  // byte offset of each field's first token inside the stage
+  int n, pos0, row, first_of_piece, last_of_piece, piece;
+  int t0;    // compressed tiles: index of the first token inside the first copied block
 };
 
 __device__ __forceinline__ void set_status(const AttnParams& p, volatile int* abort, int code) {
@@ -97,14 +98,13 @@ __device__ __forceinline__ bool consumer_sync(uint64_t* bar, uint32_t& phase, vo
   return ok;
 }
 
-template <int D, int RMAX, int NW, bool RVQ_SMEM>
+template <int D, int RMAX, int NW, int DS>
 __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr int DPL = D / 8;  // dims per lane
-  constexpr int NG = DPL / 8;  // 8-dim groups per lane
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + p.smem_bar);
-  uint64_t* empty_bar = full_bar + kStages;
-  uint64_t* sync_bar = empty_bar + kStages;
+  uint64_t* empty_bar = full_bar + kMaxStages;
+  uint64_t* sync_bar = empty_bar + kMaxStages;
   TileDesc* descs = reinterpret_cast<TileDesc*>(smem + p.smem_desc);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + p.smem_flag);
   uint16_t* s_pq = reinterpret_cast<uint16_t*>(smem + p.smem_pq);
@@ -114,7 +114,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < p.stages; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], NW);
     }
@@ -123,10 +123,30 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
     fence_mbar_init();
   }
   {  // stage codebooks
-    const int n16 = p.M * p.K * p.ds / 8;
-    for (int i = threadIdx.x; i < n16; i += blockDim.x)
-      reinterpret_cast<uint4*>(s_pq)[i] = __ldg(reinterpret_cast<const uint4*>(p.pq_cb) + i);
-    if (RVQ_SMEM && p.L > 0) {
+    // PQ codebook [M][K][ds] staged code-major [K][M][ds]: one code's centroids
+    // for all subspaces form one row, so a token's lanes read distinct banks
+    const int nc = p.M * p.K;
+    if (p.ds % 8 == 0) {
+      const int per = p.ds / 8;
+      for (int i = threadIdx.x; i < nc * per; i += blockDim.x) {
+        const int cen = i / per, part = i - cen * per;
+        const int m = cen / p.K, c = cen - m * p.K;
+        reinterpret_cast<uint4*>(s_pq)[(c * p.M + m) * per + part] =
+            __ldg(reinterpret_cast<const uint4*>(p.pq_cb) + i);
+      }
+    } else if (p.ds == 4) {
+      for (int i = threadIdx.x; i < nc; i += blockDim.x) {
+        const int m = i / p.K, c = i - m * p.K;
+        reinterpret_cast<uint2*>(s_pq)[c * p.M + m] = __ldg(reinterpret_cast<const uint2*>(p.pq_cb) + i);
+      }
+    } else {
+      for (int i = threadIdx.x; i < nc * p.ds; i += blockDim.x) {
+        const int cen = i / p.ds, k = i - cen * p.ds;
+        const int m = cen / p.K, c = cen - m * p.K;
+        s_pq[(c * p.M + m) * p.ds + k] = p.pq_cb[i];
+      }
+    }
+    if (p.rvq_smem && p.L > 0) {
       const int r16 = p.L * p.Kr * D / 8;
       for (int i = threadIdx.x; i < r16; i += blockDim.x)
         reinterpret_cast<uint4*>(s_rvq)[i] = __ldg(reinterpret_cast<const uint4*>(p.rvq_cb) + i);
@@ -139,26 +159,16 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
   const int64_t cta_e = min(cta_a + p.per_cta, total);
 
   // ======================= producer warp =======================
+  // All 32 lanes walk the same tile sequence.  Lane 0 waits for a free stage,
+  // writes the tile descriptor and arms the stage's mbarrier with the byte
+  // count; then lane f issues the bulk copy of field f, so a tile's copies
+  // enter the TMA unit in parallel instead of one after another.
   if (warp == NW) {
-    if (lane != 0) return;
     int stage = 0;
     uint32_t phase = 0;
-    bool inflight[kStages] = {};
-    uint32_t inflight_parity[kStages] = {};
+    bool inflight[kMaxStages] = {};
+    uint32_t inflight_parity[kMaxStages] = {};
     bool ok = true;
-    auto acquire = [&](int s) -> bool {
-      if (!mbar_wait_bounded(&empty_bar[s], phase ^ 1u, abort)) {
-        set_status(p, abort, kDevStatusTimeoutEmpty);
-        return false;
-      }
-      return true;
-    };
-    auto advance = [&]() {
-      if (++stage == kStages) {
-        stage = 0;
-        phase ^= 1u;
-      }
-    };
     for (int64_t a = cta_a; a < cta_e && ok;) {
       const int64_t row = a / p.W;
       const int64_t w0 = a - row * p.W;
@@ -170,73 +180,86 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
         const int64_t s0 = max(w0, (int64_t)sg.wstart);
         const int64_t s1 = min(w1, (int64_t)sg.wstart + sg.count);
         if (s0 >= s1) continue;
-        const int tile = sg.store == 0 ? p.tile_dense : p.tile_codes;
-        for (int64_t t = s0; t < s1; t += tile) {
-          const int n = (int)min((int64_t)tile, s1 - t);
-          if (!acquire(stage)) {
+        for (int64_t t = s0; t < s1;) {
+          const int64_t tok = sg.first + (t - sg.wstart);
+          int n;
+          if (sg.store == 0) {
+            n = (int)min((int64_t)p.tile_dense, s1 - t);
+          } else {  // whole 16-token blocks: the first may start mid-block
+            n = (int)min((int64_t)p.tile_blocks * kBlockTokens - (tok % kBlockTokens), s1 - t);
+          }
+          int got = 1;
+          if (lane == 0 && !mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, abort)) {
+            set_status(p, abort, kDevStatusTimeoutEmpty);
+            got = 0;
+          }
+          if (!__shfl_sync(0xffffffffu, got, 0)) {
             ok = false;
             break;
           }
-          inflight[stage] = false;
-          TileDesc* d = &descs[stage];
-          unsigned char* sb = smem + (size_t)stage * kStageBytes;
-          const int64_t tok = sg.first + (t - sg.wstart);
-          for (int f = 0; f < kNumFields; ++f) d->off[f] = 0;
-          d->n = n;
-          d->pos0 = sg.pos0 + (int)(t - sg.wstart);
-          d->row = (int)row;
-          d->first_of_piece = first;
-          d->last_of_piece = (t + n >= w1);
-          d->piece = piece;
-          first = false;
+          unsigned char* sb = smem + p.ring_off + (size_t)stage * p.stage_bytes;
+          const void* my_src = nullptr;
+          void* my_dst = nullptr;
+          uint32_t my_len = 0;
           uint32_t tx = 0;
+          int t0 = 0;
           if (sg.store == 0) {
-            d->kind = 0;
             const uint32_t bytes = (uint32_t)n * D * 2;
             const size_t src = ((size_t)row * p.hot_cap + tok) * D;
-            d->off[0] = 0;
-            d->off[1] = p.tile_dense * D * 2;
             tx = 2 * bytes;
-            mbar_arrive_expect_tx(&full_bar[stage], tx);
-            bulk_g2s(sb, p.hot_k + src, bytes, &full_bar[stage]);
-            bulk_g2s(sb + d->off[1], p.hot_v + src, bytes, &full_bar[stage]);
-          } else {
-            d->kind = 1;
-            const StoreDev& SK = p.sk[sg.store];
-            const StoreDev& SV = p.sv[sg.store];
-            const int64_t tindex = ((int64_t)sg.slot * SK.rows + row) * SK.cap + tok;
-            uintptr_t lo[kNumFields];
-            uint32_t len[kNumFields];
-            for (int f = 0; f < kNumFields; ++f) {
-              len[f] = 0;
-              if (!p.field_bpt[f]) continue;
-              const uint8_t* base = (f < 5 ? SK.f[f] : SV.f[f - 5]);
-              const uintptr_t src = reinterpret_cast<uintptr_t>(base) + (uintptr_t)(tindex * p.field_bpt[f]);
-              const uintptr_t l0 = src & ~(uintptr_t)15;
-              const uintptr_t hi = (src + (uintptr_t)n * p.field_bpt[f] + 15) & ~(uintptr_t)15;
-              lo[f] = l0;
-              len[f] = (uint32_t)(hi - l0);
-              d->off[f] = p.field_base[f] + (int)(src - l0);
-              tx += len[f];
+            if (lane < 2) {
+              my_src = (lane == 0 ? p.hot_k : p.hot_v) + src;
+              my_dst = sb + (lane == 0 ? 0 : p.tile_dense * D * 2);
+              my_len = bytes;
             }
-            mbar_arrive_expect_tx(&full_bar[stage], tx);
-            for (int f = 0; f < kNumFields; ++f)
-              if (len[f]) bulk_g2s(sb + p.field_base[f], reinterpret_cast<const void*>(lo[f]), len[f], &full_bar[stage]);
+          } else {
+            const StoreDev& SD = p.st[sg.store];
+            const int64_t b0 = tok / kBlockTokens;
+            const int64_t b1 = (tok + n + kBlockTokens - 1) / kBlockTokens;
+            const int64_t blk = ((int64_t)sg.slot * SD.rows + row) * (SD.cap / kBlockTokens) + b0;
+            t0 = (int)(tok - b0 * kBlockTokens);
+            tx = (uint32_t)((b1 - b0) * p.lay.block_bytes);
+            if (lane == 0) {
+              my_src = SD.data + blk * p.lay.block_bytes;
+              my_dst = sb;
+              my_len = tx;
+            }
           }
+          if (lane == 0) {
+            TileDesc* d = &descs[stage];
+            d->kind = sg.store == 0 ? 0 : 1;
+            d->n = n;
+            d->pos0 = sg.pos0 + (int)(t - sg.wstart);
+            d->row = (int)row;
+            d->first_of_piece = first;
+            d->last_of_piece = (t + n >= w1);
+            d->piece = piece;
+            d->t0 = t0;
+            mbar_arrive_expect_tx(&full_bar[stage], tx);
+          }
+          t += n;
+          first = false;
+          __syncwarp();  // the barrier is armed before any copy can complete
+          if (my_len) bulk_g2s(my_dst, my_src, my_len, &full_bar[stage]);
           inflight[stage] = true;
           inflight_parity[stage] = phase;
-          advance();
+          if (++stage == p.stages) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
       }
       a += (w1 - w0);
     }
-    if (ok && acquire(stage)) {
+    if (lane != 0) return;
+    if (ok && mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, abort)) {
       descs[stage].kind = -1;
       mbar_arrive(&full_bar[stage]);
     } else {
-      // Abort path: wait (bounded) for copies this thread issued so the CTA
-      // never retires with bulk copies still writing its shared memory.
-      for (int k = 0; k < kStages; ++k) {
+      if (ok) set_status(p, abort, kDevStatusTimeoutEmpty);
+      // Abort path: wait (bounded) for the copies issued into each stage so the
+      // CTA never retires with bulk copies still writing its shared memory.
+      for (int k = 0; k < p.stages; ++k) {
         if (!inflight[k]) continue;
         const uint64_t t0 = global_timer_ns();
         while (!mbar_try_wait(&full_bar[k], inflight_parity[k])) {
@@ -248,66 +271,106 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
   }
 
   // ======================= consumer warps =======================
-  const int slot = lane >> 3;  // token slot within a row-step (0..3)
-  const int j = lane & 7;      // dim group owner
+  // Lane (slot, j): slot = lane/8 is the token of a 4-token row-step, j = lane%8
+  // owns dims [j*DPL, (j+1)*DPL).  K scores come from mma.m16n8k16 with the
+  // lanes' reconstructed half2 registers as the B fragment (column = lane/4 =
+  // (slot, dim half h = j/4), k = dims); A holds the query rows twice: rows
+  // 0..7 matched to the h=0 dims, rows 8..15 to the h=1 dims.  Score(slot, r)
+  // is then c0 + c3 of lane 4r + slot.  V is accumulated on CUDA cores.
+  const int slot = lane >> 3;
+  const int j = lane & 7;
   const int dim0 = j * DPL;
+  const int srow = lane >> 2;   // score lane: query row r
+  const int sslot = lane & 3;   // score lane: token slot
   float* qtab = reinterpret_cast<float*>(smem + p.smem_qtab) + (size_t)warp * D * RMAX;  // [D][RMAX]
-  float* vsp = reinterpret_cast<float*>(smem + p.smem_vsp) + (size_t)warp * RMAX * D;    // [RMAX][D]
+  // sparse-V sums, one copy per token slot (a token's sparse dims are distinct, so
+  // plain read-modify-write is race-free): [4][D][RMAX]; reused as [RMAX][D] to combine
+  float* vsp = reinterpret_cast<float*>(smem + p.smem_vsp) + (size_t)warp * 4 * RMAX * D;
   float* s_ml = reinterpret_cast<float*>(smem + p.smem_ml);                              // [NW][RMAX][2]
-
-  QzView qv;
-  qv.pq_cb = s_pq;
-  qv.rvq_cb = RVQ_SMEM ? s_rvq : p.rvq_cb;
-  qv.M = p.M; qv.K = p.K; qv.ds = p.ds; qv.L = p.L; qv.Kr = p.Kr; qv.D = D; qv.S = p.S; qv.rvq_u16 = p.rvq_u16;
-  const int rvq_bpt = p.L * (p.rvq_u16 ? 2 : 1);
+  const int M = p.M, Kc = p.K, L = p.L, S = p.S;
+  const int rvq_bpt = L * (p.rvq_u16 ? 2 : 1);
   const float NEG_INF = __int_as_float(0xff800000);
+  const float sl2 = p.scale * 1.4426950408889634f;  // scores kept in log2 units
+  constexpr int NMMA = DPL / 4;  // K mma k-steps per row-step
+  constexpr int NSP = (RMAX + 3) / 4;
 
-  float qreg[RMAX][DPL];
+  ChunkShared cs;
+  cs.pq_cm = s_pq;
+  cs.rvq_s = s_rvq;
+  cs.rvq_g = p.rvq_cb;
+  cs.qtab = qtab;
+  cs.vsp = vsp;
+  cs.M = M; cs.K = Kc; cs.ds = p.ds; cs.L = L; cs.Kr = p.Kr; cs.S = S; cs.rvq_u16 = p.rvq_u16;
+  cs.rvq_smem = p.rvq_smem; cs.has_mask = p.has_mask; cs.rvq_bpt = rvq_bpt;
+  cs.lay = p.lay;
+  cs.R = p.R; cs.causal = p.causal; cs.sl2 = sl2;
+  cs.n = 0; cs.pos0 = 0; cs.qp_lane = 0;
+  const int mode_codes = (L == 1 && p.rvq_smem && !p.rvq_u16 && S <= 8) ? kRvq1
+                         : (L == 0 && S <= 8) ? kPqOnly : kGeneric;
+  uint32_t aq[NMMA][4];      // query A fragments
+  uint32_t asp[NSP][4];      // constant 0/1 A fragments summing sparse corrections over 8 lanes
   float acc[RMAX][DPL];
-  float m_run[RMAX], l_run[RMAX];
-  int qp[RMAX];
+  float m_run = NEG_INF, l_run = 0.f;  // online state of row srow (replicated over its 4 lanes)
+  int qp_lane = 0x7fffffff;            // causal position of row srow
   int stage = 0;
   uint32_t phase = 0, sync_phase = 0;
+  int chunk_base = 0;  // global index of the current tile's first chunk
+
+#pragma unroll
+  for (int t = 0; t < NSP; ++t) {
+    const int gA = lane >> 2;
+    asp[t][0] = asp[t][1] = pack_h2(gA == 4 * t ? 1.f : 0.f, gA == 4 * t + 1 ? 1.f : 0.f);
+    asp[t][2] = asp[t][3] = pack_h2(gA == 4 * t + 2 ? 1.f : 0.f, gA == 4 * t + 3 ? 1.f : 0.f);
+  }
 
   for (;;) {
     if (!mbar_wait_bounded(&full_bar[stage], phase, abort)) {
       set_status(p, abort, kDevStatusTimeoutFull);
       break;
     }
-    const TileDesc desc = descs[stage];
-    if (desc.kind < 0) break;
-    const unsigned char* sb = smem + (size_t)stage * kStageBytes;
-    const int row = desc.row;
+    const TileDesc* dsc = &descs[stage];
+    const int kind = dsc->kind;
+    if (kind < 0) break;
+    const int n = dsc->n;
+    const int pos0 = dsc->pos0;
+    const int row = dsc->row;
+    const int first_of_piece = dsc->first_of_piece;
+    const int last_of_piece = dsc->last_of_piece;
+    const int piece = dsc->piece;
+    const unsigned char* sb = smem + p.ring_off + (size_t)stage * p.stage_bytes;
+    const int t0 = dsc->t0;
+    const uint16_t* hot_k = reinterpret_cast<const uint16_t*>(sb);
+    const uint16_t* hot_v = reinterpret_cast<const uint16_t*>(sb) + (size_t)p.tile_dense * D;
     const int b = row / p.Hkv;
     const int kvh = row - b * p.Hkv;
 
-    if (desc.first_of_piece) {
-      // load this row's query rows (queries x GQA group) into registers / table
+    if (first_of_piece) {
+      m_run = NEG_INF;
+      l_run = 0.f;
 #pragma unroll
-      for (int r = 0; r < RMAX; ++r) {
-        m_run[r] = NEG_INF;
-        l_run[r] = 0.f;
-        qp[r] = 0x7fffffff;
+      for (int r = 0; r < RMAX; ++r)
 #pragma unroll
-        for (int i = 0; i < DPL; ++i) {
-          qreg[r][i] = 0.f;
-          acc[r][i] = 0.f;
+        for (int i = 0; i < DPL; ++i) acc[r][i] = 0.f;
+      {  // A fragments: lane (gA, tA) = (lane/4, lane%4); row gA is query row gA
+        const int gA = lane >> 2, tA = lane & 3;
+        const uint16_t* qrow = nullptr;
+        if (gA < p.R) {
+          const int qi = gA / p.G, g = gA - qi * p.G;
+          qrow = p.q + ((size_t)(b * p.Q + qi) * p.Hq + kvh * p.G + g) * D;
         }
-        if (r < p.R) {
-          const int qi = r / p.G, g = r - qi * p.G;
-          const size_t qoff = ((size_t)(b * p.Q + qi) * p.Hq + kvh * p.G + g);
-          const uint16_t* qsrc = p.q + qoff * D + dim0;
 #pragma unroll
-          for (int gg = 0; gg < NG; ++gg) {
-            const uint4 w = *reinterpret_cast<const uint4*>(qsrc + 8 * gg);
-            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-            float f[8];
-            unpack8(ww, f);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) qreg[r][8 * gg + i] = f[i];
-          }
-          if (p.causal) qp[r] = p.qpos[qoff];
+        for (int s = 0; s < NMMA; ++s) {
+          const int dlo = tA * DPL + 4 * s, dhi = (4 + tA) * DPL + 4 * s;
+          aq[s][0] = qrow ? ldg_u32(qrow + dlo) : 0u;
+          aq[s][1] = qrow ? ldg_u32(qrow + dhi) : 0u;
+          aq[s][2] = qrow ? ldg_u32(qrow + dlo + 2) : 0u;
+          aq[s][3] = qrow ? ldg_u32(qrow + dhi + 2) : 0u;
         }
+      }
+      qp_lane = 0x7fffffff;
+      if (srow < p.R && p.causal) {
+        const int qi = srow / p.G, g = srow - qi * p.G;
+        qp_lane = p.qpos[(size_t)(b * p.Q + qi) * p.Hq + kvh * p.G + g];
       }
       for (int idx = lane; idx < D * RMAX; idx += 32) {
         const int d = idx / RMAX, r = idx - d * RMAX;
@@ -317,133 +380,42 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
           v = h2f(p.q[((size_t)(b * p.Q + qi) * p.Hq + kvh * p.G + g) * D + d]);
         }
         qtab[idx] = v;
-        vsp[idx] = 0.f;
       }
+      for (int idx = lane; idx < 4 * D * RMAX; idx += 32) vsp[idx] = 0.f;
       __syncwarp();
     }
 
-    const int n = desc.n;
+    // chunks are dealt round-robin over the CTA's whole tile stream, so no
+    // warp carries an extra chunk of every tile
     const int nchunks = (n + kChunk - 1) / kChunk;
-    for (int c = warp; c < nchunks; c += NW) {
-      // ---------------- scores ----------------
-      float sc[2][RMAX];
-#pragma unroll
-      for (int rs = 0; rs < 2; ++rs) {
-        const int tl = c * kChunk + rs * 4 + slot;
-        const bool valid = tl < n;
-        float part[RMAX];
-#pragma unroll
-        for (int r = 0; r < RMAX; ++r) part[r] = 0.f;
-        if (valid) {
-#pragma unroll
-          for (int gg = 0; gg < NG; ++gg) {
-            uint32_t w[4];
-            if (desc.kind == 0) {
-              const uint4 v4 = *reinterpret_cast<const uint4*>(sb + desc.off[0] + ((size_t)tl * D + dim0 + 8 * gg) * 2);
-              w[0] = v4.x; w[1] = v4.y; w[2] = v4.z; w[3] = v4.w;
-            } else {
-              const bool act = !p.has_mask || sb[desc.off[2] + tl] != 0;
-              recon8(qv, sb + desc.off[0] + tl * p.M, sb + desc.off[1] + tl * rvq_bpt, act, dim0 + 8 * gg, w);
-            }
-            float f[8];
-            unpack8(w, f);
-#pragma unroll
-            for (int r = 0; r < RMAX; ++r)
-#pragma unroll
-              for (int i = 0; i < 8; ++i) part[r] = __fmaf_rn(qreg[r][8 * gg + i], f[i], part[r]);
-          }
-          if (desc.kind == 1) {
-            for (int e = j; e < p.S; e += 8) {
-              const int idx = sb[desc.off[3] + tl * p.S + e];
-              const float val = h2f(reinterpret_cast<const uint16_t*>(sb + desc.off[4])[tl * p.S + e]);
-#pragma unroll
-              for (int r = 0; r < RMAX; ++r) part[r] = __fmaf_rn(qtab[idx * RMAX + r], val, part[r]);
-            }
-          }
-        }
-#pragma unroll
-        for (int r = 0; r < RMAX; ++r) {
-          float v = part[r];
-          v += __shfl_xor_sync(0xffffffffu, v, 1);
-          v += __shfl_xor_sync(0xffffffffu, v, 2);
-          v += __shfl_xor_sync(0xffffffffu, v, 4);
-          const bool allowed = valid && r < p.R && (!p.causal || desc.pos0 + tl <= qp[r]);
-          sc[rs][r] = allowed ? v * p.scale : NEG_INF;
-        }
-      }
-      // ---------------- online softmax ----------------
-      float pr[2][RMAX];
-      bool grow = false;
-      float alpha[RMAX];
-#pragma unroll
-      for (int r = 0; r < RMAX; ++r) {
-        float mx = fmaxf(sc[0][r], sc[1][r]);
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-        const float m_new = fmaxf(m_run[r], mx);
-        alpha[r] = 1.f;
-        if (m_new > m_run[r]) {
-          alpha[r] = (m_run[r] == NEG_INF) ? 0.f : __expf(m_run[r] - m_new);
-          grow = true;
-          m_run[r] = m_new;
-        }
-        float ls = 0.f;
-#pragma unroll
-        for (int rs = 0; rs < 2; ++rs) {
-          pr[rs][r] = (sc[rs][r] == NEG_INF) ? 0.f : __expf(sc[rs][r] - m_run[r]);
-          ls += pr[rs][r];
-        }
-        ls += __shfl_xor_sync(0xffffffffu, ls, 8);
-        ls += __shfl_xor_sync(0xffffffffu, ls, 16);
-        // xor-8/16 sums over the 4 token slots of one dim-owner j: each token once
-        l_run[r] = l_run[r] * alpha[r] + ls;
-      }
-      if (grow) {  // warp-uniform: m_run is replicated on all lanes
-#pragma unroll
-        for (int r = 0; r < RMAX; ++r)
-#pragma unroll
-          for (int i = 0; i < DPL; ++i) acc[r][i] *= alpha[r];
-        for (int idx = lane; idx < RMAX * D; idx += 32) vsp[idx] *= alpha[idx / D];
-        __syncwarp();
-      }
-      // ---------------- values ----------------
-#pragma unroll
-      for (int rs = 0; rs < 2; ++rs) {
-        const int tl = c * kChunk + rs * 4 + slot;
-        if (tl >= n) continue;
-#pragma unroll
-        for (int gg = 0; gg < NG; ++gg) {
-          uint32_t w[4];
-          if (desc.kind == 0) {
-            const uint4 v4 = *reinterpret_cast<const uint4*>(sb + desc.off[1] + ((size_t)tl * D + dim0 + 8 * gg) * 2);
-            w[0] = v4.x; w[1] = v4.y; w[2] = v4.z; w[3] = v4.w;
-          } else {
-            const bool act = !p.has_mask || sb[desc.off[7] + tl] != 0;
-            recon8(qv, sb + desc.off[5] + tl * p.M, sb + desc.off[6] + tl * rvq_bpt, act, dim0 + 8 * gg, w);
-          }
-          float f[8];
-          unpack8(w, f);
-#pragma unroll
-          for (int r = 0; r < RMAX; ++r)
-#pragma unroll
-            for (int i = 0; i < 8; ++i) acc[r][8 * gg + i] = __fmaf_rn(pr[rs][r], f[i], acc[r][8 * gg + i]);
-        }
-        if (desc.kind == 1) {
-          for (int e = j; e < p.S; e += 8) {
-            const int idx = sb[desc.off[8] + tl * p.S + e];
-            const float val = h2f(reinterpret_cast<const uint16_t*>(sb + desc.off[9])[tl * p.S + e]);
-#pragma unroll
-            for (int r = 0; r < RMAX; ++r)
-              if (r < p.R && pr[rs][r] != 0.f) atomicAdd(&vsp[r * D + idx], pr[rs][r] * val);
-          }
-        }
-      }
+    const int c_first = (warp - chunk_base % NW + NW) % NW;
+    chunk_base += nchunks;
+    cs.n = n;
+    cs.pos0 = pos0;
+    cs.qp_lane = qp_lane;
+    TileView tk, tvv;
+    tk.base = sb; tk.t0 = t0; tk.kvo = 0; tk.dense = hot_k;
+    tvv.base = sb; tvv.t0 = t0; tvv.kvo = 5; tvv.dense = hot_v;
+    if (kind == 0) {
+      for (int c = c_first; c < nchunks; c += NW)
+        process_chunk<D, RMAX, DS, kDense>(cs, tk, tvv, c * kChunk, aq, asp, acc, m_run, l_run);
+    } else if (DS != 0 && mode_codes == kRvq1) {
+      for (int c = c_first; c < nchunks; c += NW)
+        process_chunk<D, RMAX, DS == 0 ? 8 : DS, (DS == 0 ? kGeneric : kRvq1)>(cs, tk, tvv, c * kChunk, aq, asp,
+                                                                               acc, m_run, l_run);
+    } else if (DS != 0 && mode_codes == kPqOnly) {
+      for (int c = c_first; c < nchunks; c += NW)
+        process_chunk<D, RMAX, DS == 0 ? 8 : DS, (DS == 0 ? kGeneric : kPqOnly)>(cs, tk, tvv, c * kChunk, aq, asp,
+                                                                                 acc, m_run, l_run);
+    } else {
+      for (int c = c_first; c < nchunks; c += NW)
+        process_chunk<D, RMAX, DS == 0 ? 8 : DS, kGeneric>(cs, tk, tvv, c * kChunk, aq, asp, acc, m_run, l_run);
     }
     // release the stage
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty_bar[stage]);
 
-    if (desc.last_of_piece) {
+    if (last_of_piece) {
       // reduce over the 4 token slots; fold in the sparse accumulator
 #pragma unroll
       for (int r = 0; r < RMAX; ++r)
@@ -455,40 +427,52 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
           acc[r][i] = v;
         }
       __syncwarp();
+      if (slot == 0) {  // fold the 4 slot copies into acc, then lay out [RMAX][D]
+#pragma unroll
+        for (int i = 0; i < DPL; ++i)
+#pragma unroll
+          for (int s4 = 0; s4 < 4; ++s4) {
+            float cur[RMAX];
+            load_row<RMAX>(vsp + ((size_t)s4 * D + dim0 + i) * RMAX, cur);
+#pragma unroll
+            for (int r = 0; r < RMAX; ++r) acc[r][i] += cur[r];
+          }
+      }
+      __syncwarp();
       if (slot == 0) {
 #pragma unroll
         for (int r = 0; r < RMAX; ++r)
 #pragma unroll
-          for (int i = 0; i < DPL; ++i) vsp[r * D + dim0 + i] += acc[r][i];
+          for (int i = 0; i < DPL; ++i) vsp[r * D + dim0 + i] = acc[r][i];
       }
-      if (lane < RMAX) {
-        s_ml[(warp * RMAX + lane) * 2 + 0] = m_run[lane];
-        s_ml[(warp * RMAX + lane) * 2 + 1] = l_run[lane];
+      if (sslot == 0 && srow < RMAX) {
+        s_ml[(warp * RMAX + srow) * 2 + 0] = m_run;
+        s_ml[(warp * RMAX + srow) * 2 + 1] = l_run;
       }
       if (!consumer_sync(sync_bar, sync_phase, abort)) {
         set_status(p, abort, kDevStatusTimeoutFull);
         break;
       }
-      // combine the NW warps' partials of this row
+      // combine the NW warps' partials of this row (m in log2 units)
       const float* all_vsp = reinterpret_cast<const float*>(smem + p.smem_vsp);
-      const size_t pbase = ((size_t)row * p.max_pieces + desc.piece) * p.R;
+      const size_t pbase = ((size_t)row * p.max_pieces + piece) * p.R;
       for (int idx = threadIdx.x; idx < p.R * D; idx += NW * 32) {
         const int r = idx / D, d = idx - r * D;
-        float M = NEG_INF;
-        for (int w = 0; w < NW; ++w) M = fmaxf(M, s_ml[(w * RMAX + r) * 2]);
+        float Mx = NEG_INF;
+        for (int w = 0; w < NW; ++w) Mx = fmaxf(Mx, s_ml[(w * RMAX + r) * 2]);
         float O = 0.f, Ls = 0.f;
-        if (M != NEG_INF) {
+        if (Mx != NEG_INF) {
           for (int w = 0; w < NW; ++w) {
             const float mw = s_ml[(w * RMAX + r) * 2];
             if (mw == NEG_INF) continue;
-            const float sc_w = __expf(mw - M);
-            O = __fmaf_rn(all_vsp[(size_t)w * RMAX * D + r * D + d], sc_w, O);
+            const float sc_w = ex2_approx(mw - Mx);
+            O = __fmaf_rn(all_vsp[(size_t)w * 4 * RMAX * D + r * D + d], sc_w, O);
             Ls = __fmaf_rn(s_ml[(w * RMAX + r) * 2 + 1], sc_w, Ls);
           }
         }
         p.ws_o[(pbase + r) * D + d] = O;
         if (d == 0) {
-          p.ws_ml[(pbase + r) * 2 + 0] = M;
+          p.ws_ml[(pbase + r) * 2 + 0] = Mx;
           p.ws_ml[(pbase + r) * 2 + 1] = Ls;
         }
       }
@@ -497,7 +481,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
         break;
       }
     }
-    if (++stage == kStages) {
+    if (++stage == p.stages) {
       stage = 0;
       phase ^= 1u;
     }
@@ -531,7 +515,7 @@ __global__ void rfsn_merge_kernel(const __grid_constant__ MergeParams p) {
         const size_t pb = ((size_t)row * p.max_pieces + k) * p.R + r;
         const float mk = p.ws_ml[pb * 2];
         if (mk == NEG_INF) continue;
-        const float s = __expf(mk - M);
+        const float s = ex2_approx(mk - M);
         O = __fmaf_rn(p.ws_o[pb * p.D + d], s, O);
         L = __fmaf_rn(p.ws_ml[pb * 2 + 1], s, L);
       }
@@ -563,7 +547,8 @@ struct Plan {
 // Consumer warps per CTA, chosen so the per-thread register budget of one
 // CTA per SM covers q and the output accumulator without spilling.
 static constexpr int consumer_warps(int D, int rmax) {
-  return D == 64 ? (rmax == 1 ? 16 : rmax == 2 ? 12 : rmax == 4 ? 10 : 6) : (rmax == 1 ? 10 : rmax == 2 ? 8 : 6);
+  // total warps (NW + producer) a multiple of 4 so each SM sub-partition gets the same count
+  return D == 64 ? (rmax <= 4 ? 15 : 11) : (rmax <= 2 ? 15 : 11);
 }
 
 static int sm_count_cached() {
@@ -578,11 +563,7 @@ static int sm_count_cached() {
 }
 
 static void fill_store(StoreDev& d, const rfsn_code_store& s) {
-  d.f[0] = s.pq;
-  d.f[1] = reinterpret_cast<const uint8_t*>(s.rvq);
-  d.f[2] = s.mask;
-  d.f[3] = s.sp_idx;
-  d.f[4] = reinterpret_cast<const uint8_t*>(s.sp_val);
+  d.data = s.data;
   d.cap = s.cap;
   d.rows = s.rows;
 }
@@ -608,8 +589,8 @@ static int make_plan(const rfsn_attn_args* a, const rfsn_quantizer* qz, Plan& pl
   p.B = a->batch; p.Q = a->queries; p.Hq = a->q_heads; p.Hkv = a->kv_heads; p.D = a->head_dim; p.G = G; p.R = R;
   p.causal = a->causal; p.scale = a->scale;
   p.hot_k = a->hot.k; p.hot_v = a->hot.v; p.hot_cap = a->hot.cap;
-  fill_store(p.sk[1], a->warm_k); fill_store(p.sv[1], a->warm_v);
-  fill_store(p.sk[2], a->cold_k); fill_store(p.sv[2], a->cold_v);
+  fill_store(p.st[1], a->warm);
+  fill_store(p.st[2], a->cold);
   p.pq_cb = qz->pq_codebooks; p.rvq_cb = qz->rvq_codebooks;
   p.M = qz->num_subspaces; p.K = qz->pq_codebook_size; p.ds = qz->subspace_dim; p.L = qz->rvq_layers;
   p.Kr = qz->rvq_codebook_size; p.S = qz->sparse_topk; p.rvq_u16 = qz->rvq_codebook_size > 256;
@@ -629,11 +610,8 @@ static int make_plan(const rfsn_attn_args* a, const rfsn_quantizer* qz, Plan& pl
       if ((reinterpret_cast<uintptr_t>(a->hot.k) & 15) || (reinterpret_cast<uintptr_t>(a->hot.v) & 15))
         return RFSN_ERR_ALIGNMENT;
     } else {
-      const rfsn_code_store& ks = s.store == 1 ? a->warm_k : a->cold_k;
-      const rfsn_code_store& vs = s.store == 1 ? a->warm_v : a->cold_v;
+      const rfsn_code_store& ks = s.store == 1 ? a->warm : a->cold;
       if ((st = validate_store(&ks, qz)) != RFSN_OK) return st;
-      if ((st = validate_store(&vs, qz)) != RFSN_OK) return st;
-      if (ks.cap != vs.cap || ks.rows != vs.rows || ks.slots != vs.slots) return RFSN_ERR_INVALID_ARGUMENT;
       if (ks.rows < p.rows) return RFSN_ERR_INVALID_ARGUMENT;
       if (s.slot < 0 || s.slot >= ks.slots || (int64_t)s.first + s.count > ks.cap) return RFSN_ERR_INVALID_ARGUMENT;
     }
@@ -645,52 +623,44 @@ static int make_plan(const rfsn_attn_args* a, const rfsn_quantizer* qz, Plan& pl
   if (W >= (int64_t)1 << 30) return RFSN_ERR_UNSUPPORTED;
   p.W = W;
 
-  // per-token bytes of each compressed field and the stage layout
-  const int rvq_bpt = qz->rvq_layers * (p.rvq_u16 ? 2 : 1);
-  const int bpt[5] = {p.M, rvq_bpt, p.has_mask ? 1 : 0, p.S, p.S * 2};
-  int per_token_bytes = 0;
-  for (int f = 0; f < kNumFields; ++f) {
-    p.field_bpt[f] = bpt[f % 5];
-    per_token_bytes += p.field_bpt[f];
-  }
-  if (p.L == 0) p.field_bpt[1] = p.field_bpt[6] = 0;
-  // compressed tile: largest multiple of 16 tokens (<= 256) whose regions fit a stage
-  int tile = 256;
-  for (; tile >= 16; tile -= 16) {
-    int off = 0;
-    for (int f = 0; f < kNumFields; ++f) {
-      p.field_base[f] = off;
-      if (p.field_bpt[f]) off += (int)align_up((int64_t)tile * p.field_bpt[f], 16) + 16;
-    }
-    if (off <= kStageBytes) break;
-  }
-  if (tile < 16) return RFSN_ERR_UNSUPPORTED;
-  p.tile_codes = tile;
-  p.tile_dense = kStageBytes / (2 * p.D * 2);  // 128 tokens for D=64, 64 for D=128
-  (void)per_token_bytes;
-
+  p.lay = layout_of(qz);
+  // (tile sizes are chosen after the shared-memory layout fixes the stage size)
   // kernel variant
   pl.rmax = R <= 1 ? 1 : R <= 2 ? 2 : R <= 4 ? 4 : 8;
   if (p.D == 128 && pl.rmax > 4) return RFSN_ERR_UNSUPPORTED;
   pl.nw = consumer_warps(p.D, pl.rmax);
   const int64_t pq_bytes = (int64_t)p.M * p.K * p.ds * 2;
   const int64_t rvq_bytes = (int64_t)p.L * p.Kr * p.D * 2;
-  // Shared-memory layout; the RVQ codebook is staged only if it fits (else it
-  // is read through L1/L2 from global memory).
+  // Shared-memory layout: codebooks and per-warp tables first, the TMA ring
+  // takes the rest (3 stages of up to 48 KB).  The RVQ codebook is staged only
+  // if the ring keeps at least 3 x 24 KB (else it is read through L1/L2).
+  p.stages = 3;
   for (int attempt = 0; attempt < 2; ++attempt) {
     pl.rvq_smem = attempt == 0 && p.L > 0 && rvq_bytes <= 64 * 1024;
-    int64_t off = (int64_t)kStages * kStageBytes;
+    int64_t off = 0;
     p.smem_pq = (int)off; off = align_up(off + pq_bytes, 128);
     p.smem_rvq = (int)off; if (pl.rvq_smem) off = align_up(off + rvq_bytes, 128);
     p.smem_qtab = (int)off; off = align_up(off + (int64_t)pl.nw * p.D * pl.rmax * 4, 128);
-    p.smem_vsp = (int)off; off = align_up(off + (int64_t)pl.nw * pl.rmax * p.D * 4, 128);
+    p.smem_vsp = (int)off; off = align_up(off + (int64_t)pl.nw * 4 * pl.rmax * p.D * 4, 128);
     p.smem_ml = (int)off; off = align_up(off + (int64_t)pl.nw * pl.rmax * 2 * 4, 128);
-    p.smem_desc = (int)off; off = align_up(off + (int64_t)kStages * sizeof(TileDesc), 128);
-    p.smem_bar = (int)off; off = align_up(off + (2 * kStages + 1) * 8, 128);
+    p.smem_desc = (int)off; off = align_up(off + (int64_t)kMaxStages * sizeof(TileDesc), 128);
+    p.smem_bar = (int)off; off = align_up(off + (2 * kMaxStages + 1) * 8, 128);
     p.smem_flag = (int)off; off = align_up(off + 16, 128);
-    pl.smem = off;
-    if (pl.smem <= kMaxSmem) break;
+    const int64_t ring = ((kMaxSmem - off) / p.stages) / 1024 * 1024;
+    p.stage_bytes = (int)(ring < kMaxStageBytes ? ring : kMaxStageBytes);
+    pl.smem = off + (int64_t)p.stages * p.stage_bytes;
+    if (p.stage_bytes >= 24 * 1024) break;
   }
+  if (p.stage_bytes < 8 * 1024 || pl.smem > kMaxSmem) return RFSN_ERR_UNSUPPORTED;
+  // the ring sits after the fixed regions
+  p.ring_off = (int)(pl.smem - (int64_t)p.stages * p.stage_bytes);
+  // compressed tile: whole 16-token blocks (<= 64) that fit one stage
+  p.tile_blocks = p.stage_bytes / p.lay.block_bytes;
+  if (p.tile_blocks > 64) p.tile_blocks = 64;
+  if (p.tile_blocks < 2) return RFSN_ERR_UNSUPPORTED;
+  p.tile_dense = (p.stage_bytes / (4 * p.D)) / 16 * 16;  // K and V rows of fp16
+  if (p.tile_dense < 16) return RFSN_ERR_UNSUPPORTED;
+  p.rvq_smem = pl.rvq_smem ? 1 : 0;
   if (pl.smem > kMaxSmem) return RFSN_ERR_UNSUPPORTED;
 
   // work split: equal contiguous ranges of the flattened (row, token) space
@@ -711,9 +681,9 @@ static int make_plan(const rfsn_attn_args* a, const rfsn_quantizer* qz, Plan& pl
   return RFSN_OK;
 }
 
-template <int D, int RMAX, int NW, bool RVQS>
+template <int D, int RMAX, int NW, int DS>
 static cudaError_t launch_variant(const Plan& pl, cudaStream_t s) {
-  auto kern = rfsn_decode_attn_kernel<D, RMAX, NW, RVQS>;
+  auto kern = rfsn_decode_attn_kernel<D, RMAX, NW, DS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
   if (e != cudaSuccess) return e;
   kern<<<pl.grid, (NW + 1) * 32, pl.smem, s>>>(pl.p);
@@ -721,24 +691,26 @@ static cudaError_t launch_variant(const Plan& pl, cudaStream_t s) {
 }
 
 template <int D, int RMAX, int NW>
-static cudaError_t launch_rvq(const Plan& pl, cudaStream_t s) {
-  return pl.rvq_smem ? launch_variant<D, RMAX, NW, true>(pl, s) : launch_variant<D, RMAX, NW, false>(pl, s);
+static cudaError_t launch_ds(const Plan& pl, cudaStream_t s) {
+  if (D == 64 && pl.p.ds == 4) return launch_variant<D, RMAX, NW, 4>(pl, s);
+  if (pl.p.ds == 8) return launch_variant<D, RMAX, NW, 8>(pl, s);
+  return launch_variant<D, RMAX, NW, 0>(pl, s);
 }
 
 static cudaError_t launch(const Plan& pl, cudaStream_t s) {
   const int D = pl.p.D;
   if (D == 64) {
     switch (pl.rmax) {
-      case 1: return launch_rvq<64, 1, consumer_warps(64, 1)>(pl, s);
-      case 2: return launch_rvq<64, 2, consumer_warps(64, 2)>(pl, s);
-      case 4: return launch_rvq<64, 4, consumer_warps(64, 4)>(pl, s);
-      default: return launch_rvq<64, 8, consumer_warps(64, 8)>(pl, s);
+      case 1: return launch_ds<64, 1, consumer_warps(64, 1)>(pl, s);
+      case 2: return launch_ds<64, 2, consumer_warps(64, 2)>(pl, s);
+      case 4: return launch_ds<64, 4, consumer_warps(64, 4)>(pl, s);
+      default: return launch_ds<64, 8, consumer_warps(64, 8)>(pl, s);
     }
   }
   switch (pl.rmax) {
-    case 1: return launch_rvq<128, 1, consumer_warps(128, 1)>(pl, s);
-    case 2: return launch_rvq<128, 2, consumer_warps(128, 2)>(pl, s);
-    default: return launch_rvq<128, 4, consumer_warps(128, 4)>(pl, s);
+    case 1: return launch_ds<128, 1, consumer_warps(128, 1)>(pl, s);
+    case 2: return launch_ds<128, 2, consumer_warps(128, 2)>(pl, s);
+    default: return launch_ds<128, 4, consumer_warps(128, 4)>(pl, s);
   }
 }
 

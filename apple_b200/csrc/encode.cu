@@ -26,11 +26,9 @@ namespace rfsn {
 struct EncodeParams {
   const uint16_t* x;
   int64_t batch, tokens, heads, sb, st, sh;
-  uint8_t* pq;
-  void* rvq;
-  uint8_t* mask;
-  uint8_t* sp_idx;
-  uint16_t* sp_val;
+  uint8_t* data;
+  BlockLayout lay;
+  int kv;
   int64_t cap, rows, slot, first;
   uint16_t* residual_out;
   const uint16_t* pq_cb;
@@ -106,7 +104,12 @@ __global__ void __launch_bounds__(kEncThreads) encode_kernel(const __grid_consta
 
   const int64_t row = b * p.heads + h;
   const int64_t tok = p.first + t;
-  const int64_t base = (p.slot * p.rows + row) * p.cap + tok;
+  const int fk = p.kv * 5;
+  uint8_t* f_pq = p.data + field_byte(p.lay, p.rows, p.cap, p.slot, row, tok, fk + 0);
+  uint8_t* f_rvq = p.data + field_byte(p.lay, p.rows, p.cap, p.slot, row, tok, fk + 1);
+  uint8_t* f_act = p.data + field_byte(p.lay, p.rows, p.cap, p.slot, row, tok, fk + 2);
+  uint8_t* f_spi = p.data + field_byte(p.lay, p.rows, p.cap, p.slot, row, tok, fk + 3);
+  uint16_t* f_spv = reinterpret_cast<uint16_t*>(p.data + field_byte(p.lay, p.rows, p.cap, p.slot, row, tok, fk + 4));
 
   // ---- PQ: per-subspace argmin, fp16 residual (quantization.py:133-142) ----
   uint8_t codes[kMaxD];
@@ -138,7 +141,7 @@ __global__ void __launch_bounds__(kEncThreads) encode_kernel(const __grid_consta
     }
   }
   // store PQ codes
-  for (int m = 0; m < p.M; ++m) p.pq[base * p.M + m] = codes[m];
+  for (int m = 0; m < p.M; ++m) f_pq[m] = codes[m];
 
   // ---- RVQ (quantization.py:216-250) ----
   int rcodes[8] = {0, 0, 0, 0, 0, 0, 0, 0};
@@ -173,19 +176,19 @@ __global__ void __launch_bounds__(kEncThreads) encode_kernel(const __grid_consta
 #pragma unroll
         for (int i = 0; i < D; ++i) res[i] = __fsub_rn(res[i], h2f(chosen[i]));
         if (p.rvq_u16)
-          reinterpret_cast<uint16_t*>(p.rvq)[base * p.L + l] = (uint16_t)bi;
+          reinterpret_cast<uint16_t*>(f_rvq)[l] = (uint16_t)bi;
         else
-          reinterpret_cast<uint8_t*>(p.rvq)[base * p.L + l] = (uint8_t)bi;
+          f_rvq[l] = (uint8_t)bi;
       }
     } else {
       for (int l = 0; l < p.L; ++l) {
         if (p.rvq_u16)
-          reinterpret_cast<uint16_t*>(p.rvq)[base * p.L + l] = 0;
+          reinterpret_cast<uint16_t*>(f_rvq)[l] = 0;
         else
-          reinterpret_cast<uint8_t*>(p.rvq)[base * p.L + l] = 0;
+          f_rvq[l] = 0;
       }
     }
-    p.mask[base] = active ? 1 : 0;
+    f_act[0] = active ? 1 : 0;
   }
 
   // ---- sparse top-S residual (extension) ----
@@ -232,19 +235,17 @@ __global__ void __launch_bounds__(kEncThreads) encode_kernel(const __grid_consta
           mag[i] = -2.f;
         }
       }
-      p.sp_idx[base * p.S + s] = (uint8_t)bi;
-      p.sp_val[base * p.S + s] = f2h(ev);
+      f_spi[s] = (uint8_t)bi;
+      f_spv[s] = f2h(ev);
     }
   }
 }
 
 struct DecodeCodesParams {
   QzView q;
-  const uint8_t* pq;
-  const void* rvq;
-  const uint8_t* mask;
-  const uint8_t* sp_idx;
-  const uint16_t* sp_val;
+  const uint8_t* data;
+  BlockLayout lay;
+  int kv;
   int64_t cap, store_rows, nrows, slot, first, count, heads;
   uint16_t* out;
   int64_t sb, st, sh;
@@ -257,22 +258,28 @@ __global__ void decode_codes_kernel(const __grid_constant__ DecodeCodesParams p)
     const int g = (int)(i % G);
     const int64_t t = (i / G) % p.count;
     const int64_t row = i / ((int64_t)G * p.count);
-    const int64_t base = (p.slot * p.store_rows + row) * p.cap + p.first + t;
-    const int csz = p.q.rvq_u16 ? 2 : 1;
-    const bool active = p.q.L > 0 && (p.mask == nullptr || p.mask[base] != 0);
+    const int64_t tok = p.first + t;
+    const int fk = p.kv * 5;
+    const uint8_t* f_pq = p.data + field_byte(p.lay, p.store_rows, p.cap, p.slot, row, tok, fk + 0);
+    const uint8_t* f_rvq = p.data + field_byte(p.lay, p.store_rows, p.cap, p.slot, row, tok, fk + 1);
+    const uint8_t* f_act = p.data + field_byte(p.lay, p.store_rows, p.cap, p.slot, row, tok, fk + 2);
+    const uint8_t* f_spi = p.data + field_byte(p.lay, p.store_rows, p.cap, p.slot, row, tok, fk + 3);
+    const uint16_t* f_spv =
+        reinterpret_cast<const uint16_t*>(p.data + field_byte(p.lay, p.store_rows, p.cap, p.slot, row, tok, fk + 4));
+    const bool active = p.q.L > 0 && f_act[0] != 0;
     uint32_t w[4];
-    recon8(p.q, p.pq + base * p.q.M, reinterpret_cast<const uint8_t*>(p.rvq) + base * p.q.L * csz, active, 8 * g, w);
+    recon8(p.q, f_pq, f_rvq, active, 8 * g, w);
     if (p.q.S > 0) {
       float f[8];
       unpack8(w, f);
       bool touched = false;
       for (int e = 0; e < p.q.S; ++e) {
-        const int id = p.sp_idx[base * p.q.S + e] - 8 * g;
+        const int id = f_spi[e] - 8 * g;
         if (id >= 0 && id < 8) {
           touched = true;
 #pragma unroll
           for (int k = 0; k < 8; ++k)
-            if (k == id) f[k] = __fadd_rn(f[k], h2f(p.sp_val[base * p.q.S + e]));
+            if (k == id) f[k] = __fadd_rn(f[k], h2f(f_spv[e]));
         }
       }
       if (touched) {
@@ -296,7 +303,7 @@ using namespace rfsn;
 
 extern "C" int rfsn_encode(const rfsn_quantizer* qz, const uint16_t* x, int64_t batch, int64_t tokens, int64_t heads,
                            int64_t stride_b, int64_t stride_t, int64_t stride_h, const rfsn_code_store* dst,
-                           int64_t dst_slot, int64_t dst_first, uint16_t* residual_out, void* stream) {
+                           int32_t kv, int64_t dst_slot, int64_t dst_first, uint16_t* residual_out, void* stream) {
   int st = validate_quantizer(qz);
   if (st != RFSN_OK) return st;
   if (!x || !dst || batch < 0 || tokens < 0 || heads <= 0) return RFSN_ERR_INVALID_ARGUMENT;
@@ -305,7 +312,7 @@ extern "C" int rfsn_encode(const rfsn_quantizer* qz, const uint16_t* x, int64_t 
   st = validate_store(dst, qz);
   if (st != RFSN_OK) return st;
   if (batch * heads > dst->rows || dst_slot < 0 || dst_slot >= dst->slots || dst_first < 0 ||
-      dst_first + tokens > dst->cap)
+      dst_first + tokens > dst->cap || (kv != 0 && kv != 1))
     return RFSN_ERR_INVALID_ARGUMENT;
   if (((uintptr_t)x & 15) || (stride_b & 7) || (stride_t & 7) || (stride_h & 7)) return RFSN_ERR_ALIGNMENT;
   const int64_t nvec = batch * tokens * heads;
@@ -314,7 +321,7 @@ extern "C" int rfsn_encode(const rfsn_quantizer* qz, const uint16_t* x, int64_t 
   EncodeParams p{};
   p.x = x; p.batch = batch; p.tokens = tokens; p.heads = heads;
   p.sb = stride_b; p.st = stride_t; p.sh = stride_h;
-  p.pq = dst->pq; p.rvq = dst->rvq; p.mask = dst->mask; p.sp_idx = dst->sp_idx; p.sp_val = dst->sp_val;
+  p.data = dst->data; p.lay = layout_of(qz); p.kv = kv;
   p.cap = dst->cap; p.rows = dst->rows; p.slot = dst_slot; p.first = dst_first;
   p.residual_out = residual_out;
   p.pq_cb = qz->pq_codebooks; p.rvq_cb = qz->rvq_codebooks;
@@ -341,15 +348,16 @@ extern "C" int rfsn_encode(const rfsn_quantizer* qz, const uint16_t* x, int64_t 
   return check_cuda(e == cudaSuccess ? cudaGetLastError() : e);
 }
 
-extern "C" int rfsn_decode_codes(const rfsn_quantizer* qz, const rfsn_code_store* src, int64_t slot, int64_t first,
-                                 int64_t count, int64_t batch, int64_t heads, uint16_t* out, int64_t stride_b,
-                                 int64_t stride_t, int64_t stride_h, void* stream) {
+extern "C" int rfsn_decode_codes(const rfsn_quantizer* qz, const rfsn_code_store* src, int32_t kv, int64_t slot,
+                                 int64_t first, int64_t count, int64_t batch, int64_t heads, uint16_t* out,
+                                 int64_t stride_b, int64_t stride_t, int64_t stride_h, void* stream) {
   int st = validate_quantizer(qz);
   if (st != RFSN_OK) return st;
   if (!src || !out || count < 0 || batch < 0 || heads <= 0) return RFSN_ERR_INVALID_ARGUMENT;
   st = validate_store(src, qz);
   if (st != RFSN_OK) return st;
-  if (batch * heads > src->rows || slot < 0 || slot >= src->slots || first < 0 || first + count > src->cap)
+  if (batch * heads > src->rows || slot < 0 || slot >= src->slots || first < 0 || first + count > src->cap ||
+      (kv != 0 && kv != 1))
     return RFSN_ERR_INVALID_ARGUMENT;
   if (((uintptr_t)out & 15) || (stride_b & 7) || (stride_t & 7) || (stride_h & 7)) return RFSN_ERR_ALIGNMENT;
   if (count == 0 || batch == 0) return RFSN_OK;
@@ -358,7 +366,7 @@ extern "C" int rfsn_decode_codes(const rfsn_quantizer* qz, const rfsn_code_store
   p.q.M = qz->num_subspaces; p.q.K = qz->pq_codebook_size; p.q.ds = qz->subspace_dim; p.q.L = qz->rvq_layers;
   p.q.Kr = qz->rvq_codebook_size; p.q.D = qz->head_dim; p.q.S = qz->sparse_topk;
   p.q.rvq_u16 = qz->rvq_codebook_size > 256;
-  p.pq = src->pq; p.rvq = src->rvq; p.mask = src->mask; p.sp_idx = src->sp_idx; p.sp_val = src->sp_val;
+  p.data = src->data; p.lay = layout_of(qz); p.kv = kv;
   p.cap = src->cap; p.store_rows = src->rows; p.nrows = batch * heads; p.slot = slot; p.first = first;
   p.count = count; p.heads = heads;
   p.out = out; p.sb = stride_b; p.st = stride_t; p.sh = stride_h;

@@ -5,6 +5,7 @@
 #include <stdint.h>
 
 #include "../../include/rfsn_b200.h"
+#include "rfsn_layout.h"
 
 namespace rfsn {
 
@@ -14,8 +15,10 @@ int check_cuda(cudaError_t e);
 // Checks the quantizer description: shapes, codebook pointers and alignment.
 int validate_quantizer(const rfsn_quantizer* qz);
 
-// Checks a code store against the quantizer: pointers present for the enabled
-// fields, cap a multiple of 16, 16-byte aligned bases.
+// Checks a code store: data present and 16-byte aligned, cap a multiple of 16.
 int validate_store(const rfsn_code_store* s, const rfsn_quantizer* qz);
+
+// Block layout of a code store for this quantizer.
+BlockLayout layout_of(const rfsn_quantizer* qz);
 
 }  // namespace rfsn

@@ -90,51 +90,95 @@ class QuantizerBuffers:
         return q
 
 
+BLOCK_TOKENS = 16
+FIELD_NAMES = ("pq", "rvq", "active", "sp_idx", "sp_val")
+
+
+def block_layout(qz: "QuantizerBuffers"):
+    """Byte layout of one 16-token block (mirrors apple_b200/csrc/rfsn_layout.h).
+
+    Returns (offsets[10], bytes_per_token[5], block_bytes); field f = kv*5 + k with
+    k in (pq, rvq, active, sp_idx, sp_val)."""
+    cs = 2 if qz.Kr > 256 else 1
+    bpt = [qz.M, qz.L * cs, 1 if qz.L > 0 else 0, qz.sparse_topk, 2 * qz.sparse_topk]
+    off, pos = [], 0
+    for f in range(10):
+        off.append(pos)
+        pos += BLOCK_TOKENS * bpt[f % 5]
+    return off, bpt, pos
+
+
 class CodeStoreBuffers:
-    """Device arrays of an ``rfsn_code_store``: [slots, rows, cap, ...] per field."""
+    """Device (or pinned host) ``rfsn_code_store``: K and V codes of [slots, rows, cap]
+    tokens in 16-token blocks that interleave every field (one contiguous range per
+    token run, so a tile is one bulk copy)."""
 
     def __init__(self, qz: QuantizerBuffers, rows: int, cap: int, slots: int = 1,
                  device: Optional[torch.device] = None, pin_memory: bool = False):
         cap = align16(max(cap, 16))
         dev = device if device is not None else qz.pq_codebooks.device
-        kw = dict(device="cpu", pin_memory=True) if pin_memory else dict(device=dev)
+        self.qz = qz
         self.rows, self.cap, self.slots = rows, cap, slots
-        self.pq = torch.zeros((slots, rows, cap, qz.M), dtype=torch.uint8, **kw)
-        L = max(qz.L, 0)
-        self.rvq = torch.zeros((slots, rows, cap, L), dtype=qz.rvq_code_dtype, **kw) if L else None
-        self.mask = torch.zeros((slots, rows, cap), dtype=torch.uint8, **kw) if L else None
-        S = qz.sparse_topk
-        self.sp_idx = torch.zeros((slots, rows, cap, S), dtype=torch.uint8, **kw) if S else None
-        self.sp_val = torch.zeros((slots, rows, cap, S), dtype=torch.float16, **kw) if S else None
-
-    def fields(self) -> List[Optional[torch.Tensor]]:
-        return [self.pq, self.rvq, self.mask, self.sp_idx, self.sp_val]
+        self.off, self.bpt, self.block_bytes = block_layout(qz)
+        shape = (slots, rows, cap // BLOCK_TOKENS, self.block_bytes)
+        if pin_memory:
+            self.data = torch.zeros(shape, dtype=torch.uint8, device="cpu", pin_memory=True)
+        else:
+            self.data = torch.zeros(shape, dtype=torch.uint8, device=dev)
 
     def struct(self) -> CodeStore:
         s = CodeStore()
-        s.pq, s.rvq, s.mask, s.sp_idx, s.sp_val = (_ptr(t) for t in self.fields())
+        s.data = _ptr(self.data)
         s.cap, s.rows, s.slots = self.cap, self.rows, self.slots
         return s
 
-    def nbytes_per_slot(self) -> int:
-        return sum(t[0].numel() * t.element_size() for t in self.fields() if t is not None)
+    def field(self, kv: int, name: str) -> Optional[torch.Tensor]:
+        """Strided view [slots, rows, cap/16, 16, width] of one field (None if absent).
 
-    def copy_slot_(self, dst_slot: int, src: "CodeStoreBuffers", src_slot: int, non_blocking: bool = True) -> None:
-        for d, s in zip(self.fields(), src.fields()):
-            if d is not None:
-                d[dst_slot].copy_(s[src_slot], non_blocking=non_blocking)
+        dtypes: pq/active/sp_idx uint8; rvq uint8 (Kr <= 256) or int16; sp_val fp16."""
+        k = FIELD_NAMES.index(name)
+        w = self.bpt[k]
+        if w == 0:
+            return None
+        f = kv * 5 + k
+        v = self.data[..., self.off[f]: self.off[f] + BLOCK_TOKENS * w]
+        v = v.unflatten(-1, (BLOCK_TOKENS, w))
+        if name == "sp_val":
+            v = v.view(torch.float16)
+        elif name == "rvq" and self.qz.Kr > 256:
+            v = v.view(torch.int16)
+        return v
+
+    def read(self, kv: int, name: str, slot: int, row: int, first: int, count: int) -> Optional[torch.Tensor]:
+        """Copy of a field for tokens [first, first+count) of one row: [count, width]."""
+        v = self.field(kv, name)
+        if v is None:
+            return None
+        t = torch.arange(first, first + count, device=v.device)
+        return v[slot, row, t // BLOCK_TOKENS, t % BLOCK_TOKENS]
+
+    def write(self, kv: int, name: str, slot: int, row: int, first: int, values: torch.Tensor) -> None:
+        """Scatter [count, width] values into tokens [first, first+count) of one row."""
+        v = self.field(kv, name)
+        if v is None:
+            return
+        t = torch.arange(first, first + values.shape[0], device=v.device)
+        v[slot, row, t // BLOCK_TOKENS, t % BLOCK_TOKENS] = values.to(device=v.device, dtype=v.dtype)
+
+    def nbytes_per_slot(self) -> int:
+        return self.data[0].numel()
 
     def grow(self, qz: QuantizerBuffers, new_cap: int) -> "CodeStoreBuffers":
-        new = CodeStoreBuffers(qz, self.rows, new_cap, self.slots, device=self.pq.device)
-        for d, s in zip(new.fields(), self.fields()):
-            if d is not None:
-                d[:, :, : self.cap].copy_(s)
+        new = CodeStoreBuffers(qz, self.rows, new_cap, self.slots, device=self.data.device)
+        nb = self.cap // BLOCK_TOKENS
+        new.data[:, :, :nb].copy_(self.data)
         return new
 
 
 def encode(qz: QuantizerBuffers, x: torch.Tensor, store: CodeStoreBuffers, slot: int, first: int,
-           residual_out: Optional[torch.Tensor] = None) -> None:
-    """Encode fp16 vectors x [B, T, H, D] (D contiguous) into rows b*H+h, tokens first..first+T."""
+           residual_out: Optional[torch.Tensor] = None, kv: int = 0) -> None:
+    """Encode fp16 vectors x [B, T, H, D] (D contiguous) into the K (kv=0) or V (kv=1)
+    fields of rows b*H+h, tokens first..first+T."""
     _need_cuda(x, "x")
     if x.dtype != torch.float16 or x.dim() != 4 or x.shape[-1] != qz.D or x.stride(-1) != 1:
         raise ValueError("x must be fp16 [B, T, H, D] with a contiguous last dim")
@@ -144,19 +188,20 @@ def encode(qz: QuantizerBuffers, x: torch.Tensor, store: CodeStoreBuffers, slot:
     q = qz.struct()
     s = store.struct()
     call("rfsn_encode", C.byref(q), _ptr(x), B, T, H, x.stride(0), x.stride(1), x.stride(2), C.byref(s),
-         slot, first, _ptr(residual_out), _stream())
+         kv, slot, first, _ptr(residual_out), _stream())
 
 
 def decode_codes(qz: QuantizerBuffers, store: CodeStoreBuffers, slot: int, first: int, count: int,
-                 out: torch.Tensor) -> torch.Tensor:
-    """Exact fp16 decode of tokens [first, first+count) into out [B, count, H, D] (D contiguous)."""
+                 out: torch.Tensor, kv: int = 0) -> torch.Tensor:
+    """Exact fp16 decode of K (kv=0) or V (kv=1) tokens [first, first+count) into
+    out [B, count, H, D] (D contiguous)."""
     _need_cuda(out, "out")
     if out.dtype != torch.float16 or out.dim() != 4 or out.shape[1] != count or out.stride(-1) != 1:
         raise ValueError("out must be fp16 [B, count, H, D]")
     B, _, H, _ = out.shape
     q = qz.struct()
     s = store.struct()
-    call("rfsn_decode_codes", C.byref(q), C.byref(s), slot, first, count, B, H, _ptr(out), out.stride(0),
+    call("rfsn_decode_codes", C.byref(q), C.byref(s), kv, slot, first, count, B, H, _ptr(out), out.stride(0),
          out.stride(1), out.stride(2), _stream())
     return out
 
@@ -177,12 +222,12 @@ def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
 def decode_attention(qz: QuantizerBuffers, q: torch.Tensor, out: torch.Tensor, segments: Sequence[Tuple],
                      kv_heads: int, qpos: Optional[torch.Tensor] = None, causal: bool = True, scale: Optional[float] = None,
                      hot: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
-                     warm: Optional[Tuple[CodeStoreBuffers, CodeStoreBuffers]] = None,
-                     cold: Optional[Tuple[CodeStoreBuffers, CodeStoreBuffers]] = None,
+                     warm: Optional[CodeStoreBuffers] = None,
+                     cold: Optional[CodeStoreBuffers] = None,
                      num_ctas: int = 0, device_status: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Fused decode attention.  q/out fp16 [B, Q, Hq, D]; qpos int32 [B, Q, Hq] (global positions).
 
-    hot: (k, v) fp16 [rows, cap, D]; warm/cold: (k_store, v_store).
+    hot: (k, v) fp16 [rows, cap, D]; warm/cold: code stores (K and V fields).
     segments: (store, slot, first, count, pos0) tuples in window order.
     """
     _need_cuda(q, "q")
@@ -203,9 +248,9 @@ def decode_attention(qz: QuantizerBuffers, q: torch.Tensor, out: torch.Tensor, s
     if hot is not None:
         a.hot = DenseStore(_ptr(hot[0]), _ptr(hot[1]), hot[0].shape[1], hot[0].shape[0])
     if warm is not None:
-        a.warm_k, a.warm_v = warm[0].struct(), warm[1].struct()
+        a.warm = warm.struct()
     if cold is not None:
-        a.cold_k, a.cold_v = cold[0].struct(), cold[1].struct()
+        a.cold = cold.struct()
     a.head_dim = D
     a.causal = int(bool(causal))
     a.scale = float(D ** -0.5 if scale is None else scale)

@@ -67,22 +67,37 @@ typedef struct rfsn_quantizer {
   int32_t sparse_topk;           /* S: extension, top-S |error| fp16 entries per token (0 = off) */
 } rfsn_quantizer;
 
-/* Compressed code store (the device form of CompressedTensorMLX, storage.py:75-98).
- * Dense per-token layout: token t of row r in slot s lives at index
- * (s * rows + r) * cap + t of every array.  RVQ codes are stored for every
- * token (zero when inactive) next to a per-token activity byte, instead of the
- * reference's (codes, offsets) pair; rvq[mask] and flatnonzero(mask) give the
- * reference form back. */
+/* Compressed code store: the device form of a key/value pair of
+ * CompressedTensorMLX (storage.py:75-98).
+ *
+ * Tokens are grouped in blocks of RFSN_BLOCK_TOKENS (16) consecutive tokens of
+ * one row; a block holds every field of the K codes and then of the V codes:
+ *
+ *   K pq     uint8  [16][M]
+ *   K rvq    uint8  [16][L] (Kr <= 256) or uint16 [16][L]   (absent if L == 0)
+ *   K active uint8  [16]   1 = RVQ codes apply              (absent if L == 0)
+ *   K sp_idx uint8  [16][S]                                  (absent if S == 0)
+ *   K sp_val fp16   [16][S]                                  (absent if S == 0)
+ *   V ... the same five fields
+ *
+ * Every sub-array is a multiple of 16 bytes, so blocks and fields stay 16-byte
+ * aligned; rfsn_code_block_bytes() gives the block size.  Block b of row r of
+ * slot s starts at data + ((s * rows + r) * (cap / 16) + b) * block_bytes, so
+ * a run of tokens of one row is one contiguous byte range (one bulk copy).
+ * RVQ codes are stored for every token (zero when inactive) next to the
+ * activity byte, instead of the reference's (codes, offsets) pair;
+ * rvq[active] and flatnonzero(active) give the reference form back. */
+#define RFSN_BLOCK_TOKENS 16
+
 typedef struct rfsn_code_store {
-  uint8_t* pq;       /* uint8  [slots][rows][cap][M] */
-  void* rvq;         /* uint8 or uint16 [slots][rows][cap][L] */
-  uint8_t* mask;     /* uint8  [slots][rows][cap]  1 = RVQ active */
-  uint8_t* sp_idx;   /* uint8  [slots][rows][cap][S] */
-  uint16_t* sp_val;  /* fp16   [slots][rows][cap][S] */
+  uint8_t* data;     /* [slots][rows][cap / 16][block_bytes] */
   int64_t cap;       /* tokens per row; multiple of 16 */
   int64_t rows;      /* rows per slot (batch * kv heads) */
-  int64_t slots;     /* number of slots (1 for hot/warm stores; >1 for a cold chunk pool) */
+  int64_t slots;     /* number of slots (1 for a warm store; >1 for a cold chunk pool) */
 } rfsn_code_store;
+
+/* Bytes of one 16-token block for this quantizer (K and V fields). */
+int64_t rfsn_code_block_bytes(const rfsn_quantizer* qz);
 
 /* Dense fp16 store for exact (hot) tokens: [rows][cap][D]. */
 typedef struct rfsn_dense_store {
@@ -99,19 +114,20 @@ typedef struct rfsn_dense_store {
  * the way RFSNv10KVCacheMLX._add_to_warm / _add_to_cold append (cache.py:122-191).
  *
  * x: fp16, vector (b, t, h) at x[b*stride_b + t*stride_t + h*stride_h], D contiguous.
- * Vector (b, t, h) is written to row b*heads + h, token dst_first + t of slot dst_slot.
+ * Vector (b, t, h) is written to the K (kv = 0) or V (kv = 1) fields of row b*heads + h,
+ * token dst_first + t of slot dst_slot.
  * residual_out (optional, may be NULL): fp16 PQ residual in the same layout as x. */
 int rfsn_encode(const rfsn_quantizer* qz, const uint16_t* x, int64_t batch, int64_t tokens, int64_t heads,
-                int64_t stride_b, int64_t stride_t, int64_t stride_h, const rfsn_code_store* dst,
+                int64_t stride_b, int64_t stride_t, int64_t stride_h, const rfsn_code_store* dst, int32_t kv,
                 int64_t dst_slot, int64_t dst_first, uint16_t* residual_out, void* stream);
 
 /* Decode compressed tokens to dense fp16 — _decode_compressed_tensor (quantization.py:394-402),
  * i.e. fp16(pq_decode + rvq_correction) (:319) plus the sparse residual added in fp32 and
- * rounded once.  Tokens [first, first+count) of every row of slot `slot`; token i of row
+ * rounded once.  K (kv = 0) or V (kv = 1) tokens [first, first+count) of every row of slot `slot`; token i of row
  * (b, h) goes to out[b*stride_b + i*stride_t + h*stride_h] (D contiguous).  This is what
  * RFSNv10KVCacheMLX.materialize_window (cache.py:344-393) returns for warm/cold tokens. */
-int rfsn_decode_codes(const rfsn_quantizer* qz, const rfsn_code_store* src, int64_t slot, int64_t first,
-                      int64_t count, int64_t batch, int64_t heads, uint16_t* out, int64_t stride_b,
+int rfsn_decode_codes(const rfsn_quantizer* qz, const rfsn_code_store* src, int32_t kv, int64_t slot,
+                      int64_t first, int64_t count, int64_t batch, int64_t heads, uint16_t* out, int64_t stride_b,
                       int64_t stride_t, int64_t stride_h, void* stream);
 
 /* One contiguous run of window tokens in one store. */
@@ -143,8 +159,8 @@ typedef struct rfsn_attn_args {
   int32_t causal;
   float scale;                     /* head_dim ** -0.5 in the reference (cache.py:424) */
   rfsn_dense_store hot;
-  rfsn_code_store warm_k, warm_v;
-  rfsn_code_store cold_k, cold_v;
+  rfsn_code_store warm;
+  rfsn_code_store cold;
   const rfsn_segment* segments;
   int32_t num_segments;
   int32_t num_ctas;                /* 0 = one CTA per SM */

@@ -8,24 +8,28 @@ from apple_b200 import kernels as K
 
 
 def codes_to_store(qz: K.QuantizerBuffers, codes_per_row, cap: int, store: K.CodeStoreBuffers = None,
-                   slot: int = 0, first: int = 0):
-    """codes_per_row: list (one per row) of oracle ``Codes`` with [T, 1, ...] or [T, ...] arrays."""
+                   slot: int = 0, first: int = 0, kv: int = 0, slots: int = 1):
+    """Write oracle ``Codes`` (one per row, arrays [T, ...]) into the K (kv=0) or V (kv=1)
+    fields of a packed code store, tokens [first, first+T) of each row."""
     rows = len(codes_per_row)
     if store is None:
-        store = K.CodeStoreBuffers(qz, rows, cap)
-    dev = store.pq.device
+        store = K.CodeStoreBuffers(qz, rows, cap, slots=slots)
     for r, c in enumerate(codes_per_row):
         T = c.pq.shape[0]
-        sl = slice(first, first + T)
-        store.pq[slot, r, sl] = torch.from_numpy(c.pq.reshape(T, -1)).to(dev)
-        if store.rvq is not None:
-            rv = c.rvq.reshape(T, -1).astype(np.int64)
-            store.rvq[slot, r, sl] = torch.from_numpy(rv).to(dev).to(store.rvq.dtype)
-            store.mask[slot, r, sl] = torch.from_numpy(c.mask.reshape(T).astype(np.uint8)).to(dev)
-        if store.sp_idx is not None:
-            store.sp_idx[slot, r, sl] = torch.from_numpy(c.sp_idx.reshape(T, -1)).to(dev)
-            store.sp_val[slot, r, sl] = torch.from_numpy(c.sp_val.reshape(T, -1)).to(dev)
+        store.write(kv, "pq", slot, r, first, torch.from_numpy(np.ascontiguousarray(c.pq.reshape(T, -1))))
+        if qz.L:
+            rv = torch.from_numpy(c.rvq.reshape(T, -1).astype(np.int64))
+            store.write(kv, "rvq", slot, r, first, rv)
+            store.write(kv, "active", slot, r, first, torch.from_numpy(c.mask.reshape(T, 1).astype(np.uint8)))
+        if qz.sparse_topk:
+            store.write(kv, "sp_idx", slot, r, first, torch.from_numpy(np.ascontiguousarray(c.sp_idx.reshape(T, -1))))
+            store.write(kv, "sp_val", slot, r, first, torch.from_numpy(np.ascontiguousarray(c.sp_val.reshape(T, -1))))
     return store
+
+
+def kv_to_store(qz, kcodes, vcodes, cap, store=None, slot=0, first=0, slots=1):
+    store = codes_to_store(qz, kcodes, cap, store=store, slot=slot, first=first, kv=0, slots=slots)
+    return codes_to_store(qz, vcodes, cap, store=store, slot=slot, first=first, kv=1)
 
 
 def to_dev(a, dtype=None):

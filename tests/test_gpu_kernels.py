@@ -20,7 +20,7 @@ pytestmark = pytest.mark.gpu
 
 if torch.cuda.is_available():
     from apple_b200 import kernels as K
-    from tests.gpu_util import codes_to_store, to_dev
+    from tests.gpu_util import codes_to_store, kv_to_store, to_dev
 
 QUANT_CASES = ["quant_d128_m8x16_rvq3", "quant_d64_m16x4_rvq1_dense", "quant_d64_m8x8_rvq1", "quant_d64_m8x8_pqonly"]
 
@@ -58,17 +58,17 @@ def test_encode_matches_reference_codes(name):
     res = torch.empty_like(x)
     K.encode(qz, x.view(1, N, 1, D), store, 0, 0, residual_out=res.view(1, N, 1, D))
     torch.cuda.synchronize()
-    pq = store.pq[0, 0, :N].cpu().numpy()
+    pq = store.read(0, "pq", 0, 0, 0, N).cpu().numpy()
     pq_tie_ok(g["x"], g["pq_codebooks"], pq, g["pq_codes"])
     agree = (pq == g["pq_codes"]).all(axis=1)
     assert agree.mean() > 0.99
     np.testing.assert_array_equal(res.cpu().numpy()[agree].view(np.uint16), g["residual"][agree].view(np.uint16))
     if qz.L:
-        mask = store.mask[0, 0, :N].cpu().numpy().astype(bool)
+        mask = store.read(0, "active", 0, 0, 0, N)[:, 0].cpu().numpy().astype(bool)
         np.testing.assert_array_equal(mask[agree], g["rvq_mask"][agree])
         dense = np.zeros((N, qz.L), np.int64)
         dense[g["rvq_offsets"]] = g["rvq_codes"]
-        got = store.rvq[0, 0, :N].cpu().numpy().astype(np.int64)
+        got = store.read(0, "rvq", 0, 0, 0, N).cpu().numpy().astype(np.int64)
         sel = agree & g["rvq_mask"]
         if sel.any():
             assert ((got[sel] == dense[sel]).all(axis=1)).mean() > 0.99
@@ -100,11 +100,11 @@ def test_sparse_encode_and_decode_match_oracle():
     ref = oq.compress(x[:, None])
     store = K.CodeStoreBuffers(qz, rows=1, cap=N)
     K.encode(qz, to_dev(x).view(1, N, 1, D), store, 0, 0)
-    pq = store.pq[0, 0, :N].cpu().numpy()
+    pq = store.read(0, "pq", 0, 0, 0, N).cpu().numpy()
     agree = (pq == ref.pq[:, 0]).all(axis=1)
     assert agree.mean() > 0.99
-    np.testing.assert_array_equal(store.sp_idx[0, 0, :N].cpu().numpy()[agree], ref.sp_idx[agree, 0])
-    np.testing.assert_array_equal(store.sp_val[0, 0, :N].cpu().numpy()[agree].view(np.uint16),
+    np.testing.assert_array_equal(store.read(0, "sp_idx", 0, 0, 0, N).cpu().numpy()[agree], ref.sp_idx[agree, 0])
+    np.testing.assert_array_equal(store.read(0, "sp_val", 0, 0, 0, N).cpu().numpy()[agree].view(np.uint16),
                                   ref.sp_val[agree, 0].view(np.uint16))
     # decode of the oracle's codes is bit-exact with the oracle decode
     st2 = codes_to_store(qz, [R.Codes(ref.pq[:, 0], ref.rvq[:, 0], ref.mask[:, 0], ref.sp_idx[:, 0],
@@ -126,12 +126,10 @@ def test_hybrid_attention_golden():
     oq = R.Quantizer(g["pq_codebooks"], g["rvq_codebooks"], float(g["threshold"]))
     kc, vc = oq.compress(g["keys"]), oq.compress(g["values"])
     H, T = 4, 24
-    per_row_k = [kc.slice(0, T) for _ in range(H)]
-    ks = codes_to_store(qz, [R.Codes(kc.pq[:, h], kc.rvq[:, h], kc.mask[:, h], kc.sp_idx[:, h], kc.sp_val[:, h])
-                             for h in range(H)], cap=T)
-    vs = codes_to_store(qz, [R.Codes(vc.pq[:, h], vc.rvq[:, h], vc.mask[:, h], vc.sp_idx[:, h], vc.sp_val[:, h])
-                             for h in range(H)], cap=T)
-    del per_row_k
+    ws = kv_to_store(qz, [R.Codes(kc.pq[:, h], kc.rvq[:, h], kc.mask[:, h], kc.sp_idx[:, h], kc.sp_val[:, h])
+                          for h in range(H)],
+                     [R.Codes(vc.pq[:, h], vc.rvq[:, h], vc.mask[:, h], vc.sp_idx[:, h], vc.sp_val[:, h])
+                      for h in range(H)], cap=T)
     q = to_dev(g["q"]).view(1, 2, H, 128)  # two queries against one sequence
     out = torch.empty_like(q)
     seg = [(K.STORE_WARM, 0, 0, T, 0)]
@@ -140,7 +138,7 @@ def test_hybrid_attention_golden():
         qpos = None
         if causal:
             qpos = to_dev(np.broadcast_to(np.asarray(pos, np.int32).reshape(2, -1), (2, H)).reshape(1, 2, H).copy())
-        K.decode_attention(qz, q, out, seg, kv_heads=H, qpos=qpos, causal=causal, warm=(ks, vs))
+        K.decode_attention(qz, q, out, seg, kv_heads=H, qpos=qpos, causal=causal, warm=ws)
         assert_attn_close(out.cpu().numpy()[0], g[key], key)
 
 
@@ -169,13 +167,10 @@ def test_tiered_attention_golden(num_ctas):
     def rows(c):
         return [R.Codes(c.pq[:, h], c.rvq[:, h], c.mask[:, h], c.sp_idx[:, h], c.sp_val[:, h]) for h in range(H)]
 
-    wk = codes_to_store(qz, rows(oc.warm_k[0]), cap=32)
-    wv = codes_to_store(qz, rows(oc.warm_v[0]), cap=32)
-    ck = K.CodeStoreBuffers(qz, rows=H, cap=16, slots=len(oc.cold))
-    cv = K.CodeStoreBuffers(qz, rows=H, cap=16, slots=len(oc.cold))
+    ws = kv_to_store(qz, rows(oc.warm_k[0]), rows(oc.warm_v[0]), cap=32)
+    cst = K.CodeStoreBuffers(qz, rows=H, cap=16, slots=len(oc.cold))
     for i, meta in enumerate(oc.cold):
-        codes_to_store(qz, rows(meta["k"][0]), cap=16, store=ck, slot=i)
-        codes_to_store(qz, rows(meta["v"][0]), cap=16, store=cv, slot=i)
+        kv_to_store(qz, rows(meta["k"][0]), rows(meta["v"][0]), cap=16, store=cst, slot=i)
     q = to_dev(g["q"]).view(1, 1, H, D)
     out = torch.empty_like(q)
     spans = [(K.STORE_HOT, 0, 0, 16), (K.STORE_WARM, 0, 16, 24)] + \
@@ -191,7 +186,7 @@ def test_tiered_attention_golden(num_ctas):
                 segs.append((st, slot, a - s0, b - a, a))
         qp = to_dev(_qpos_global(adj, start, (1, 1)).repeat(H).reshape(1, 1, H))
         K.decode_attention(qz, q, out, segs, kv_heads=H, qpos=qp, causal=True, hot=(hot_k, hot_v),
-                           warm=(wk, wv), cold=(ck, cv), num_ctas=num_ctas)
+                           warm=ws, cold=cst, num_ctas=num_ctas)
         assert_attn_close(out.cpu().numpy()[0], g[f"{tag}_out"], tag)
 
 
@@ -231,8 +226,7 @@ def test_fused_attention_vs_oracle(B, Hkv, G, Qn, D, ds, L, S, thr, T_hot, T_war
         return [R.Codes(c.pq[:, h], c.rvq[:, h], c.mask[:, h], c.sp_idx[:, h], c.sp_val[:, h])
                 for c in cs for h in range(Hkv)]
 
-    wk = codes_to_store(qz, rows(kc), cap=T_warm)
-    wv = codes_to_store(qz, rows(vc), cap=T_warm)
+    ws = kv_to_store(qz, rows(kc), rows(vc), cap=T_warm)
     hot_k = to_dev(np.ascontiguousarray(k[:, T_warm:].transpose(0, 2, 1, 3).reshape(B * Hkv, T_hot, D)))
     hot_v = to_dev(np.ascontiguousarray(v[:, T_warm:].transpose(0, 2, 1, 3).reshape(B * Hkv, T_hot, D)))
     Hq = Hkv * G
@@ -244,7 +238,7 @@ def test_fused_attention_vs_oracle(B, Hkv, G, Qn, D, ds, L, S, thr, T_hot, T_war
     out = torch.empty((B, Qn, Hq, D), dtype=torch.float16, device="cuda")
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     K.decode_attention(qz, to_dev(q), out, segs, kv_heads=Hkv, qpos=to_dev(pos), causal=True,
-                       hot=(hot_k, hot_v), warm=(wk, wv), num_ctas=num_ctas, device_status=status)
+                       hot=(hot_k, hot_v), warm=ws, num_ctas=num_ctas, device_status=status)
     got = out.cpu().numpy()
     assert int(status.item()) == 0
     for b in range(B):
@@ -273,4 +267,4 @@ def test_abi_rejects_out_of_range_segment():
     out = torch.empty_like(q)
     from apple_b200 import RFSNError
     with pytest.raises(RFSNError):
-        K.decode_attention(qz, q, out, [(K.STORE_WARM, 0, 20, 20, 0)], kv_heads=4, causal=False, warm=(st, st))
+        K.decode_attention(qz, q, out, [(K.STORE_WARM, 0, 20, 20, 0)], kv_heads=4, causal=False, warm=st)
