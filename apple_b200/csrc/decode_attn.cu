@@ -14,19 +14,19 @@
 // (max, sum, unnormalised output) per row it touches; rfsn_merge_kernel combines
 // the partials of each row by log-sum-exp and writes fp16.
 //
-// Inside a CTA.  Warp NW (the producer, one elected lane) walks the CTA's tiles
-// and issues 1-D bulk TMA copies (cp.async.bulk) of each tile's code streams
-// (PQ, RVQ, RVQ-active, sparse idx/val) or hot fp16 K/V rows into a 3-stage
-// shared-memory ring, signalling an mbarrier with the byte count.  Consumer
-// warps 0..NW-1 take 8-token chunks of a tile; 8 lanes cooperate on one token,
-// lane j owning dims [j*D/8, (j+1)*D/8).  For each token a lane rebuilds its
-// dims exactly (fp16 PQ centroid + fp16 RVQ correction, fp16 add — see
-// rfsn_decode.cuh) from codebooks staged in shared memory, forms partial dot
-// products for every query row of the KV head (GQA group x queries), and the
-// 8 partials are combined with xor-shuffles.  The top-S sparse residual enters
-// K scores as q[idx]*val (fp32) and V outputs through a per-warp shared
-// accumulator.  Softmax state is fp32 and rescaled only when a row's running
-// max grows.  All waits are bounded (rfsn_common.cuh).
+// Inside a CTA.  Warp NW (the producer) walks the CTA's tiles and issues 1-D
+// bulk TMA copies (cp.async.bulk): a code tile is a run of whole 16-token
+// blocks of the packed store (K and V fields interleaved, rfsn_layout.h), one
+// contiguous copy; a hot tile is two copies (K rows, V rows).  Copies land in
+// a shared-memory ring whose stages are guarded by full/empty mbarriers.
+// Consumer warps 0..NW-1 take one 16-token block at a time (dealt
+// round-robin); 8 lanes cooperate on one token, lane j owning dims
+// [j*D/8, (j+1)*D/8).  A lane rebuilds its dims exactly from codebooks staged
+// in shared memory (rfsn_attn_chunk.cuh), K scores for all query rows of the
+// KV head (GQA group x queries) come from one tensor-core MMA per 8 dims, and
+// V is accumulated in fp32 with paired FMAs.  Softmax state is fp32 and
+// rescaled only when a row's running max grows.  All waits are bounded
+// (rfsn_common.cuh).
 #include <cuda_runtime.h>
 #include <math.h>
 
@@ -39,7 +39,7 @@ namespace rfsn {
 
 constexpr int kMaxStages = 8;                // mbarrier slots reserved per CTA
 constexpr int kMaxStageBytes = 48 * 1024;    // upper bound of one ring stage
-constexpr int kChunk = 16;      // tokens per warp chunk (4 row-steps of 4 tokens)
+constexpr int kNoLimit = 1 << 30;         // position limit of a row that sees every token
 constexpr int64_t kMaxSmem = 227 * 1024;  // opt-in shared memory per CTA on sm_100
 
 struct SegDev {
@@ -71,7 +71,7 @@ struct AttnParams {
   int max_pieces;
   int tile_blocks, tile_dense;  // code-tile length in 16-token blocks; dense-tile length in tokens
   int nseg;
-  int smem_pq, smem_rvq, smem_qtab, smem_vsp, smem_ml, smem_desc, smem_bar, smem_flag;
+  int smem_pq, smem_pqsw, smem_rvq, smem_scr, scr_bytes, smem_ml, smem_desc, smem_bar, smem_flag;
   int stages, stage_bytes, ring_off;  // ring depth, bytes per stage, ring offset in smem
   SegDev seg[RFSN_MAX_SEGMENTS];
 };
@@ -98,7 +98,7 @@ __device__ __forceinline__ bool consumer_sync(uint64_t* bar, uint32_t& phase, vo
   return ok;
 }
 
-template <int D, int RMAX, int NW, int DS>
+template <int D, int RMAX, int NW, int LP>
 __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr int DPL = D / 8;  // dims per lane
@@ -108,6 +108,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
   TileDesc* descs = reinterpret_cast<TileDesc*>(smem + p.smem_desc);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + p.smem_flag);
   uint16_t* s_pq = reinterpret_cast<uint16_t*>(smem + p.smem_pq);
+  uint16_t* s_pqsw = reinterpret_cast<uint16_t*>(smem + p.smem_pqsw);  // 4-dim presets only
   uint16_t* s_rvq = reinterpret_cast<uint16_t*>(smem + p.smem_rvq);
 
   const int warp = threadIdx.x >> 5;
@@ -124,26 +125,30 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
   }
   {  // stage codebooks
     // PQ codebook [M][K][ds] staged code-major [K][M][ds]: one code's centroids
-    // for all subspaces form one row, so a token's lanes read distinct banks
+    // for all subspaces form one row, so a token's lanes read distinct banks.
+    // Consecutive threads write consecutive shared addresses (i = (c*M + m)*per + part).
     const int nc = p.M * p.K;
     if (p.ds % 8 == 0) {
       const int per = p.ds / 8;
       for (int i = threadIdx.x; i < nc * per; i += blockDim.x) {
         const int cen = i / per, part = i - cen * per;
-        const int m = cen / p.K, c = cen - m * p.K;
-        reinterpret_cast<uint4*>(s_pq)[(c * p.M + m) * per + part] =
-            __ldg(reinterpret_cast<const uint4*>(p.pq_cb) + i);
+        const int c = cen / p.M, m = cen - c * p.M;
+        reinterpret_cast<uint4*>(s_pq)[i] = __ldg(reinterpret_cast<const uint4*>(p.pq_cb) + (m * p.K + c) * per + part);
       }
     } else if (p.ds == 4) {
+      // 4-dim presets also stage a copy with subspace pairs swapped (position m holds m^1)
+      const bool sw = LP != kGeneric && Preset<LP>::DS == 4;
       for (int i = threadIdx.x; i < nc; i += blockDim.x) {
-        const int m = i / p.K, c = i - m * p.K;
-        reinterpret_cast<uint2*>(s_pq)[c * p.M + m] = __ldg(reinterpret_cast<const uint2*>(p.pq_cb) + i);
+        const int c = i / p.M, m = i - c * p.M;
+        const uint2 v = __ldg(reinterpret_cast<const uint2*>(p.pq_cb) + m * p.K + c);
+        reinterpret_cast<uint2*>(s_pq)[i] = v;
+        if (sw) reinterpret_cast<uint2*>(s_pqsw)[i ^ 1] = v;
       }
     } else {
       for (int i = threadIdx.x; i < nc * p.ds; i += blockDim.x) {
         const int cen = i / p.ds, k = i - cen * p.ds;
-        const int m = cen / p.K, c = cen - m * p.K;
-        s_pq[(c * p.M + m) * p.ds + k] = p.pq_cb[i];
+        const int c = cen / p.M, m = cen - c * p.M;
+        s_pq[i] = p.pq_cb[(m * p.K + c) * p.ds + k];
       }
     }
     if (p.rvq_smem && p.L > 0) {
@@ -282,46 +287,32 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
   const int dim0 = j * DPL;
   const int srow = lane >> 2;   // score lane: query row r
   const int sslot = lane & 3;   // score lane: token slot
-  float* qtab = reinterpret_cast<float*>(smem + p.smem_qtab) + (size_t)warp * D * RMAX;  // [D][RMAX]
-  // sparse-V sums, one copy per token slot (a token's sparse dims are distinct, so
-  // plain read-modify-write is race-free): [4][D][RMAX]; reused as [RMAX][D] to combine
-  float* vsp = reinterpret_cast<float*>(smem + p.smem_vsp) + (size_t)warp * 4 * RMAX * D;
-  float* s_ml = reinterpret_cast<float*>(smem + p.smem_ml);                              // [NW][RMAX][2]
-  const int M = p.M, Kc = p.K, L = p.L, S = p.S;
-  const int rvq_bpt = L * (p.rvq_u16 ? 2 : 1);
+  // per-warp scratch: fp16 sparse scatter rows while a piece runs, then the
+  // warp's fp32 partial output [RMAX][D] when it ends
+  unsigned char* scr = smem + p.smem_scr + (size_t)warp * p.scr_bytes;
+  float* s_ml = reinterpret_cast<float*>(smem + p.smem_ml);  // [NW][RMAX][2]
   const float NEG_INF = __int_as_float(0xff800000);
-  const float sl2 = p.scale * 1.4426950408889634f;  // scores kept in log2 units
   constexpr int NMMA = DPL / 4;  // K mma k-steps per row-step
-  constexpr int NSP = (RMAX + 3) / 4;
+  constexpr int kBlock = LP != kGeneric ? Preset<LP>::BLOCK : 0;
+  const int block_bytes = LP != kGeneric ? kBlock : p.lay.block_bytes;
 
-  ChunkShared cs;
-  cs.pq_cm = s_pq;
-  cs.rvq_s = s_rvq;
-  cs.rvq_g = p.rvq_cb;
-  cs.qtab = qtab;
-  cs.vsp = vsp;
-  cs.M = M; cs.K = Kc; cs.ds = p.ds; cs.L = L; cs.Kr = p.Kr; cs.S = S; cs.rvq_u16 = p.rvq_u16;
-  cs.rvq_smem = p.rvq_smem; cs.has_mask = p.has_mask; cs.rvq_bpt = rvq_bpt;
-  cs.lay = p.lay;
-  cs.R = p.R; cs.causal = p.causal; cs.sl2 = sl2;
-  cs.n = 0; cs.pos0 = 0; cs.qp_lane = 0;
-  const int mode_codes = (L == 1 && p.rvq_smem && !p.rvq_u16 && S <= 8) ? kRvq1
-                         : (L == 0 && S <= 8) ? kPqOnly : kGeneric;
-  uint32_t aq[NMMA][4];      // query A fragments
-  uint32_t asp[NSP][4];      // constant 0/1 A fragments summing sparse corrections over 8 lanes
+  ChunkCtx c;
+  c.pq_cm = s_pq;
+  c.pq_sel = (Preset<LP>::DS == 4 && LP != kGeneric && (slot & 1)) ? s_pqsw : s_pq;
+  c.rvq_s = s_rvq;
+  c.rvq_g = p.rvq_cb;
+  c.scratch = reinterpret_cast<uint16_t*>(scr);
+  c.lay = p.lay;
+  c.M = p.M; c.K = p.K; c.ds = p.ds; c.L = p.L; c.Kr = p.Kr; c.S = p.S; c.rvq_u16 = p.rvq_u16;
+  c.rvq_smem = p.rvq_smem; c.has_mask = p.has_mask;
+  c.qp_lim = 0;
+  c.sl2 = p.scale * 1.4426950408889634f;  // scores kept in log2 units
+  uint32_t aq[NMMA][4];  // query A fragments
   float acc[RMAX][DPL];
   float m_run = NEG_INF, l_run = 0.f;  // online state of row srow (replicated over its 4 lanes)
-  int qp_lane = 0x7fffffff;            // causal position of row srow
   int stage = 0;
   uint32_t phase = 0, sync_phase = 0;
   int chunk_base = 0;  // global index of the current tile's first chunk
-
-#pragma unroll
-  for (int t = 0; t < NSP; ++t) {
-    const int gA = lane >> 2;
-    asp[t][0] = asp[t][1] = pack_h2(gA == 4 * t ? 1.f : 0.f, gA == 4 * t + 1 ? 1.f : 0.f);
-    asp[t][2] = asp[t][3] = pack_h2(gA == 4 * t + 2 ? 1.f : 0.f, gA == 4 * t + 3 ? 1.f : 0.f);
-  }
 
   for (;;) {
     if (!mbar_wait_bounded(&full_bar[stage], phase, abort)) {
@@ -338,7 +329,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
     const int last_of_piece = dsc->last_of_piece;
     const int piece = dsc->piece;
     const unsigned char* sb = smem + p.ring_off + (size_t)stage * p.stage_bytes;
-    const int t0 = dsc->t0;
+    const int lead = kind == 0 ? 0 : dsc->t0;  // tokens of the first block that precede the tile
     const uint16_t* hot_k = reinterpret_cast<const uint16_t*>(sb);
     const uint16_t* hot_v = reinterpret_cast<const uint16_t*>(sb) + (size_t)p.tile_dense * D;
     const int b = row / p.Hkv;
@@ -367,56 +358,42 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
           aq[s][3] = qrow ? ldg_u32(qrow + dhi + 2) : 0u;
         }
       }
-      qp_lane = 0x7fffffff;
+      // last position row srow may see; rows past R see nothing
+      c.qp_lim = srow < p.R ? kNoLimit : -kNoLimit;
       if (srow < p.R && p.causal) {
         const int qi = srow / p.G, g = srow - qi * p.G;
-        qp_lane = p.qpos[(size_t)(b * p.Q + qi) * p.Hq + kvh * p.G + g];
+        c.qp_lim = p.qpos[(size_t)(b * p.Q + qi) * p.Hq + kvh * p.G + g];
       }
-      for (int idx = lane; idx < D * RMAX; idx += 32) {
-        const int d = idx / RMAX, r = idx - d * RMAX;
-        float v = 0.f;
-        if (r < p.R) {
-          const int qi = r / p.G, g = r - qi * p.G;
-          v = h2f(p.q[((size_t)(b * p.Q + qi) * p.Hq + kvh * p.G + g) * D + d]);
-        }
-        qtab[idx] = v;
-      }
-      for (int idx = lane; idx < 4 * D * RMAX; idx += 32) vsp[idx] = 0.f;
+      for (int idx = lane; idx < p.scr_bytes / 16; idx += 32)
+        reinterpret_cast<uint4*>(scr)[idx] = make_uint4(0u, 0u, 0u, 0u);
       __syncwarp();
     }
 
-    // chunks are dealt round-robin over the CTA's whole tile stream, so no
-    // warp carries an extra chunk of every tile
-    const int nchunks = (n + kChunk - 1) / kChunk;
+    // chunks (16-token blocks) are dealt round-robin over the CTA's whole tile
+    // stream, so no warp carries an extra chunk of every tile
+    const int span = lead + n;
+    const int nchunks = (span + kBlockTokens - 1) / kBlockTokens;
     const int c_first = (warp - chunk_base % NW + NW) % NW;
     chunk_base += nchunks;
-    cs.n = n;
-    cs.pos0 = pos0;
-    cs.qp_lane = qp_lane;
-    TileView tk, tvv;
-    tk.base = sb; tk.t0 = t0; tk.kvo = 0; tk.dense = hot_k;
-    tvv.base = sb; tvv.t0 = t0; tvv.kvo = 5; tvv.dense = hot_v;
-    if (kind == 0) {
-      for (int c = c_first; c < nchunks; c += NW)
-        process_chunk<D, RMAX, DS, kDense>(cs, tk, tvv, c * kChunk, aq, asp, acc, m_run, l_run);
-    } else if (DS != 0 && mode_codes == kRvq1) {
-      for (int c = c_first; c < nchunks; c += NW)
-        process_chunk<D, RMAX, DS == 0 ? 8 : DS, (DS == 0 ? kGeneric : kRvq1)>(cs, tk, tvv, c * kChunk, aq, asp,
-                                                                               acc, m_run, l_run);
-    } else if (DS != 0 && mode_codes == kPqOnly) {
-      for (int c = c_first; c < nchunks; c += NW)
-        process_chunk<D, RMAX, DS == 0 ? 8 : DS, (DS == 0 ? kGeneric : kPqOnly)>(cs, tk, tvv, c * kChunk, aq, asp,
-                                                                                 acc, m_run, l_run);
-    } else {
-      for (int c = c_first; c < nchunks; c += NW)
-        process_chunk<D, RMAX, DS == 0 ? 8 : DS, kGeneric>(cs, tk, tvv, c * kChunk, aq, asp, acc, m_run, l_run);
+    for (int ch = c_first; ch < nchunks; ch += NW) {
+      const int t_lo = ch == 0 ? lead : 0;
+      const int t_hi = min(kBlockTokens, span - ch * kBlockTokens);
+      const int pos_base = pos0 - lead + ch * kBlockTokens;
+      if (kind == 0) {
+        const size_t r0 = (size_t)ch * kBlockTokens * D;
+        process_block<D, RMAX, LP, true>(c, nullptr, hot_k + r0, hot_v + r0, t_lo, t_hi, pos_base, aq, acc, m_run,
+                                         l_run);
+      } else {
+        process_block<D, RMAX, LP, false>(c, sb + ch * block_bytes, nullptr, nullptr, t_lo, t_hi, pos_base, aq,
+                                          acc, m_run, l_run);
+      }
     }
     // release the stage
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty_bar[stage]);
 
     if (last_of_piece) {
-      // reduce over the 4 token slots; fold in the sparse accumulator
+      // reduce over the 4 token slots, then lay the warp's partial out as [RMAX][D]
 #pragma unroll
       for (int r = 0; r < RMAX; ++r)
 #pragma unroll
@@ -426,24 +403,14 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
           v += __shfl_xor_sync(0xffffffffu, v, 16);
           acc[r][i] = v;
         }
-      __syncwarp();
-      if (slot == 0) {  // fold the 4 slot copies into acc, then lay out [RMAX][D]
-#pragma unroll
-        for (int i = 0; i < DPL; ++i)
-#pragma unroll
-          for (int s4 = 0; s4 < 4; ++s4) {
-            float cur[RMAX];
-            load_row<RMAX>(vsp + ((size_t)s4 * D + dim0 + i) * RMAX, cur);
-#pragma unroll
-            for (int r = 0; r < RMAX; ++r) acc[r][i] += cur[r];
-          }
-      }
-      __syncwarp();
+      float* part = reinterpret_cast<float*>(scr);
       if (slot == 0) {
 #pragma unroll
         for (int r = 0; r < RMAX; ++r)
 #pragma unroll
-          for (int i = 0; i < DPL; ++i) vsp[r * D + dim0 + i] = acc[r][i];
+          for (int i = 0; i < DPL; i += 4)
+            *reinterpret_cast<float4*>(part + r * D + dim0 + i) =
+                make_float4(acc[r][i], acc[r][i + 1], acc[r][i + 2], acc[r][i + 3]);
       }
       if (sslot == 0 && srow < RMAX) {
         s_ml[(warp * RMAX + srow) * 2 + 0] = m_run;
@@ -454,7 +421,6 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
         break;
       }
       // combine the NW warps' partials of this row (m in log2 units)
-      const float* all_vsp = reinterpret_cast<const float*>(smem + p.smem_vsp);
       const size_t pbase = ((size_t)row * p.max_pieces + piece) * p.R;
       for (int idx = threadIdx.x; idx < p.R * D; idx += NW * 32) {
         const int r = idx / D, d = idx - r * D;
@@ -466,7 +432,8 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
             const float mw = s_ml[(w * RMAX + r) * 2];
             if (mw == NEG_INF) continue;
             const float sc_w = ex2_approx(mw - Mx);
-            O = __fmaf_rn(all_vsp[(size_t)w * 4 * RMAX * D + r * D + d], sc_w, O);
+            const float* wp = reinterpret_cast<const float*>(smem + p.smem_scr + (size_t)w * p.scr_bytes);
+            O = __fmaf_rn(wp[r * D + d], sc_w, O);
             Ls = __fmaf_rn(s_ml[(w * RMAX + r) * 2 + 1], sc_w, Ls);
           }
         }
@@ -537,7 +504,7 @@ __global__ void rfsn_zero_kernel(uint16_t* out, int64_t n) {
 
 struct Plan {
   AttnParams p;
-  int nw, rmax;
+  int nw, rmax, lp;
   bool rvq_smem;
   int64_t smem;
   int grid;
@@ -560,6 +527,26 @@ static int sm_count_cached() {
     if (count <= 0) count = 148;
   }
   return count;
+}
+
+// Compile-time layout preset for this configuration (kGeneric when none fits).
+static int pick_preset(const AttnParams& p, bool rvq_smem) {
+  if (p.D != 64 || p.K != 256) return kGeneric;
+  if (p.L == 1 && (!rvq_smem || p.Kr != 256)) return kGeneric;
+  int lp = kGeneric;
+  if (p.ds == 4 && p.L == 1 && !p.has_mask && p.S == 8) lp = kDs4Rvq1DenseS8;
+  else if (p.ds == 4 && p.L == 1 && p.has_mask && p.S == 0) lp = kDs4Rvq1Mask;
+  else if (p.ds == 8 && p.L == 0 && p.S == 0) lp = kDs8PqOnly;
+  else if (p.ds == 8 && p.L == 1 && p.has_mask && p.S == 0) lp = kDs8Rvq1Mask;
+  bool ok = true;
+  switch (lp) {
+    case kDs4Rvq1DenseS8: ok = preset_layout_matches<kDs4Rvq1DenseS8>(p.lay); break;
+    case kDs4Rvq1Mask: ok = preset_layout_matches<kDs4Rvq1Mask>(p.lay); break;
+    case kDs8PqOnly: ok = preset_layout_matches<kDs8PqOnly>(p.lay); break;
+    case kDs8Rvq1Mask: ok = preset_layout_matches<kDs8Rvq1Mask>(p.lay); break;
+    default: break;
+  }
+  return ok ? lp : (int)kGeneric;
 }
 
 static void fill_store(StoreDev& d, const rfsn_code_store& s) {
@@ -631,17 +618,22 @@ static int make_plan(const rfsn_attn_args* a, const rfsn_quantizer* qz, Plan& pl
   pl.nw = consumer_warps(p.D, pl.rmax);
   const int64_t pq_bytes = (int64_t)p.M * p.K * p.ds * 2;
   const int64_t rvq_bytes = (int64_t)p.L * p.Kr * p.D * 2;
-  // Shared-memory layout: codebooks and per-warp tables first, the TMA ring
+  // Shared-memory layout: codebooks and per-warp scratch first, the TMA ring
   // takes the rest (3 stages of up to 48 KB).  The RVQ codebook is staged only
   // if the ring keeps at least 3 x 24 KB (else it is read through L1/L2).
+  // Per-warp scratch: 32*D bytes = fp16 sparse scatter rows [2][2][4][D], reused
+  // for the warp's fp32 partial output [RMAX][D] (RMAX <= 8).
   p.stages = 3;
+  p.scr_bytes = 32 * p.D;
   for (int attempt = 0; attempt < 2; ++attempt) {
     pl.rvq_smem = attempt == 0 && p.L > 0 && rvq_bytes <= 64 * 1024;
+    pl.lp = pick_preset(p, pl.rvq_smem);
+    const bool pq_swap = pl.lp == kDs4Rvq1DenseS8 || pl.lp == kDs4Rvq1Mask;
     int64_t off = 0;
     p.smem_pq = (int)off; off = align_up(off + pq_bytes, 128);
+    p.smem_pqsw = (int)off; if (pq_swap) off = align_up(off + pq_bytes, 128);
     p.smem_rvq = (int)off; if (pl.rvq_smem) off = align_up(off + rvq_bytes, 128);
-    p.smem_qtab = (int)off; off = align_up(off + (int64_t)pl.nw * p.D * pl.rmax * 4, 128);
-    p.smem_vsp = (int)off; off = align_up(off + (int64_t)pl.nw * 4 * pl.rmax * p.D * 4, 128);
+    p.smem_scr = (int)off; off = align_up(off + (int64_t)pl.nw * p.scr_bytes, 128);
     p.smem_ml = (int)off; off = align_up(off + (int64_t)pl.nw * pl.rmax * 2 * 4, 128);
     p.smem_desc = (int)off; off = align_up(off + (int64_t)kMaxStages * sizeof(TileDesc), 128);
     p.smem_bar = (int)off; off = align_up(off + (2 * kMaxStages + 1) * 8, 128);
@@ -681,9 +673,9 @@ static int make_plan(const rfsn_attn_args* a, const rfsn_quantizer* qz, Plan& pl
   return RFSN_OK;
 }
 
-template <int D, int RMAX, int NW, int DS>
+template <int D, int RMAX, int NW, int LP>
 static cudaError_t launch_variant(const Plan& pl, cudaStream_t s) {
-  auto kern = rfsn_decode_attn_kernel<D, RMAX, NW, DS>;
+  auto kern = rfsn_decode_attn_kernel<D, RMAX, NW, LP>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
   if (e != cudaSuccess) return e;
   kern<<<pl.grid, (NW + 1) * 32, pl.smem, s>>>(pl.p);
@@ -692,9 +684,16 @@ static cudaError_t launch_variant(const Plan& pl, cudaStream_t s) {
 
 template <int D, int RMAX, int NW>
 static cudaError_t launch_ds(const Plan& pl, cudaStream_t s) {
-  if (D == 64 && pl.p.ds == 4) return launch_variant<D, RMAX, NW, 4>(pl, s);
-  if (pl.p.ds == 8) return launch_variant<D, RMAX, NW, 8>(pl, s);
-  return launch_variant<D, RMAX, NW, 0>(pl, s);
+  if constexpr (D == 64) {
+    switch (pl.lp) {
+      case kDs4Rvq1DenseS8: return launch_variant<D, RMAX, NW, kDs4Rvq1DenseS8>(pl, s);
+      case kDs4Rvq1Mask: return launch_variant<D, RMAX, NW, kDs4Rvq1Mask>(pl, s);
+      case kDs8PqOnly: return launch_variant<D, RMAX, NW, kDs8PqOnly>(pl, s);
+      case kDs8Rvq1Mask: return launch_variant<D, RMAX, NW, kDs8Rvq1Mask>(pl, s);
+      default: break;
+    }
+  }
+  return launch_variant<D, RMAX, NW, kGeneric>(pl, s);
 }
 
 static cudaError_t launch(const Plan& pl, cudaStream_t s) {

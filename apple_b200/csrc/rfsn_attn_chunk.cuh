@@ -1,18 +1,30 @@
-// rfsn_attn_chunk.cuh — one warp's work on one 16-token chunk of a tile.
+// rfsn_attn_chunk.cuh — one consumer warp's work on one 16-token block of a tile.
 //
-// A chunk is 4 row-steps of 4 tokens; lane (slot, j) handles token slot of a
-// row-step and dims [j*D/8, (j+1)*D/8).  Work is written as straight-line
-// phases over pairs of row-steps (all code loads, then all codebook gathers,
-// then arithmetic) so shared-memory latency overlaps across tokens; tokens
-// past the tile end read token 0's data (always valid) and are masked out of
-// the softmax instead of branched around.
+// A chunk is one 16-token block of the code store (or 16 hot rows): 4
+// row-steps of 4 tokens; lane (slot, j) handles token 4*rs + slot of the block
+// and dims [j*D/8, (j+1)*D/8).  Work is straight-line phases over pairs of
+// row-steps so shared-memory latency overlaps across tokens; tokens outside
+// the tile's valid range [t_lo, t_hi) are masked in the softmax instead of
+// branched around.
 //
-// Modes: kDense (hot fp16 rows), kRvq1 (PQ + one uint8 RVQ layer staged in
-// shared memory, sparse S <= 8), kPqOnly (PQ, sparse S <= 8), kGeneric (any
-// RVQ layout / sparse width, via recon_lane).  PQ codebooks are staged
-// code-major ([K][M][ds]) so one token's 8 lanes read 8 distinct banks; with
-// 4-dim subspaces odd token slots load their two centroids in swapped order
-// so a half-warp (two tokens) stays conflict-free.
+// Exact values.  A lane rebuilds its dims the way the reference decodes them
+// (quantization.py:310-319): fp16 PQ centroid + fp16 RVQ row (one layer) or
+// fp16(fp32 sum of rows), fp16 add.  The top-S sparse residual is applied as
+// materialisation does, value = fp16(recon + val): each lane writes its
+// token's entries into a per-warp fp16 scratch row [slot][D] (a token's
+// entries have distinct dims), the warp syncs, and every lane reads back its
+// own dims as 16-byte loads, adds them with __hadd2 and zeroes them.  Two
+// scratch buffers alternate between consecutive rounds, so the __syncwarp of
+// one round orders the previous round's zeroing before the next writes to the
+// same buffer.  fp32 addition of two fp16 values followed by one rounding to
+// fp16 equals the correctly rounded fp16 sum (24 >= 2*11+1 bits), so __hadd2
+// reproduces the fp32-then-round decode exactly.
+//
+// Layout presets (LP) fix the block layout at compile time for the common
+// D = 64 configurations, so field addresses are block base + immediates.  The
+// PQ codebook is staged code-major ([K][M][ds]); with 4-dim subspaces odd
+// token slots read a second copy whose subspace pairs are swapped, so the two
+// tokens of a half-warp cover all 32 banks once with no selects.
 #pragma once
 
 #include "rfsn_attn_util.cuh"
@@ -21,214 +33,231 @@
 
 namespace rfsn {
 
-enum ChunkMode { kDense = 0, kRvq1 = 1, kPqOnly = 2, kGeneric = 3 };
-
-struct TileView {
-  const unsigned char* base;  // compressed tiles: the stage holding whole 16-token blocks
-  int t0;                     // index of the tile's first token inside the first block
-  int kvo;                    // field offset: 0 = K fields, 5 = V fields
-  const uint16_t* dense;      // hot fp16 rows (dense tiles)
+enum LayoutPreset {
+  kGeneric = 0,         // runtime layout: any ds, RVQ depth, code width, sparse width, D = 64 or 128
+  kDs4Rvq1DenseS8 = 1,  // D=64, PQ 16x4 K=256, one uint8 RVQ layer (Kr=256) on every token, top-8 sparse
+  kDs4Rvq1Mask = 2,     // D=64, PQ 16x4 K=256, one uint8 RVQ layer gated by activity bytes, no sparse
+  kDs8PqOnly = 3,       // D=64, PQ 8x8 K=256, no RVQ, no sparse
+  kDs8Rvq1Mask = 4,     // D=64, PQ 8x8 K=256, one uint8 RVQ layer gated by activity bytes, no sparse
 };
 
-struct ChunkShared {
-  const uint16_t* pq_cm;    // code-major PQ codebook [K][M][ds] (shared)
-  const uint16_t* rvq_s;    // RVQ codebook [L][Kr][D] (shared, when staged)
-  const uint16_t* rvq_g;    // RVQ codebook in global memory
-  const float* qtab;        // this warp's fp32 query table [D][RMAX]
-  float* vsp;               // this warp's sparse-V sums [4][D][RMAX]
-  int M, K, ds, L, Kr, S, rvq_u16, rvq_smem, has_mask, rvq_bpt;
-  BlockLayout lay;          // field offsets inside a 16-token block
-  int n, pos0, R, causal, qp_lane;
-  float sl2;                // scale * log2(e)
+template <int LP>
+struct Preset {
+  static constexpr int DS = (LP == kDs4Rvq1DenseS8 || LP == kDs4Rvq1Mask) ? 4 : 8;
+  static constexpr int M = 64 / DS;
+  static constexpr int L = (LP == kDs8PqOnly) ? 0 : 1;
+  static constexpr bool MASK = (LP == kDs4Rvq1Mask || LP == kDs8Rvq1Mask);
+  static constexpr int S = (LP == kDs4Rvq1DenseS8) ? 8 : 0;
+  // field offsets inside a block: K fields, then the same V fields at FB
+  static constexpr int OPQ = 0;
+  static constexpr int ORVQ = OPQ + 16 * M;
+  static constexpr int OACT = ORVQ + 16 * L;
+  static constexpr int OSPI = OACT + 16 * L;
+  static constexpr int OSPV = OSPI + 16 * S;
+  static constexpr int FB = OSPV + 32 * S;
+  static constexpr int BLOCK = 2 * FB;
 };
 
-// code-major PQ gather of one lane's 8 dims [d0, d0+8) (fast paths).
-template <int DS>
-__device__ __forceinline__ void pq8_cm(const uint16_t* cm, int M, const unsigned char* codes, int d0, bool odd,
-                                       uint32_t* o) {
-  if constexpr (DS == 4) {
-    const int m0 = d0 >> 2;
-    const uint32_t c01 = *reinterpret_cast<const uint16_t*>(codes + m0);
+// True when the runtime block layout equals preset LP's compile-time one.
+template <int LP>
+__host__ inline bool preset_layout_matches(const BlockLayout& b) {
+  using P = Preset<LP>;
+  const int want[5] = {P::OPQ, P::ORVQ, P::OACT, P::OSPI, P::OSPV};
+  const int bpt[5] = {P::M, P::L, P::L, P::S, 2 * P::S};
+  for (int k = 0; k < 5; ++k) {
+    if (b.bpt[k] != bpt[k]) return false;
+    if (bpt[k] && (b.off[k] != want[k] || b.off[5 + k] != P::FB + want[k])) return false;
+  }
+  return b.block_bytes == P::BLOCK;
+}
+
+struct ChunkCtx {
+  const uint16_t* pq_cm;   // code-major PQ codebook [K][M][ds] (shared)
+  const uint16_t* pq_sel;  // this lane's copy: pq_cm, or the pair-swapped copy for odd slots (4-dim presets)
+  const uint16_t* rvq_s;   // RVQ codebook [L][Kr][D] (shared, when staged)
+  const uint16_t* rvq_g;   // RVQ codebook (global)
+  uint16_t* scratch;       // this warp's sparse scatter rows [2 buffers][2 tokens][4 slots][D] fp16
+  BlockLayout lay;         // runtime block layout (generic path)
+  int M, K, ds, L, Kr, S, rvq_u16, rvq_smem, has_mask;
+  int qp_lim;              // score lane's row: last visible position (causal), huge (not causal), very negative (unused row)
+  float sl2;               // softmax scale * log2(e)
+};
+
+// Fast path: this lane's 8 dims of token tb of a block, K (kv = 0) or V (kv = 1) fields.
+template <int LP>
+__device__ __forceinline__ void recon_fast(const ChunkCtx& c, const unsigned char* blk, int kv, int tb, int j,
+                                           bool odd, uint32_t* w) {
+  using P = Preset<LP>;
+  const unsigned char* f = blk + kv * P::FB;
+  if constexpr (P::DS == 4) {
+    const int m0 = 2 * j;
+    const uint32_t c01 = *reinterpret_cast<const uint16_t*>(f + P::OPQ + tb * P::M + m0);
     const uint32_t c0 = c01 & 0xffu, c1 = c01 >> 8;
-    // odd slots read subspace m0+1 first: the two tokens of a half-warp hit
-    // complementary bank halves
-    const uint32_t ma = odd ? m0 + 1 : m0, ca = odd ? c1 : c0;
-    const uint32_t mb = odd ? m0 : m0 + 1, cb = odd ? c0 : c1;
-    const uint2 a = *reinterpret_cast<const uint2*>(cm + ((ca * M + ma) << 2));
-    const uint2 b = *reinterpret_cast<const uint2*>(cm + ((cb * M + mb) << 2));
-    o[0] = odd ? b.x : a.x;
-    o[1] = odd ? b.y : a.y;
-    o[2] = odd ? a.x : b.x;
-    o[3] = odd ? a.y : b.y;
-  } else {  // DS == 8
-    const int m = d0 >> 3;
-    const uint4 a = *reinterpret_cast<const uint4*>(cm + (((uint32_t)codes[m] * M + m) << 3));
-    o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
-  }
-}
-
-// generic code-major PQ gather (any ds)
-__device__ __forceinline__ void pq8_cm_generic(const uint16_t* cm, int M, int ds, const unsigned char* codes, int d0,
-                                               uint32_t* o) {
-  if (ds >= 8) {
-    const int m = d0 / ds, off = d0 - m * ds;
-    const uint4 a = *reinterpret_cast<const uint4*>(cm + ((uint32_t)codes[m] * M + m) * ds + off);
-    o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
-  } else if (ds == 4) {
-    const int m = d0 >> 2;
-    const uint2 a = *reinterpret_cast<const uint2*>(cm + (((uint32_t)codes[m] * M + m) << 2));
-    const uint2 b = *reinterpret_cast<const uint2*>(cm + (((uint32_t)codes[m + 1] * M + m + 1) << 2));
-    o[0] = a.x; o[1] = a.y; o[2] = b.x; o[3] = b.y;
-  } else if (ds == 2) {
-    const int m = d0 >> 1;
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      o[i] = *reinterpret_cast<const uint32_t*>(cm + (((uint32_t)codes[m + i] * M + m + i) << 1));
+    // odd slots: the swapped copy holds subspace m0 at position m0+1 and vice versa
+    const int pa = odd ? 1 : 0;
+    const uint2 a = *reinterpret_cast<const uint2*>(c.pq_sel + ((c0 * P::M + m0 + pa) << 2));
+    const uint2 b = *reinterpret_cast<const uint2*>(c.pq_sel + ((c1 * P::M + m0 + 1 - pa) << 2));
+    w[0] = a.x; w[1] = a.y; w[2] = b.x; w[3] = b.y;
   } else {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t lo = cm[(uint32_t)codes[d0 + 2 * i] * M + d0 + 2 * i];
-      const uint32_t hi = cm[(uint32_t)codes[d0 + 2 * i + 1] * M + d0 + 2 * i + 1];
-      o[i] = lo | (hi << 16);
+    const uint32_t cc = f[P::OPQ + tb * P::M + j];
+    const uint4 a = *reinterpret_cast<const uint4*>(c.pq_cm + ((cc * P::M + j) << 3));
+    w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+  }
+  if constexpr (P::L == 1) {
+    const uint32_t code = f[P::ORVQ + tb];
+    if constexpr (P::MASK) {
+      const bool act = f[P::OACT + tb] != 0;
+      const uint4 r = *reinterpret_cast<const uint4*>(c.rvq_s + (act ? code : 0u) * 64 + 8 * j);
+      w[0] = hadd2_u32(w[0], act ? r.x : 0u); w[1] = hadd2_u32(w[1], act ? r.y : 0u);
+      w[2] = hadd2_u32(w[2], act ? r.z : 0u); w[3] = hadd2_u32(w[3], act ? r.w : 0u);
+    } else {
+      const uint4 r = *reinterpret_cast<const uint4*>(c.rvq_s + code * 64 + 8 * j);
+      w[0] = hadd2_u32(w[0], r.x); w[1] = hadd2_u32(w[1], r.y);
+      w[2] = hadd2_u32(w[2], r.z); w[3] = hadd2_u32(w[3], r.w);
     }
   }
 }
 
-// Start of field k (0 pq, 1 rvq, 2 active, 3 sp_idx, 4 sp_val) of token t of a tile.
-__device__ __forceinline__ const unsigned char* tok_field(const ChunkShared& cs, const TileView& tv, int t, int k) {
-  const int ti = tv.t0 + t;
-  return tv.base + (ti >> 4) * cs.lay.block_bytes + cs.lay.off[tv.kvo + k] + (ti & 15) * cs.lay.bpt[k];
-}
-
-// Reconstruct one lane's dims of token t (tile-local, already clamped to a valid token).
-template <int D, int DS, int MODE>
-__device__ __forceinline__ void recon_token(const ChunkShared& cs, const TileView& tv, int t, int dim0, bool odd,
-                                            uint32_t* w) {
+// Generic path: runtime layout.  Codes are clamped to the codebook sizes so a
+// store holding stray bytes (tokens outside the window) never indexes past them.
+template <int D>
+__device__ __forceinline__ void recon_generic(const ChunkCtx& c, const unsigned char* blk, int kv, int tb, int dim0,
+                                              uint32_t* w) {
   constexpr int DPL = D / 8;
-  if constexpr (MODE == kDense) {
-    load_dense<DPL>(tv.dense + (size_t)t * D + dim0, w);
-  } else if constexpr (MODE == kRvq1 || MODE == kPqOnly) {
-    const unsigned char* codes = tok_field(cs, tv, t, 0);
+  const unsigned char* codes = blk + c.lay.off[kv * 5 + 0] + tb * c.lay.bpt[0];
+  const uint32_t kmax = (uint32_t)c.K - 1u;
 #pragma unroll
-    for (int g8 = 0; g8 < DPL / 8; ++g8) pq8_cm<DS>(cs.pq_cm, cs.M, codes, dim0 + 8 * g8, odd, w + 4 * g8);
-    if constexpr (MODE == kRvq1) {
-      const bool act = !cs.has_mask || *tok_field(cs, tv, t, 2) != 0;
-      const uint32_t c = act ? *tok_field(cs, tv, t, 1) : 0u;
+  for (int g8 = 0; g8 < DPL / 8; ++g8) {
+    const int d0 = dim0 + 8 * g8;
+    uint32_t* o = w + 4 * g8;
+    if (c.ds >= 8) {
+      const int m = d0 / c.ds, off = d0 - m * c.ds;
+      const uint32_t cc = min((uint32_t)codes[m], kmax);
+      const uint4 a = *reinterpret_cast<const uint4*>(c.pq_cm + (cc * c.M + m) * c.ds + off);
+      o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
+    } else if (c.ds == 4) {
+      const int m = d0 >> 2;
+      const uint32_t ca = min((uint32_t)codes[m], kmax), cb = min((uint32_t)codes[m + 1], kmax);
+      const uint2 a = *reinterpret_cast<const uint2*>(c.pq_cm + ((ca * c.M + m) << 2));
+      const uint2 b = *reinterpret_cast<const uint2*>(c.pq_cm + ((cb * c.M + m + 1) << 2));
+      o[0] = a.x; o[1] = a.y; o[2] = b.x; o[3] = b.y;
+    } else if (c.ds == 2) {
+      const int m = d0 >> 1;
 #pragma unroll
-      for (int g8 = 0; g8 < DPL / 8; ++g8) {
-        const uint4 r = *reinterpret_cast<const uint4*>(cs.rvq_s + c * D + dim0 + 8 * g8);
-        w[4 * g8 + 0] = hadd2_u32(w[4 * g8 + 0], act ? r.x : 0u);
-        w[4 * g8 + 1] = hadd2_u32(w[4 * g8 + 1], act ? r.y : 0u);
-        w[4 * g8 + 2] = hadd2_u32(w[4 * g8 + 2], act ? r.z : 0u);
-        w[4 * g8 + 3] = hadd2_u32(w[4 * g8 + 3], act ? r.w : 0u);
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t cc = min((uint32_t)codes[m + i], kmax);
+        o[i] = *reinterpret_cast<const uint32_t*>(c.pq_cm + ((cc * c.M + m + i) << 1));
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t ca = min((uint32_t)codes[d0 + 2 * i], kmax), cb = min((uint32_t)codes[d0 + 2 * i + 1], kmax);
+        const uint32_t lo = c.pq_cm[ca * c.M + d0 + 2 * i];
+        const uint32_t hi = c.pq_cm[cb * c.M + d0 + 2 * i + 1];
+        o[i] = lo | (hi << 16);
       }
     }
-  } else {
-    const unsigned char* codes = tok_field(cs, tv, t, 0);
+  }
+  const bool act = c.L > 0 && (!c.has_mask || blk[c.lay.off[kv * 5 + 2] + tb] != 0);
+  if (act) {
+    const unsigned char* rc = blk + c.lay.off[kv * 5 + 1] + tb * c.lay.bpt[1];
+    const uint16_t* cb = c.rvq_smem ? c.rvq_s : c.rvq_g;
 #pragma unroll
-    for (int g8 = 0; g8 < DPL / 8; ++g8) pq8_cm_generic(cs.pq_cm, cs.M, cs.ds, codes, dim0 + 8 * g8, w + 4 * g8);
-    const bool act = cs.L > 0 && (!cs.has_mask || *tok_field(cs, tv, t, 2) != 0);
-    if (act) {
-      const unsigned char* rc = tok_field(cs, tv, t, 1);
-      if (cs.rvq_smem) {
+    for (int g8 = 0; g8 < DPL / 8; ++g8) rvq_add8<D>(cb, c.L, c.Kr, c.rvq_u16, rc, dim0 + 8 * g8, w + 4 * g8);
+  }
+}
+
+// Sparse residual of two tokens (row-steps 2hs, 2hs+1): scatter, then add this lane's dims.
+template <int D, int LP>
+__device__ __forceinline__ void sparse_apply2(const ChunkCtx& c, const unsigned char* blk, int kv, const int* tb,
+                                              const bool* valid, int round, int slot, int j, int dim0,
+                                              uint32_t (*w)[D / 16]) {
+  constexpr int DPL = D / 8;
+  uint16_t* buf = c.scratch + (round & 1) * (2 * 4 * D);
 #pragma unroll
-        for (int g8 = 0; g8 < DPL / 8; ++g8) rvq_add8<D>(cs.rvq_s, cs.L, cs.Kr, cs.rvq_u16, rc, dim0 + 8 * g8, w + 4 * g8);
-      } else {
+  for (int u = 0; u < 2; ++u) {
+    uint16_t* row = buf + (u * 4 + slot) * D;
+    if constexpr (LP != kGeneric) {
+      using P = Preset<LP>;
+      const unsigned char* f = blk + kv * P::FB;
+      const int idx = f[P::OSPI + tb[u] * P::S + j] & (D - 1);
+      const uint16_t val = *reinterpret_cast<const uint16_t*>(f + P::OSPV + (tb[u] * P::S + j) * 2);
+      row[idx] = valid[u] ? val : (uint16_t)0;
+    } else {
+      const unsigned char* spi = blk + c.lay.off[kv * 5 + 3] + tb[u] * c.S;
+      const uint16_t* spv = reinterpret_cast<const uint16_t*>(blk + c.lay.off[kv * 5 + 4]) + tb[u] * c.S;
+      for (int e = j; e < c.S; e += 8) row[spi[e] & (D - 1)] = valid[u] ? spv[e] : (uint16_t)0;
+    }
+  }
+  __syncwarp();
 #pragma unroll
-        for (int g8 = 0; g8 < DPL / 8; ++g8) rvq_add8<D>(cs.rvq_g, cs.L, cs.Kr, cs.rvq_u16, rc, dim0 + 8 * g8, w + 4 * g8);
-      }
+  for (int u = 0; u < 2; ++u) {
+    uint16_t* src = buf + (u * 4 + slot) * D + dim0;
+#pragma unroll
+    for (int g8 = 0; g8 < DPL / 8; ++g8) {
+      uint4* p4 = reinterpret_cast<uint4*>(src + 8 * g8);
+      const uint4 d = *p4;
+      w[u][4 * g8 + 0] = hadd2_u32(w[u][4 * g8 + 0], d.x);
+      w[u][4 * g8 + 1] = hadd2_u32(w[u][4 * g8 + 1], d.y);
+      w[u][4 * g8 + 2] = hadd2_u32(w[u][4 * g8 + 2], d.z);
+      w[u][4 * g8 + 3] = hadd2_u32(w[u][4 * g8 + 3], d.w);
+      *p4 = make_uint4(0u, 0u, 0u, 0u);
     }
   }
 }
 
-// Sparse residual terms handled by this lane for token t: returns sum_e q_r[idx_e] * val_e
-// (K side) over entries e = j, j+8, ... < S.
-template <int RMAX, int MODE>
-__device__ __forceinline__ void sparse_k(const ChunkShared& cs, const TileView& tv, int t, int j, float* corr) {
+// Rebuild this lane's dims of the two tokens tb[0], tb[1] (K or V fields).
+template <int D, int LP, bool DENSE>
+__device__ __forceinline__ void load_pair(const ChunkCtx& c, const unsigned char* blk, const uint16_t* dense,
+                                          int kv, const int* tb, const bool* valid, int t_lo, int round, int slot,
+                                          int j, int dim0, bool odd, uint32_t (*w)[D / 16]) {
+  constexpr int DPL = D / 8;
 #pragma unroll
-  for (int r = 0; r < RMAX; ++r) corr[r] = 0.f;
-  const unsigned char* spi = tok_field(cs, tv, t, 3);
-  const uint16_t* spv = reinterpret_cast<const uint16_t*>(tok_field(cs, tv, t, 4));
-  if constexpr (MODE == kRvq1 || MODE == kPqOnly) {  // S <= 8: at most one entry per lane
-    const bool has = j < cs.S;
-    const int e = has ? j : 0;
-    const int idx = spi[e];
-    const float val = has ? h2f(spv[e]) : 0.f;
-    float qv[RMAX];
-    load_row<RMAX>(cs.qtab + idx * RMAX, qv);
-#pragma unroll
-    for (int r = 0; r < RMAX; ++r) corr[r] = qv[r] * val;
-  } else {
-    for (int e = j; e < cs.S; e += 8) {
-      const int idx = spi[e];
-      const float val = h2f(spv[e]);
-      float qv[RMAX];
-      load_row<RMAX>(cs.qtab + idx * RMAX, qv);
-#pragma unroll
-      for (int r = 0; r < RMAX; ++r) corr[r] = __fmaf_rn(qv[r], val, corr[r]);
+  for (int u = 0; u < 2; ++u) {
+    if constexpr (DENSE) {
+      load_dense<DPL>(dense + (valid[u] ? tb[u] : t_lo) * D + dim0, w[u]);
+    } else if constexpr (LP != kGeneric) {
+      recon_fast<LP>(c, blk, kv, tb[u], j, odd, w[u]);
+    } else {
+      recon_generic<D>(c, blk, kv, tb[u], dim0, w[u]);
     }
+  }
+  if constexpr (!DENSE) {
+    if (c.S > 0) sparse_apply2<D, LP>(c, blk, kv, tb, valid, round, slot, j, dim0, w);
   }
 }
 
-// V side: add p_r * val_e into this slot's sparse-V sums for entries of token t.
-template <int RMAX, int MODE>
-__device__ __forceinline__ void sparse_v(const ChunkShared& cs, const TileView& tv, int t, int j, int slot,
-                                         int D, const float* pv) {
-  const unsigned char* spi = tok_field(cs, tv, t, 3);
-  const uint16_t* spv = reinterpret_cast<const uint16_t*>(tok_field(cs, tv, t, 4));
-  if constexpr (MODE == kRvq1 || MODE == kPqOnly) {
-    const bool has = j < cs.S;
-    const int e = has ? j : 0;
-    const int idx = spi[e];
-    const float val = has ? h2f(spv[e]) : 0.f;
-    float* dst = cs.vsp + ((size_t)slot * D + idx) * RMAX;
-    float cur[RMAX];
-    load_row<RMAX>(dst, cur);
-#pragma unroll
-    for (int r = 0; r < RMAX; ++r) cur[r] = __fmaf_rn(pv[r], val, cur[r]);
-    store_row<RMAX>(dst, cur);
-  } else {
-    for (int e = j; e < cs.S; e += 8) {
-      const int idx = spi[e];
-      const float val = h2f(spv[e]);
-      float* dst = cs.vsp + ((size_t)slot * D + idx) * RMAX;
-      float cur[RMAX];
-      load_row<RMAX>(dst, cur);
-#pragma unroll
-      for (int r = 0; r < RMAX; ++r) cur[r] = __fmaf_rn(pv[r], val, cur[r]);
-      store_row<RMAX>(dst, cur);
-    }
-  }
-}
-
-// One 16-token chunk: scores on tensor cores, online softmax, V accumulation.
-template <int D, int RMAX, int DS, int MODE>
-__device__ __forceinline__ void process_chunk(const ChunkShared& cs, const TileView& tk, const TileView& tvv,
-                                              int cbase, const uint32_t (*aq)[4], const uint32_t (*asp)[4],
-                                              float (*acc)[D / 8], float& m_run, float& l_run) {
+// One 16-token chunk: K scores on tensor cores, online softmax, V accumulation.
+// blk: the block's bytes (code tiles); dense_k/dense_v: the chunk's 16 hot rows
+// (dense tiles).  Valid tokens are [t_lo, t_hi); token tb is at position pos_base + tb.
+template <int D, int RMAX, int LP, bool DENSE>
+__device__ __forceinline__ void process_block(const ChunkCtx& c, const unsigned char* blk, const uint16_t* dense_k,
+                                              const uint16_t* dense_v, int t_lo, int t_hi, int pos_base,
+                                              const uint32_t (*aq)[4], float (*acc)[D / 8], float& m_run,
+                                              float& l_run) {
   constexpr int DPL = D / 8;
   constexpr int NMMA = DPL / 4;
-  constexpr int NSP = (RMAX + 3) / 4;
   const float NEG_INF = __int_as_float(0xff800000);
   const int lane = threadIdx.x & 31;
   const int slot = lane >> 3, j = lane & 7, dim0 = j * DPL;
-  const int srow = lane >> 2, sslot = lane & 3;
+  const int sslot = lane & 3;
   const bool odd = slot & 1;
-  const bool sparse = MODE != kDense && cs.S > 0;
+  // score lane (row srow, token slot sslot): visible tokens are [t_lo, s_hi)
+  const int s_hi = min(t_hi, c.qp_lim - pos_base + 1);
 
   // ---------------- scores ----------------
   float sc[4];
 #pragma unroll
   for (int hs = 0; hs < 2; ++hs) {
-    int tc[2];
+    int tb[2];
+    bool valid[2];
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
-      const int tl = cbase + 4 * (2 * hs + u) + slot;
-      tc[u] = tl < cs.n ? tl : 0;
+      tb[u] = 4 * (2 * hs + u) + slot;
+      valid[u] = tb[u] >= t_lo && tb[u] < t_hi;
     }
     uint32_t w[2][DPL / 2];
-#pragma unroll
-    for (int u = 0; u < 2; ++u) recon_token<D, DS, MODE>(cs, tk, tc[u], dim0, odd, w[u]);
+    load_pair<D, LP, DENSE>(c, blk, dense_k, 0, tb, valid, t_lo, hs, slot, j, dim0, odd, w);
     float cfr[2][4];
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
@@ -236,29 +265,10 @@ __device__ __forceinline__ void process_chunk(const ChunkShared& cs, const TileV
 #pragma unroll
       for (int s = 0; s < NMMA; ++s) mma16816(cfr[u], aq[s], w[u][2 * s], w[u][2 * s + 1]);
     }
-    if (sparse) {
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        float corr[RMAX];
-        sparse_k<RMAX, MODE>(cs, tk, tc[u], j, corr);
-#pragma unroll
-        for (int t = 0; t < NSP; ++t) {
-          float c4[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) c4[i] = (4 * t + i < RMAX) ? corr[4 * t + i] : 0.f;
-          uint32_t hi01, hi23, lo01, lo23;
-          split_h2(c4[0], c4[1], hi01, lo01);
-          split_h2(c4[2], c4[3], hi23, lo23);
-          mma16816(cfr[u], asp[t], hi01, hi23);
-          mma16816(cfr[u], asp[t], lo01, lo23);
-        }
-      }
-    }
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
-      const int stl = cbase + 4 * (2 * hs + u) + sslot;
-      const bool allowed = stl < cs.n && srow < cs.R && (!cs.causal || cs.pos0 + stl <= cs.qp_lane);
-      sc[2 * hs + u] = allowed ? (cfr[u][0] + cfr[u][3]) * cs.sl2 : NEG_INF;
+      const int stb = 4 * (2 * hs + u) + sslot;
+      sc[2 * hs + u] = (stb >= t_lo && stb < s_hi) ? (cfr[u][0] + cfr[u][3]) * c.sl2 : NEG_INF;
     }
   }
 
@@ -281,36 +291,29 @@ __device__ __forceinline__ void process_chunk(const ChunkShared& cs, const TileV
   l_run = l_run * alpha + lsum;
   m_run = m_new;
   if (__any_sync(0xffffffffu, alpha != 1.f)) {  // a row's max grew: rescale its sums
-    float arow[RMAX];
 #pragma unroll
-    for (int r = 0; r < RMAX; ++r) arow[r] = __shfl_sync(0xffffffffu, alpha, 4 * r);
+    for (int r = 0; r < RMAX; ++r) {
+      const float ar = __shfl_sync(0xffffffffu, alpha, 4 * r);
 #pragma unroll
-    for (int r = 0; r < RMAX; ++r)
-#pragma unroll
-      for (int i = 0; i < DPL; ++i) acc[r][i] *= arow[r];
-    if (cs.S > 0) {
-#pragma unroll
-      for (int r = 0; r < RMAX; ++r)
-        for (int k = lane; k < 4 * D; k += 32) cs.vsp[k * RMAX + r] *= arow[r];
+      for (int i = 0; i < DPL; ++i) acc[r][i] *= ar;
     }
-    __syncwarp();
   }
 
   // ---------------- values ----------------
 #pragma unroll
   for (int hs = 0; hs < 2; ++hs) {
-    int tc[2];
+    int tb[2];
+    bool valid[2];
     float pv[2][RMAX];
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
-      const int tl = cbase + 4 * (2 * hs + u) + slot;
-      tc[u] = tl < cs.n ? tl : 0;
+      tb[u] = 4 * (2 * hs + u) + slot;
+      valid[u] = tb[u] >= t_lo && tb[u] < t_hi;
 #pragma unroll
       for (int r = 0; r < RMAX; ++r) pv[u][r] = __shfl_sync(0xffffffffu, pr[2 * hs + u], 4 * r + slot);
     }
     uint32_t w[2][DPL / 2];
-#pragma unroll
-    for (int u = 0; u < 2; ++u) recon_token<D, DS, MODE>(cs, tvv, tc[u], dim0, odd, w[u]);
+    load_pair<D, LP, DENSE>(c, blk, dense_v, 1, tb, valid, t_lo, hs, slot, j, dim0, odd, w);
 #pragma unroll
     for (int u = 0; u < 2; ++u)
 #pragma unroll
@@ -319,10 +322,6 @@ __device__ __forceinline__ void process_chunk(const ChunkShared& cs, const TileV
 #pragma unroll
         for (int r = 0; r < RMAX; ++r) ffma2(acc[r][2 * i], acc[r][2 * i + 1], pv[u][r], v2.x, v2.y);
       }
-    if (sparse) {
-#pragma unroll
-      for (int u = 0; u < 2; ++u) sparse_v<RMAX, MODE>(cs, tvv, tc[u], j, slot, D, pv[u]);
-    }
   }
 }
 

@@ -191,8 +191,8 @@ def time_cpu_step(s) -> float:
     c = CFG
     D, T = c["head_dim"], c["context"]
     t0 = time.perf_counter()
-    kw = np.concatenate([s["oq"].decode_f32(s["kc"]), s["hot_k"].astype(np.float32)], 0)
-    vw = np.concatenate([s["oq"].decode_f32(s["vc"]), s["hot_v"].astype(np.float32)], 0)
+    kw = np.concatenate([s["oq"].decode(s["kc"]), s["hot_k"]], 0)
+    vw = np.concatenate([s["oq"].decode(s["vc"]), s["hot_v"]], 0)
     R.blockwise_exact_attention(s["q"], kw, vw, D ** -0.5, 128, True, np.full((1, s["q"].shape[1]), T - 1))
     dt = time.perf_counter() - t0
     return dt * (c["batch"] * c["kv_heads"]) / s["rows"]

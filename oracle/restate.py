@@ -541,13 +541,12 @@ class OracleCache:
 
     # -- materialize ------------------------------------------------------------
     def materialize_window(self, query_positions=None, context_window=None, current_position=None,
-                           cold_hits: Optional[set] = None, used_router: bool = False, exact_f32: bool = False):
+                           cold_hits: Optional[set] = None, used_router: bool = False):
         """cache.py:344-393 — dense fp16 window [B, W, H, D] in position order + stats.
 
-        ``exact_f32=True`` returns the fp32 reconstruction instead (identical to
-        the fp16 window when sparse_topk == 0); attention uses it so that the
-        sparse residual (an extension) is added in fp32 and never rounded."""
-        dec = self.q.decode_f32 if exact_f32 else self.q.decode
+        Sparse residuals (an extension) are added in fp32 and the sum is rounded
+        to fp16 once, so attention sees exactly the materialised values."""
+        dec = self.q.decode
         start, end, adjusted = window_bounds(self.total_tokens, query_positions, context_window, current_position)
         stats = _empty_stats()
         stats["window_start"], stats["window_end"] = start, end
@@ -564,8 +563,8 @@ class OracleCache:
             a, b = ov[0] - s, ov[1] - s
             if kind == "hot":  # cache.py:250-261
                 stats["hot_tokens_materialized"] += b - a
-                pieces_k.append((ov[0], self.hot_k[:, a:b].astype(F32) if exact_f32 else self.hot_k[:, a:b]))
-                pieces_v.append((ov[0], self.hot_v[:, a:b].astype(F32) if exact_f32 else self.hot_v[:, a:b]))
+                pieces_k.append((ov[0], self.hot_k[:, a:b]))
+                pieces_v.append((ov[0], self.hot_v[:, a:b]))
             else:  # cache.py:263-291 — decoded in block_size_seq chunks from the overlap start
                 for cs in range(a, b, bs):
                     ce = min(cs + bs, b)
@@ -592,7 +591,7 @@ class OracleCache:
             stats["cold_chunks_touched"] += 1
         self.last_access_stats = dict(stats)
         if not pieces_k:
-            empty = np.zeros((self.batch, 0, self.h, self.d), F32 if exact_f32 else F16)
+            empty = np.zeros((self.batch, 0, self.h, self.d), F16)
             return empty, empty, adjusted
         if self.cfg.hot_policy == "prefix":
             # reference concatenation order: hot, warm chunks, cold chunks (cache.py:378-391)
@@ -607,8 +606,7 @@ class OracleCache:
     def attention_forward(self, q: np.ndarray, causal=True, query_positions=None, context_window=None,
                           current_position=None) -> np.ndarray:
         """cache.py:395-428 — q [B, Q, Hq, D] (one query set per sequence)."""
-        keys, vals, adjusted = self.materialize_window(query_positions, context_window, current_position,
-                                                       exact_f32=True)
+        keys, vals, adjusted = self.materialize_window(query_positions, context_window, current_position)
         self.last_access_stats["query_tokens"] = int(q.shape[1])
         if keys.shape[1] == 0:
             return np.zeros_like(q)
