@@ -76,6 +76,7 @@ SIGNATURES = {
     "rfsn_attention_workspace_size": (C.c_int, [C.POINTER(AttnArgs), C.POINTER(Quantizer),
                                                 C.POINTER(C.c_size_t)]),
     "rfsn_decode_attention": (C.c_int, [C.POINTER(AttnArgs), C.POINTER(Quantizer), C.c_void_p]),
+    "rfsn_decode_attention_noalloc": (C.c_int, [C.POINTER(AttnArgs), C.POINTER(Quantizer), C.c_void_p]),
     "rfsn_cold_prefetch": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p]),
     "rfsn_cold_evict": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
 }

@@ -30,6 +30,8 @@
 #include <cuda_runtime.h>
 #include <math.h>
 
+#include <mutex>
+
 #include "rfsn_api_internal.h"
 #include "rfsn_attn_chunk.cuh"
 #include "rfsn_attn_util.cuh"
@@ -740,6 +742,82 @@ extern "C" int rfsn_decode_attention(const rfsn_attn_args* args, const rfsn_quan
   if (!args->workspace || args->workspace_bytes < pl.ws_bytes) return RFSN_ERR_WORKSPACE_TOO_SMALL;
   if (reinterpret_cast<uintptr_t>(args->workspace) & 15) return RFSN_ERR_ALIGNMENT;
   pl.p.ws_ml = reinterpret_cast<float*>(args->workspace);
+  pl.p.ws_o = pl.p.ws_ml + align_up((int64_t)p.rows * p.max_pieces * p.R * 2, 64);
+  st = check_cuda(launch(pl, s));
+  if (st != RFSN_OK) return st;
+  MergeParams mp;
+  mp.ws_o = pl.p.ws_o; mp.ws_ml = pl.p.ws_ml; mp.out = args->out;
+  mp.B = p.B; mp.Q = p.Q; mp.Hq = p.Hq; mp.Hkv = p.Hkv; mp.D = p.D; mp.G = p.G; mp.R = p.R;
+  mp.max_pieces = p.max_pieces; mp.W = p.W; mp.per_cta = p.per_cta;
+  rfsn_merge_kernel<<<(int)p.rows, 256, 0, s>>>(mp);
+  return check_cuda(cudaGetLastError());
+}
+
+// ---------------------------------------------------------------------------
+// rfsn_decode_attention_noalloc: the same attention with partials kept in a
+// fixed module-scope buffer instead of a caller-provided workspace.
+//
+// Some callers cannot allocate device memory at the moment they run decode
+// attention: a host-language binding that holds only q/out/store pointers and
+// has no device allocator of its own, or an embedding runtime whose memory is
+// reserved up front and may not grow per call.  For them the split-K partials
+// (max, sum and unnormalised output of every row piece) live in a static
+// __device__ array of kNoAllocScratchBytes per device.  Its address is looked
+// up once per device, on the first call made with that device current, and
+// cached; that first call may load the module, so make it before capturing
+// the stream into a graph.  Nothing here calls an allocator.  Every partial
+// the merge kernel reads is written by the attention kernel of the same call,
+// so the buffer needs no clearing.  Calls that overlap in time on one device
+// (different streams, or threads without ordering) share the buffer and race;
+// calls on one stream are ordered and safe.
+// ---------------------------------------------------------------------------
+namespace rfsn {
+
+constexpr size_t kNoAllocScratchBytes = RFSN_NOALLOC_SCRATCH_BYTES;  // 4 MiB per device
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_ptr[kNoAllocMaxDevices];
+
+// Device address of this device's scratch (looked up on first use).
+static int noalloc_scratch(void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return check_cuda(e);
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return RFSN_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* addr = nullptr;
+    e = cudaGetSymbolAddress(&addr, g_noalloc_scratch);
+    if (e != cudaSuccess) return check_cuda(e);
+    if (!addr) return RFSN_ERR_CUDA;
+    g_noalloc_ptr[dev] = addr;
+  }
+  *out = g_noalloc_ptr[dev];
+  return RFSN_OK;
+}
+
+}  // namespace rfsn
+
+extern "C" int rfsn_decode_attention_noalloc(const rfsn_attn_args* args, const rfsn_quantizer* qz, void* stream) {
+  Plan pl;
+  int st = make_plan(args, qz, pl);
+  if (st != RFSN_OK) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const AttnParams& p = pl.p;
+  const int64_t nout = (int64_t)p.B * p.Q * p.Hq * p.D;
+  if (p.W == 0) {
+    rfsn_zero_kernel<<<(int)((nout + 255) / 256 < 1024 ? (nout + 255) / 256 : 1024), 256, 0, s>>>(args->out, nout);
+    return check_cuda(cudaGetLastError());
+  }
+  // partials of all row pieces must fit the fixed buffer
+  if (pl.ws_bytes > kNoAllocScratchBytes) return RFSN_ERR_WORKSPACE_TOO_SMALL;
+  void* scratch = nullptr;
+  st = noalloc_scratch(&scratch);
+  if (st != RFSN_OK) return st;
+  pl.p.ws_ml = reinterpret_cast<float*>(scratch);
   pl.p.ws_o = pl.p.ws_ml + align_up((int64_t)p.rows * p.max_pieces * p.R * 2, 64);
   st = check_cuda(launch(pl, s));
   if (st != RFSN_OK) return st;

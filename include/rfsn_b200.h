@@ -174,6 +174,20 @@ int rfsn_attention_workspace_size(const rfsn_attn_args* args, const rfsn_quantiz
 
 int rfsn_decode_attention(const rfsn_attn_args* args, const rfsn_quantizer* qz, void* stream);
 
+/* Allocation-free decode attention.  No counterpart in the reference: it is an
+ * addition for callers that cannot allocate device memory when they run
+ * attention (a host binding that holds only q/out/store pointers, a runtime
+ * whose memory is fixed up front).  Same arguments and results as
+ * rfsn_decode_attention, except that args->workspace / workspace_bytes are
+ * ignored: partials go to a fixed 4 MiB buffer per device inside the library
+ * (RFSN_NOALLOC_SCRATCH_BYTES).  Returns RFSN_ERR_WORKSPACE_TOO_SMALL when the
+ * call needs more than that (rfsn_attention_workspace_size reports the need).
+ * The first call on each device looks the buffer up and may load the module:
+ * make it before capturing the stream.  Calls that overlap in time on one
+ * device share the buffer and race; calls ordered on one stream are safe. */
+#define RFSN_NOALLOC_SCRATCH_BYTES (4u << 20)
+int rfsn_decode_attention_noalloc(const rfsn_attn_args* args, const rfsn_quantizer* qz, void* stream);
+
 /* Cold tier transfer — replaces load_compressed_chunk / np.load in the router's
  * executor (storage.py:138-140, 226-234): one cudaMemcpyAsync of `bytes` from
  * pinned host memory to device memory on `stream` (the router's side stream),
