@@ -123,7 +123,8 @@ class RFSNHybridAttentionMLX:
         dev = qz.pq_codebooks.device
         if T == 0:
             return torch.zeros((nq, hq, d), dtype=q.dtype, device=dev)
-        ks, vs = key_store.to_store(qz), value_store.to_store(qz)
+        st = key_store.to_store(qz, kv=0)
+        value_store.to_store(qz, kv=1, store=st)
         qb = q.to(device=dev, dtype=torch.float16).reshape(1, nq, hq, d).contiguous()
         out = torch.empty_like(qb)
         qpos = None
@@ -131,7 +132,7 @@ class RFSNHybridAttentionMLX:
             qpos = torch.clamp(_normalize_query_positions(query_positions, nq, hq, T - 1), min=-1)
             qpos = qpos.reshape(1, nq, hq).to(dev)
         K.decode_attention(qz, qb, out, [(K.STORE_WARM, 0, 0, T, 0)], kv_heads=H, qpos=qpos, causal=causal,
-                           scale=self.scale, warm=(ks, vs))
+                           scale=self.scale, warm=st)
         return out[0].to(q.dtype)
 
 

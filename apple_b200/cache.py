@@ -79,14 +79,11 @@ class RFSNv10KVCacheMLX:
         self._hot_v: Optional[torch.Tensor] = None
         self._hot_start = 0  # global position of the oldest hot token
         self._hot_ring = max(1, self.hot_capacity)
-        self._warm_k: Optional[K.CodeStoreBuffers] = None
-        self._warm_v: Optional[K.CodeStoreBuffers] = None
+        self._warm: Optional[K.CodeStoreBuffers] = None  # K and V codes, rows x cap
         self._warm_start = 0  # global position of the oldest warm token
         self._warm_ring = 0
         self._cold: Optional[ColdTier] = None
         self._cold_root: Optional[Path] = None
-        self._stage_k: Optional[K.CodeStoreBuffers] = None
-        self._stage_v: Optional[K.CodeStoreBuffers] = None
         self._qpos_cache: Dict[Tuple, torch.Tensor] = {}
 
     # ------------------------------------------------------------------ stats
@@ -128,32 +125,23 @@ class RFSNv10KVCacheMLX:
 
     @property
     def warm_keys(self):
-        return self._warm_view(self._warm_k)
+        return self._warm_view(0)
 
     @property
     def warm_values(self):
-        return self._warm_view(self._warm_v)
+        return self._warm_view(1)
 
-    def _warm_view(self, st):
+    def _warm_view(self, kv: int):
+        """Warm codes of sequence 0 in position order as a CompressedTensorMLX [T, H, ...]."""
         from .storage import CompressedTensorMLX
-        if st is None or self.num_warm == 0:
+        if self._warm is None or self.num_warm == 0:
             return CompressedTensorMLX.empty(self.config, self.heads)
-        idx = self._warm_index(self._warm_pos0(), self.num_warm)
-        b = 0
-        sl = slice(b * self.heads, (b + 1) * self.heads)
-        pq = st.pq[0, sl][:, idx].transpose(0, 1)
-        L = st.rvq.shape[-1] if st.rvq is not None else 0
-        rvq = st.rvq[0, sl][:, idx].transpose(0, 1) if L else torch.zeros((self.num_warm, self.heads, 0),
-                                                                         dtype=torch.uint8, device=self.device)
-        mask = st.mask[0, sl][:, idx].transpose(0, 1).bool() if L else torch.zeros((self.num_warm, self.heads),
-                                                                                   dtype=torch.bool, device=self.device)
-        S = self.config.sparse_topk
-        spi = st.sp_idx[0, sl][:, idx].transpose(0, 1) if S else torch.zeros((self.num_warm, self.heads, 0),
-                                                                            dtype=torch.uint8, device=self.device)
-        spv = st.sp_val[0, sl][:, idx].transpose(0, 1) if S else torch.zeros((self.num_warm, self.heads, 0),
-                                                                            dtype=torch.float16, device=self.device)
-        return CompressedTensorMLX(pq.contiguous(), rvq.contiguous(), mask.contiguous(), spi.contiguous(),
-                                   spv.contiguous(), self.heads)
+        parts = [CompressedTensorMLX.from_store(self._warm, kv, 0, idx, cnt, self.heads)
+                 for idx, cnt, _ in self._warm_runs(self._warm_pos0(), self.num_warm)]
+        if len(parts) == 1:
+            return parts[0]
+        return CompressedTensorMLX(*(torch.cat([getattr(p, f) for p in parts], 0)
+                                     for f in ("pq_codes", "rvq", "rvq_mask", "sp_idx", "sp_val")), self.heads)
 
     # ------------------------------------------------------------ layout helpers
     def _hot_pos0(self) -> int:
@@ -228,21 +216,18 @@ class RFSNv10KVCacheMLX:
     def _ensure_warm(self, need: int) -> None:
         qz = self._qz
         if self.policy == "recent":
-            if self._warm_k is None:
+            if self._warm is None:
                 self._warm_ring = _ceil_to(max(self.warm_capacity, 1), self.chunk_tokens) + self.chunk_tokens
-                self._warm_k = K.CodeStoreBuffers(qz, self.rows, self._warm_ring, device=self.device)
-                self._warm_v = K.CodeStoreBuffers(qz, self.rows, self._warm_ring, device=self.device)
+                self._warm = K.CodeStoreBuffers(qz, self.rows, self._warm_ring, device=self.device)
             return
-        if self._warm_k is not None and self._warm_k.cap >= need:
+        if self._warm is not None and self._warm.cap >= need:
             return
-        cap = min(K.align16(self.warm_capacity), K.align16(max(need, 64, 2 * (self._warm_k.cap if self._warm_k else 0))))
+        cap = min(K.align16(self.warm_capacity), K.align16(max(need, 64, 2 * (self._warm.cap if self._warm else 0))))
         cap = max(cap, K.align16(need))
-        if self._warm_k is None:
-            self._warm_k = K.CodeStoreBuffers(qz, self.rows, cap, device=self.device)
-            self._warm_v = K.CodeStoreBuffers(qz, self.rows, cap, device=self.device)
+        if self._warm is None:
+            self._warm = K.CodeStoreBuffers(qz, self.rows, cap, device=self.device)
         else:
-            self._warm_k = self._warm_k.grow(qz, cap)
-            self._warm_v = self._warm_v.grow(qz, cap)
+            self._warm = self._warm.grow(qz, cap)
 
     def _ensure_cold(self, disk_dir: Optional[Path]) -> ColdTier:
         root = Path(self.config.disk_cache_dir) if disk_dir is None else Path(disk_dir)
@@ -288,8 +273,10 @@ class RFSNv10KVCacheMLX:
             self._hot_k[:, idx:idx + cnt] = k[:, off:off + cnt].permute(0, 2, 1, 3).reshape(self.rows, cnt, -1)
             self._hot_v[:, idx:idx + cnt] = v[:, off:off + cnt].permute(0, 2, 1, 3).reshape(self.rows, cnt, -1)
 
-    def _encode_into(self, x: torch.Tensor, store: K.CodeStoreBuffers, slot: int, first: int) -> None:
-        K.encode(self._qz, x, store, slot, first)
+    def _encode_kv(self, k: torch.Tensor, v: torch.Tensor, store: K.CodeStoreBuffers, slot: int, first: int) -> None:
+        """Spill encoder: K and V tokens [B, T, H, D] into tokens [first, first+T) of a store."""
+        K.encode(self._qz, k, store, slot, first, kv=0)
+        K.encode(self._qz, v, store, slot, first, kv=1)
 
     def _update_prefix(self, k, v, disk_dir) -> None:
         n = k.shape[1]
@@ -305,18 +292,11 @@ class RFSNv10KVCacheMLX:
         if warm_space > 0 and off < n:
             take = min(warm_space, n - off)
             self._ensure_warm(self.num_warm + take)
-            self._encode_into(k[:, off:off + take], self._warm_k, 0, self.num_warm)
-            self._encode_into(v[:, off:off + take], self._warm_v, 0, self.num_warm)
+            self._encode_kv(k[:, off:off + take], v[:, off:off + take], self._warm, 0, self.num_warm)
             self.num_warm += take
             off += take
         if off < n:
             self._add_to_cold(k[:, off:], v[:, off:], disk_dir)
-
-    def _stage(self) -> Tuple[K.CodeStoreBuffers, K.CodeStoreBuffers]:
-        if self._stage_k is None:
-            self._stage_k = K.CodeStoreBuffers(self._qz, self.rows, self.chunk_tokens, device=self.device)
-            self._stage_v = K.CodeStoreBuffers(self._qz, self.rows, self.chunk_tokens, device=self.device)
-        return self._stage_k, self._stage_v
 
     def _record_chunk_meta(self, chunk_id: int, start: int, n: int) -> None:
         root = self._cold_root
@@ -336,7 +316,6 @@ class RFSNv10KVCacheMLX:
         tier = self._ensure_cold(disk_dir)
         ct = self.chunk_tokens
         start_token = self.num_hot + self.num_warm + self.num_cold
-        sk, sv = self._stage()
         stream = torch.cuda.current_stream()
         n = k.shape[1]
         off = 0
@@ -352,9 +331,10 @@ class RFSNv10KVCacheMLX:
             if chunk is None:
                 chunk = tier.new_chunk(cid, pos)
                 within = 0
-            self._encode_into(k[:, off:off + take], sk, 0, 0)
-            self._encode_into(v[:, off:off + take], sv, 0, 0)
-            tier.write_from_device(chunk, within, sk, sv, 0, 0, take, stream)
+            elif within:
+                tier.load_stage(chunk, stream)  # keep the chunk's earlier tokens in the image
+            self._encode_kv(k[:, off:off + take], v[:, off:off + take], tier.stage, 0, within)
+            tier.store_stage(chunk, stream)
             chunk.end_token += take
             self._record_chunk_meta(cid, pos, take)
             off += take
@@ -371,9 +351,8 @@ class RFSNv10KVCacheMLX:
         warm_end = self._warm_start + self.num_warm
         # oldest hot tokens -> warm (encoded straight from the hot ring)
         for idx, cnt, p in self._hot_runs(self._hot_start, spill_hot):
-            hk = self._hot_k[:, idx:idx + cnt]
-            hv = self._hot_v[:, idx:idx + cnt]
-            self._spill_to_warm(self._as_bthd(hk), self._as_bthd(hv), p)
+            self._spill_to_warm(self._as_bthd(self._hot_k[:, idx:idx + cnt]), self._as_bthd(self._hot_v[:, idx:idx + cnt]),
+                                p)
         self._hot_start += spill_hot
         self.num_hot -= spill_hot
         if spill_new:
@@ -397,8 +376,7 @@ class RFSNv10KVCacheMLX:
     def _spill_to_warm(self, k, v, pos0: int) -> None:
         for idx, cnt, p in self._warm_runs(pos0, k.shape[1]):
             off = p - pos0
-            self._encode_into(k[:, off:off + cnt], self._warm_k, 0, idx)
-            self._encode_into(v[:, off:off + cnt], self._warm_v, 0, idx)
+            self._encode_kv(k[:, off:off + cnt], v[:, off:off + cnt], self._warm, 0, idx)
 
     def _evict_warm_chunks(self, disk_dir) -> None:
         ct = self.chunk_tokens
@@ -411,8 +389,11 @@ class RFSNv10KVCacheMLX:
             pos = self._warm_start + off
             cid = pos // ct
             chunk = tier.new_chunk(cid, pos)
-            idx = pos % self._warm_ring
-            tier.write_from_device(chunk, 0, self._warm_k, self._warm_v, 0, idx, ct, stream)
+            b0 = (pos % self._warm_ring) // K.BLOCK_TOKENS  # chunk-aligned, so whole blocks
+            nb = ct // K.BLOCK_TOKENS
+            with torch.cuda.stream(stream):
+                tier.stage.data[0].copy_(self._warm.data[0, :, b0:b0 + nb])
+            tier.store_stage(chunk, stream)
             chunk.end_token = pos + ct
             self._record_chunk_meta(cid, pos, ct)
         self._warm_start += evict
@@ -524,10 +505,9 @@ class RFSNv10KVCacheMLX:
                 for buf, out in ((self._hot_k, keys), (self._hot_v, values)):
                     out[:, w0:w0 + count] = buf[:, first:first + count].reshape(B, H, count, D).permute(0, 2, 1, 3)
             else:
-                sk, sv = (self._warm_k, self._warm_v) if store == K.STORE_WARM else (self._cold.pool_k,
-                                                                                      self._cold.pool_v)
-                K.decode_codes(self._qz, sk, slot, first, count, keys[:, w0:w0 + count])
-                K.decode_codes(self._qz, sv, slot, first, count, values[:, w0:w0 + count])
+                st = self._warm if store == K.STORE_WARM else self._cold.pool
+                K.decode_codes(self._qz, st, slot, first, count, keys[:, w0:w0 + count], kv=0)
+                K.decode_codes(self._qz, st, slot, first, count, values[:, w0:w0 + count], kv=1)
         self.last_access_stats = dict(stats)
         if B == 1:
             keys, values = keys[0], values[0]
@@ -590,11 +570,10 @@ class RFSNv10KVCacheMLX:
         if out is None:
             out = torch.empty_like(qb)
         qpos = self._qpos(query_positions, start, end, qb) if causal else None
-        cold = (self._cold.pool_k, self._cold.pool_v) if self._cold is not None else None
         K.decode_attention(self._qz, qb, out, segs, kv_heads=self.heads, qpos=qpos, causal=causal,
                            scale=self.head_dim ** -0.5,
                            hot=(self._hot_k, self._hot_v) if self._hot_k is not None else None,
-                           warm=(self._warm_k, self._warm_v) if self._warm_k is not None else None, cold=cold)
+                           warm=self._warm, cold=self._cold.pool if self._cold is not None else None)
         if squeeze:
             return out[0]
         return out.reshape(q.shape) if q.dim() == 3 else out
@@ -605,9 +584,11 @@ class RFSNv10KVCacheMLX:
         hot_bytes = self.num_hot * self.rows * c.head_dim * 2 * 2
         warm_pq_bytes = self.num_warm * self.rows * c.num_subspaces * 2
         active = 0
-        if self._warm_k is not None and self._warm_k.mask is not None and self.num_warm:
-            idx = self._warm_index(self._warm_pos0(), self.num_warm)
-            active = int(self._warm_k.mask[0][:, idx].sum().item() + self._warm_v.mask[0][:, idx].sum().item())
+        if self._warm is not None and self._qz.L and self.num_warm:
+            for kv in (0, 1):
+                for idx, cnt, _ in self._warm_runs(self._warm_pos0(), self.num_warm):
+                    act = self._warm.read_rows(kv, "active", 0, idx, cnt)
+                    active += int(act.sum().item()) if self._qz.threshold >= 0 else act.numel()
         return {"hot_bytes": hot_bytes, "warm_pq_bytes": warm_pq_bytes,
                 "warm_rvq_bytes": active * c.num_rvq_layers * 2,
                 "cold_chunks": len(self.cold_chunk_paths), "cold_tokens": self.num_cold}
@@ -621,11 +602,14 @@ class RFSNv10KVCacheMLX:
             c.ready.synchronize()
         n = c.num_tokens
         out = {"num_tokens": np.array([n], np.int32), "num_heads": np.array([self.heads], np.int32)}
-        for name, st in (("key", c.k), ("value", c.v)):
-            out[f"{name}_pq_codes"] = st.pq[0, :, :n].numpy().copy()
-            if st.rvq is not None:
-                out[f"{name}_rvq"] = st.rvq[0, :, :n].numpy().copy()
-                out[f"{name}_rvq_mask"] = st.mask[0, :, :n].numpy().astype(bool)
+        for kv, name in ((0, "key"), (1, "value")):
+            out[f"{name}_pq_codes"] = c.store.read_rows(kv, "pq", 0, 0, n).numpy().copy()
+            if self._qz.L:
+                out[f"{name}_rvq"] = c.store.read_rows(kv, "rvq", 0, 0, n).numpy().copy()
+                out[f"{name}_rvq_mask"] = c.store.read_rows(kv, "active", 0, 0, n)[..., 0].numpy().astype(bool)
+            if self._qz.sparse_topk:
+                out[f"{name}_sp_idx"] = c.store.read_rows(kv, "sp_idx", 0, 0, n).numpy().copy()
+                out[f"{name}_sp_val"] = c.store.read_rows(kv, "sp_val", 0, 0, n).numpy().copy()
         return out
 
     def close(self) -> None:

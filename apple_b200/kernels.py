@@ -165,6 +165,32 @@ class CodeStoreBuffers:
         t = torch.arange(first, first + values.shape[0], device=v.device)
         v[slot, row, t // BLOCK_TOKENS, t % BLOCK_TOKENS] = values.to(device=v.device, dtype=v.dtype)
 
+    def read_rows(self, kv: int, name: str, slot: int, first: int, count: int,
+                  rows: Optional[int] = None) -> Optional[torch.Tensor]:
+        """Copy of a field for tokens [first, first+count) of rows [0, rows): [rows, count, width]."""
+        v = self.field(kv, name)
+        if v is None:
+            return None
+        t = torch.arange(first, first + count, device=v.device)
+        return v[slot, : (self.rows if rows is None else rows)][:, t // BLOCK_TOKENS, t % BLOCK_TOKENS]
+
+    def write_rows(self, kv: int, name: str, slot: int, first: int, values: torch.Tensor) -> None:
+        """Scatter [rows, count, width] values into tokens [first, first+count) of rows [0, rows)."""
+        v = self.field(kv, name)
+        if v is None:
+            return
+        t = torch.arange(first, first + values.shape[1], device=v.device)
+        v[slot, : values.shape[0]][:, t // BLOCK_TOKENS, t % BLOCK_TOKENS] = values.to(device=v.device,
+                                                                                   dtype=v.dtype)
+
+    def put(self, kv: int, name: str, slot: int, row: int, tokens: torch.Tensor, values: torch.Tensor) -> None:
+        """Scatter [n, width] values into the given token indices of one row."""
+        v = self.field(kv, name)
+        if v is None:
+            return
+        t = tokens.to(device=v.device, dtype=torch.long)
+        v[slot, row, t // BLOCK_TOKENS, t % BLOCK_TOKENS] = values.to(device=v.device, dtype=v.dtype)
+
     def nbytes_per_slot(self) -> int:
         return self.data[0].numel()
 

@@ -59,6 +59,14 @@ def _zero_pq(D: int, device: torch.device) -> torch.Tensor:
     return torch.zeros((D // 8, 1, 8), dtype=torch.float16, device=device)
 
 
+def _code_values(codes: torch.Tensor, qz: K.QuantizerBuffers, dev: torch.device) -> torch.Tensor:
+    """RVQ codes (int32 holding uint16 values) as the store's code dtype, [A, L]."""
+    c = codes.to(device=dev, dtype=torch.int32).reshape(-1, qz.L)
+    if qz.Kr > 256:
+        c = torch.where(c > 32767, c - 65536, c)  # uint16 values stored in int16
+    return c.to(qz.rvq_code_dtype)
+
+
 def _choose_group_size(last_dim: int, preferred: int) -> Optional[int]:
     """quantization.py:23-33 (kept for API parity)."""
     cands: List[int] = [preferred] if preferred in SUPPORTED_GROUP_SIZES else []
@@ -95,9 +103,10 @@ class ProductQuantizerMLX:
         x = _as_half_cuda(vectors, qz.pq_codebooks.device).contiguous()
         store = K.CodeStoreBuffers(qz, rows=1, cap=max(n, 1))
         residual = torch.empty_like(x)
-        if n:
-            K.encode(qz, x.view(1, n, 1, d), store, 0, 0, residual_out=residual.view(1, n, 1, d))
-        return store.pq[0, 0, :n].clone(), residual
+        if n == 0:
+            return torch.zeros((0, self.num_subspaces), dtype=torch.uint8, device=x.device), residual
+        K.encode(qz, x.view(1, n, 1, d), store, 0, 0, residual_out=residual.view(1, n, 1, d))
+        return store.read_rows(0, "pq", 0, 0, n)[0], residual
 
     def decode(self, codes: torch.Tensor) -> torch.Tensor:
         """quantization.py:146-157 -> fp16 [N, D]."""
@@ -106,7 +115,7 @@ class ProductQuantizerMLX:
         out = torch.empty((1, n, 1, qz.D), dtype=torch.float16, device=qz.pq_codebooks.device)
         if n:
             store = K.CodeStoreBuffers(qz, rows=1, cap=n)
-            store.pq[0, 0, :n] = codes.to(device=store.pq.device, dtype=torch.uint8)
+            store.write(0, "pq", 0, 0, 0, codes.to(dtype=torch.uint8))
             K.decode_codes(qz, store, 0, 0, n, out)
         return out.view(n, qz.D)
 
@@ -154,9 +163,12 @@ class ResidualVQMLX:
             mask = torch.zeros(n, dtype=torch.bool, device=x.device)
             return torch.zeros((0, 0), dtype=torch.int32, device=x.device), mask, torch.zeros(0, dtype=torch.int32,
                                                                                              device=x.device)
-        mask = store.mask[0, 0, :n].bool()
+        if n == 0:
+            return (torch.zeros((0, qz.L), dtype=torch.int32, device=x.device),
+                    torch.zeros(0, dtype=torch.bool, device=x.device), torch.zeros(0, dtype=torch.int32, device=x.device))
+        mask = store.read_rows(0, "active", 0, 0, n)[0, :, 0].bool()
         offsets = torch.nonzero(mask, as_tuple=False).reshape(-1).to(torch.int32)
-        codes = (store.rvq[0, 0, :n][mask].to(torch.int32) & 0xFFFF)
+        codes = (store.read_rows(0, "rvq", 0, 0, n)[0][mask].to(torch.int32) & 0xFFFF)
         return codes, mask, offsets
 
     def decode_correction(self, rvq_codes: torch.Tensor, rvq_mask: torch.Tensor, rvq_offsets: torch.Tensor
@@ -170,8 +182,8 @@ class ResidualVQMLX:
             return out.view(n, self.head_dim)
         store = K.CodeStoreBuffers(qz, rows=1, cap=n)
         offs = rvq_offsets.to(device=dev, dtype=torch.long)
-        store.rvq[0, 0, offs] = rvq_codes.to(device=dev, dtype=torch.int32).to(store.rvq.dtype)
-        store.mask[0, 0, offs] = 1
+        store.put(0, "rvq", 0, 0, offs, _code_values(rvq_codes, qz, dev))
+        store.put(0, "active", 0, 0, offs, torch.ones((offs.numel(), 1), dtype=torch.uint8, device=dev))
         K.decode_codes(qz, store, 0, 0, n, out)
         return out.view(n, self.head_dim)
 
@@ -220,11 +232,11 @@ class HybridQuantizerMLX:
             return out.view(0, qz.D)
         q0 = K.QuantizerBuffers(qz.pq_codebooks, qz.rvq_codebooks, qz.threshold, 0)
         store = K.CodeStoreBuffers(q0, rows=1, cap=n)
-        store.pq[0, 0, :n] = pq_codes.to(device=dev, dtype=torch.uint8)
+        store.write(0, "pq", 0, 0, 0, pq_codes.to(dtype=torch.uint8))
         if q0.L and int(rvq_codes.shape[0]):
             offs = rvq_offsets.to(device=dev, dtype=torch.long)
-            store.rvq[0, 0, offs] = rvq_codes.to(device=dev, dtype=torch.int32).to(store.rvq.dtype)
-            store.mask[0, 0, offs] = 1
+            store.put(0, "rvq", 0, 0, offs, _code_values(rvq_codes, q0, dev))
+            store.put(0, "active", 0, 0, offs, torch.ones((offs.numel(), 1), dtype=torch.uint8, device=dev))
         K.decode_codes(q0, store, 0, 0, n, out)
         return out.view(n, qz.D)
 
@@ -241,17 +253,7 @@ def _compress_tensor_sequence(tensor: torch.Tensor, quantizer: HybridQuantizerML
     store = K.CodeStoreBuffers(qz, rows=num_heads, cap=max(num_tokens, 1))
     if num_tokens:
         K.encode(qz, x.view(1, num_tokens, num_heads, head_dim), store, 0, 0)
-    T = num_tokens
-    rvq = store.rvq[0, :, :T].transpose(0, 1).contiguous() if store.rvq is not None else \
-        torch.zeros((T, num_heads, 0), dtype=torch.uint8, device=dev)
-    mask = store.mask[0, :, :T].transpose(0, 1).bool().contiguous() if store.mask is not None else \
-        torch.zeros((T, num_heads), dtype=torch.bool, device=dev)
-    S = qz.sparse_topk
-    sp_idx = store.sp_idx[0, :, :T].transpose(0, 1).contiguous() if S else \
-        torch.zeros((T, num_heads, 0), dtype=torch.uint8, device=dev)
-    sp_val = store.sp_val[0, :, :T].transpose(0, 1).contiguous() if S else \
-        torch.zeros((T, num_heads, 0), dtype=torch.float16, device=dev)
-    return CompressedTensorMLX(store.pq[0, :, :T].transpose(0, 1).contiguous(), rvq, mask, sp_idx, sp_val, num_heads)
+    return CompressedTensorMLX.from_store(store, 0, 0, 0, num_tokens, num_heads)
 
 
 def _append_compressed_tensor(base: CompressedTensorMLX, addition: CompressedTensorMLX) -> CompressedTensorMLX:

@@ -6,7 +6,9 @@ CompressedTensorMLX :75-98, chunk IO :113-151, AsyncHierarchicalRouterMLX
 memory: each chunk is a pinned code store (same codes the reference writes to
 ``layer{L}_chunk{id}.npz``), copied into a device-resident chunk pool with
 ``rfsn_cold_prefetch`` (cudaMemcpyAsync) — by the router on its side stream
-ahead of time, or by the cache on the compute stream on a miss.
+ahead of time, or by the cache on the compute stream on a miss.  A chunk is
+one packed code-store image (K and V fields of every row, 16-token blocks), so
+moving it either way is a single contiguous copy.
 """
 from __future__ import annotations
 
@@ -93,6 +95,9 @@ class RFSNConfig:
             raise ValueError("hot_policy must be 'prefix' or 'recent'")
         if self.num_kv_heads is not None and self.num_heads % self.num_kv_heads:
             raise ValueError("num_heads must be a multiple of num_kv_heads")
+        if self.hot_policy == "recent" and self.chunk_tokens % 16:
+            raise ValueError("hot_policy 'recent' moves whole 16-token blocks to the cold tier: "
+                             "cold_chunk_tokens (or block_size_seq) must be a multiple of 16")
 
     @property
     def kv_heads(self) -> int:
@@ -158,19 +163,44 @@ class CompressedTensorMLX:
                    torch.zeros((0, heads, config.sparse_topk), dtype=torch.uint8, device=dev),
                    torch.zeros((0, heads, config.sparse_topk), dtype=torch.float16, device=dev), heads)
 
-    def to_store(self, qz: K.QuantizerBuffers) -> K.CodeStoreBuffers:
-        """Copy into a one-slot code store with rows = heads (for the kernels)."""
+    def to_store(self, qz: K.QuantizerBuffers, kv: int = 0,
+                 store: Optional[K.CodeStoreBuffers] = None) -> K.CodeStoreBuffers:
+        """Write into the K (kv=0) or V (kv=1) fields of a one-slot code store with
+        rows = heads (allocated when ``store`` is None)."""
         T, H = self.num_tokens, self.num_heads
-        st = K.CodeStoreBuffers(qz, rows=H, cap=max(T, 16), device=self.pq_codes.device)
+        st = store if store is not None else K.CodeStoreBuffers(qz, rows=H, cap=max(T, 16),
+                                                                device=self.pq_codes.device)
         if T:
-            st.pq[0, :, :T] = self.pq_codes.transpose(0, 1)
-            if st.rvq is not None:
-                st.rvq[0, :, :T] = self.rvq.transpose(0, 1).to(st.rvq.dtype)
-                st.mask[0, :, :T] = self.rvq_mask.transpose(0, 1).to(torch.uint8)
-            if st.sp_idx is not None:
-                st.sp_idx[0, :, :T] = self.sp_idx.transpose(0, 1)
-                st.sp_val[0, :, :T] = self.sp_val.transpose(0, 1)
+            st.write_rows(kv, "pq", 0, 0, self.pq_codes.transpose(0, 1))
+            if qz.L:
+                st.write_rows(kv, "rvq", 0, 0, self.rvq.transpose(0, 1))
+                st.write_rows(kv, "active", 0, 0, self.rvq_mask.transpose(0, 1).to(torch.uint8).unsqueeze(-1))
+            if qz.sparse_topk:
+                st.write_rows(kv, "sp_idx", 0, 0, self.sp_idx.transpose(0, 1))
+                st.write_rows(kv, "sp_val", 0, 0, self.sp_val.transpose(0, 1))
         return st
+
+    @classmethod
+    def from_store(cls, st: K.CodeStoreBuffers, kv: int, slot: int, first: int, count: int, rows: int,
+                   device: Optional[torch.device] = None) -> "CompressedTensorMLX":
+        """Tokens [first, first+count) of rows [0, rows) of a store as a [T, H, ...] tensor."""
+        qz = st.qz
+        dev = device if device is not None else st.data.device
+
+        def grab(name, empty_w, dtype):
+            v = st.read_rows(kv, name, slot, first, count, rows)
+            if v is None:
+                return torch.zeros((count, rows, empty_w), dtype=dtype, device=dev)
+            return v.transpose(0, 1).contiguous().to(dev)
+
+        pq = grab("pq", 0, torch.uint8)
+        rvq = grab("rvq", 0, qz.rvq_code_dtype)
+        act = st.read_rows(kv, "active", slot, first, count, rows)
+        mask = (act[..., 0].transpose(0, 1).bool().contiguous().to(dev) if act is not None
+                else torch.zeros((count, rows), dtype=torch.bool, device=dev))
+        if qz.L and qz.threshold < 0:
+            mask = torch.ones_like(mask)
+        return cls(pq, rvq, mask, grab("sp_idx", 0, torch.uint8), grab("sp_val", 0, torch.float16), rows)
 
 
 def _concat0(lhs: torch.Tensor, rhs: torch.Tensor) -> torch.Tensor:
@@ -203,9 +233,8 @@ class ColdChunk:
     chunk_id: int
     start_token: int
     end_token: int
-    k: K.CodeStoreBuffers  # pinned host, one slot, rows x cap
-    v: K.CodeStoreBuffers
-    ready: Optional[torch.cuda.Event] = None  # D2H writes into k/v done
+    store: K.CodeStoreBuffers  # pinned host, one slot: K and V codes of every row, chunk_tokens tokens
+    ready: Optional[torch.cuda.Event] = None  # device-to-host writes into `store` done
     version: int = 0
 
     @property
@@ -217,9 +246,10 @@ class ColdTier:
     """Cold chunks in pinned host memory plus a device-resident LRU chunk pool.
 
     ``chunks`` maps chunk id -> ColdChunk (codes for every row of the cache).
-    ``pool_k/pool_v`` are device code stores with ``slots`` chunk slots; a
-    chunk is resident when ``slot_of[chunk_id]`` exists.  Copies in either
-    direction go through the C ABI (rfsn_cold_prefetch / rfsn_cold_evict).
+    ``pool`` is a device code store with ``slots`` chunk slots; a chunk is
+    resident when ``slot_of[chunk_id]`` exists and its version matches.
+    Chunk images move with one cudaMemcpyAsync each way through the C ABI
+    (rfsn_cold_prefetch / rfsn_cold_evict).
     """
 
     def __init__(self, qz: K.QuantizerBuffers, rows: int, chunk_tokens: int, slots: int, device):
@@ -229,36 +259,43 @@ class ColdTier:
         self.device = torch.device(device)
         self.chunks: "OrderedDict[int, ColdChunk]" = OrderedDict()
         self.slots = max(1, slots)
-        self.pool_k = K.CodeStoreBuffers(qz, rows, chunk_tokens, self.slots, device=self.device)
-        self.pool_v = K.CodeStoreBuffers(qz, rows, chunk_tokens, self.slots, device=self.device)
+        self.pool = K.CodeStoreBuffers(qz, rows, chunk_tokens, self.slots, device=self.device)
+        self.stage = K.CodeStoreBuffers(qz, rows, chunk_tokens, 1, device=self.device)
         self.slot_of: "OrderedDict[int, int]" = OrderedDict()  # chunk id -> slot (LRU order)
         self.slot_version: Dict[int, int] = {}
         self.slot_ready: Dict[int, torch.cuda.Event] = {}
         self.pinned_by_router: set = set()
         self.lock = threading.Lock()
         self.h2d_bytes = 0
+        self.d2h_bytes = 0
+
+    @property
+    def image_bytes(self) -> int:
+        return self.stage.nbytes_per_slot()
 
     # -- host side -------------------------------------------------------
     def new_chunk(self, chunk_id: int, start: int) -> ColdChunk:
-        c = ColdChunk(chunk_id, start, start,
-                      K.CodeStoreBuffers(self.qz, self.rows, self.chunk_tokens, 1, pin_memory=True),
-                      K.CodeStoreBuffers(self.qz, self.rows, self.chunk_tokens, 1, pin_memory=True))
+        c = ColdChunk(chunk_id, start, start, K.CodeStoreBuffers(self.qz, self.rows, self.chunk_tokens, 1,
+                                                                 pin_memory=True))
         self.chunks[chunk_id] = c
         return c
 
-    def write_from_device(self, chunk: ColdChunk, offset: int, src_k: K.CodeStoreBuffers,
-                          src_v: K.CodeStoreBuffers, src_slot: int, src_first: int, count: int,
-                          stream: torch.cuda.Stream) -> None:
-        """D2H copy of tokens [src_first, +count) of every row into chunk tokens [offset, +count)."""
-        with torch.cuda.stream(stream):
-            for dst, src in ((chunk.k, src_k), (chunk.v, src_v)):
-                for d, s in zip(dst.fields(), src.fields()):
-                    if d is None:
-                        continue
-                    d[0, :, offset:offset + count].copy_(s[src_slot, : self.rows, src_first:src_first + count],
-                                                         non_blocking=True)
-            ev = torch.cuda.Event()
-            ev.record(stream)
+    def load_stage(self, chunk: ColdChunk, stream: torch.cuda.Stream) -> K.CodeStoreBuffers:
+        """Bring a chunk's current image into the device stage (for a partial-chunk append)."""
+        if chunk.ready is not None:
+            stream.wait_event(chunk.ready)
+        K.call("rfsn_cold_prefetch", self.stage.data.data_ptr(), chunk.store.data.data_ptr(), self.image_bytes,
+               stream.cuda_stream, None)
+        self.h2d_bytes += self.image_bytes
+        return self.stage
+
+    def store_stage(self, chunk: ColdChunk, stream: torch.cuda.Stream) -> None:
+        """Write the device stage back as the chunk's image (device -> pinned host)."""
+        K.call("rfsn_cold_evict", chunk.store.data.data_ptr(), self.stage.data.data_ptr(), self.image_bytes,
+               stream.cuda_stream)
+        self.d2h_bytes += self.image_bytes
+        ev = torch.cuda.Event()
+        ev.record(stream)
         chunk.ready = ev
         chunk.version += 1
         self.invalidate(chunk.chunk_id)
@@ -273,13 +310,9 @@ class ColdTier:
     # -- device pool ------------------------------------------------------
     def _grow(self, need: int) -> None:
         new_slots = max(need, self.slots * 2)
-        for name in ("pool_k", "pool_v"):
-            old = getattr(self, name)
-            new = K.CodeStoreBuffers(self.qz, self.rows, self.chunk_tokens, new_slots, device=self.device)
-            for d, s in zip(new.fields(), old.fields()):
-                if d is not None:
-                    d[: self.slots].copy_(s)
-            setattr(self, name, new)
+        new = K.CodeStoreBuffers(self.qz, self.rows, self.chunk_tokens, new_slots, device=self.device)
+        new.data[: self.slots].copy_(self.pool.data)
+        self.pool = new
         self.slots = new_slots
 
     def _free_slot(self, keep: set) -> int:
@@ -304,7 +337,7 @@ class ColdTier:
         return c is not None and s is not None and self.slot_version.get(s) == c.version
 
     def ensure_resident(self, chunk_id: int, stream: torch.cuda.Stream, keep: set = frozenset()) -> int:
-        """Make chunk resident (H2D on `stream` if needed); return its slot."""
+        """Make chunk resident (one H2D copy on `stream` if needed); return its slot."""
         with self.lock:
             if self.resident(chunk_id):
                 self.slot_of.move_to_end(chunk_id)
@@ -313,14 +346,9 @@ class ColdTier:
             slot = self._free_slot(set(keep) | {chunk_id})
             if chunk.ready is not None:
                 stream.wait_event(chunk.ready)
-            sptr = stream.cuda_stream
-            for dst, src in ((self.pool_k, chunk.k), (self.pool_v, chunk.v)):
-                for d, s in zip(dst.fields(), src.fields()):
-                    if d is None:
-                        continue
-                    nbytes = s[0].numel() * s.element_size()
-                    K.call("rfsn_cold_prefetch", d[slot].data_ptr(), s[0].data_ptr(), nbytes, sptr, None)
-                    self.h2d_bytes += nbytes
+            K.call("rfsn_cold_prefetch", self.pool.data[slot].data_ptr(), chunk.store.data.data_ptr(),
+                   self.image_bytes, stream.cuda_stream, None)
+            self.h2d_bytes += self.image_bytes
             ev = torch.cuda.Event()
             ev.record(stream)
             self.slot_of[chunk_id] = slot

@@ -1,0 +1,222 @@
+"""GPU parity of the reference-facing Python API (cache, quantizers, attention, layer).
+
+Mirrors the reference's own suite (rfsn_v10_mlx_ane_complete.py tests and
+cache/quantization unit behaviour) on the golden fixtures generated from the
+unmodified reference, and compares the extensions (batch > 1, GQA, sparse
+residual, hot_policy="recent") against the CPU oracle.  Tolerances: codes and
+materialised windows bit-exact; attention |out - ref| <= 2e-3 |ref| + 2e-3 rms.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import restate as R
+from tests.conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+
+if torch.cuda.is_available():
+    from apple_b200.attention import RFSNHybridAttentionMLX, _blockwise_exact_attention
+    from apple_b200.cache import RFSNv10KVCacheMLX
+    from apple_b200.layer import RFSNDecoderLayerMLX
+    from apple_b200.quantization import (HybridQuantizerMLX, _compress_tensor_sequence, _decode_compressed_tensor,
+                                         _slice_compressed_tensor)
+    from apple_b200.storage import AsyncHierarchicalRouterMLX, RFSNConfig
+
+STAT_KEYS = ("window_start", "window_end", "window_tokens", "context_window", "query_tokens", "used_router",
+             "hot_tokens_materialized", "warm_tokens_materialized", "cold_tokens_materialized",
+             "reconstructed_tokens", "warm_chunk_decodes", "cold_chunk_decodes", "cold_chunks_touched",
+             "cold_chunk_cache_hits", "cold_chunk_cache_misses")
+
+
+def close(out, ref, what=""):
+    out = np.asarray(out, np.float32)
+    ref = np.asarray(ref, np.float32)
+    rms = float(np.sqrt(np.mean(ref ** 2))) if ref.size else 0.0
+    err = np.abs(out - ref)
+    bad = err > 2e-3 * np.abs(ref) + 2e-3 * rms
+    assert not bad.any(), f"{what}: {int(bad.sum())} off, max err {err.max():.3e}"
+
+
+def u16(x):
+    x = x.cpu().numpy() if isinstance(x, torch.Tensor) else x
+    return np.ascontiguousarray(x).view(np.uint16)
+
+
+def golden_quantizer(cfg, g):
+    qz = HybridQuantizerMLX(cfg)
+    qz.pq.codebooks = torch.from_numpy(g["pq_codebooks"]).cuda()
+    qz.rvq.codebooks = torch.from_numpy(g["rvq_codebooks"]).cuda()
+    return qz
+
+
+def tiers_config(tmp_path, **kw):
+    base = dict(hidden_dim=512, num_heads=4, head_dim=128, num_subspaces=8, subspace_dim=16, num_rvq_layers=3,
+                rvq_codebook_size=256, rvq_sparsity_threshold=0.25, hot_capacity=16, warm_capacity=24,
+                block_size_seq=16, disk_cache_dir=str(tmp_path), prefetch_throttle_s=0.0)
+    base.update(kw)
+    return RFSNConfig(**base)
+
+
+def test_cache_tiers_golden(tmp_path):
+    """cache.py tiering (hot prefix, warm, partial cold chunks) vs the reference's outputs."""
+    g = dict(np.load(GOLDEN / "cache_tiers.npz"))
+    cfg = tiers_config(tmp_path)
+    qz = golden_quantizer(cfg, g)
+    cache = RFSNv10KVCacheMLX(cfg, layer_idx=0)
+    s = int(g["update_split"])
+    cache.update(torch.from_numpy(g["keys"][:s]).cuda(), torch.from_numpy(g["values"][:s]).cuda(), qz)
+    cache.update(torch.from_numpy(g["keys"][s:]).cuda(), torch.from_numpy(g["values"][s:]).cuda(), qz)
+    assert [cache.num_hot, cache.num_warm, cache.num_cold] == list(g["tiers"])
+    assert [m["chunk_id"] for m in cache.cold_chunk_metadata] == list(g["cold_chunk_ids"])
+    assert [[m["start_token"], m["end_token"]] for m in cache.cold_chunk_metadata] == g["cold_chunk_bounds"].tolist()
+    mem = cache.memory_usage_bytes()
+    assert [mem["hot_bytes"], mem["warm_pq_bytes"], mem["warm_rvq_bytes"], mem["cold_chunks"],
+            mem["cold_tokens"]] == list(g["memory"])
+    q = torch.from_numpy(g["q"]).cuda()
+    for i, (qpos, win) in enumerate(g["cases"]):
+        tag = f"q{i // 3}_w{i % 3}"
+        win = None if win < 0 else int(win)
+        out = cache.attention_forward(q, causal=True, query_positions=[int(qpos)], context_window=win)
+        assert [cache.last_access_stats[k] for k in STAT_KEYS] == list(g[f"{tag}_stats"]), tag
+        close(out.cpu().numpy(), g[f"{tag}_out"], tag)
+        kw, vw, adj = cache.materialize_window([int(qpos)], win)
+        np.testing.assert_array_equal(u16(kw), u16(g[f"{tag}_keys"]))
+        np.testing.assert_array_equal(u16(vw), u16(g[f"{tag}_values"]))
+        np.testing.assert_array_equal(adj.cpu().numpy(), g[f"{tag}_adjusted"])
+    # cold chunks read back from the pinned tier equal the codes the reference stores
+    chunk = cache.load_cold_chunk(int(g["cold_chunk_ids"][0]))
+    assert int(chunk["num_tokens"][0]) == 16
+    with pytest.raises(KeyError):
+        cache.load_cold_chunk(999)
+    cache.close()
+
+
+def test_cache_tiers_with_router(tmp_path):
+    """Router-driven prefetch: same outputs, hit/miss statistics as the oracle with the router's loads."""
+    g = dict(np.load(GOLDEN / "cache_tiers.npz"))
+    cfg = tiers_config(tmp_path)
+    qz = golden_quantizer(cfg, g)
+    cache = RFSNv10KVCacheMLX(cfg, layer_idx=3)
+    cache.update(torch.from_numpy(g["keys"]).cuda(), torch.from_numpy(g["values"]).cuda(), qz)
+    router = AsyncHierarchicalRouterMLX(cfg, layer_idx=3)
+    q = torch.from_numpy(g["q"]).cuda()
+    ocfg = R.OracleConfig(hidden_dim=512, num_heads=4, head_dim=128, num_subspaces=8, subspace_dim=16,
+                          num_rvq_layers=3, rvq_codebook_size=256, rvq_sparsity_threshold=0.25,
+                          hot_capacity=16, warm_capacity=24, block_size_seq=16)
+    oc = R.OracleCache(ocfg, R.Quantizer(g["pq_codebooks"], g["rvq_codebooks"], float(g["threshold"])), batch=1)
+    oc.update(g["keys"][None], g["values"][None])
+    held = []  # the router's chunk cache persists across calls (FIFO of 16, storage.py:186-188)
+    for pos, win in ((59, 30), (45, 16), (59, 8)):
+        out = cache.attention_forward(q, causal=True, query_positions=[pos], router=router, current_position=pos,
+                                      context_window=win)
+        ids = [m["chunk_id"] for m in oc.cold]
+        for c in R.router_candidates(ids, pos, win, 16, max(1, (win + 15) // 16)):
+            if c not in held:
+                held.append(c)
+        held = held[-16:]
+        kw, vw, adj = oc.materialize_window([pos], win, cold_hits=set(held), used_router=True)
+        ref = R.blockwise_exact_attention(g["q"], kw[0], vw[0], 128 ** -0.5, 16, True, adj)
+        close(out.cpu().numpy(), ref, f"pos {pos} win {win}")
+        st = cache.last_access_stats
+        assert st["used_router"] == 1
+        assert (st["cold_chunk_cache_hits"], st["cold_chunk_cache_misses"]) == (
+            oc.last_access_stats["cold_chunk_cache_hits"], oc.last_access_stats["cold_chunk_cache_misses"])
+    cache.close()
+
+
+@pytest.mark.parametrize("policy", ["prefix", "recent"])
+def test_cache_extensions_vs_oracle(tmp_path, policy):
+    """batch 2, GQA 4:2, top-4 sparse residual; token-by-token decode appends through every tier."""
+    rng = np.random.default_rng(11)
+    kw = dict(hidden_dim=256, num_heads=4, head_dim=64, num_subspaces=16, subspace_dim=4, num_rvq_layers=1,
+              rvq_codebook_size=256, rvq_sparsity_threshold=-1.0, hot_capacity=16, warm_capacity=32,
+              block_size_seq=16, num_kv_heads=2, sparse_topk=4, hot_policy=policy)
+    cfg = RFSNConfig(batch_size=2, disk_cache_dir=str(tmp_path), **kw)
+    ocfg = R.OracleConfig(**kw)
+    pq = (rng.standard_normal((16, 256, 4)) * 0.7).astype(np.float16)
+    rvq = (rng.standard_normal((1, 256, 64)) * 0.3).astype(np.float16)
+    qz = HybridQuantizerMLX(cfg)
+    qz.pq.codebooks, qz.rvq.codebooks = torch.from_numpy(pq).cuda(), torch.from_numpy(rvq).cuda()
+    oc = R.OracleCache(ocfg, R.Quantizer(pq, rvq, -1.0, sparse_topk=4), batch=2)
+    cache = RFSNv10KVCacheMLX(cfg, layer_idx=1)
+    k = rng.standard_normal((2, 90, 2, 64)).astype(np.float16)
+    v = rng.standard_normal((2, 90, 2, 64)).astype(np.float16)
+    cache.update(torch.from_numpy(k[:, :70]).cuda(), torch.from_numpy(v[:, :70]).cuda(), qz)
+    oc.update(k[:, :70], v[:, :70])
+    for t in range(70, 90):
+        cache.update(torch.from_numpy(k[:, t:t + 1]).cuda(), torch.from_numpy(v[:, t:t + 1]).cuda(), qz)
+        oc.update(k[:, t:t + 1], v[:, t:t + 1])
+    assert (cache.num_hot, cache.num_warm, cache.num_cold) == (oc.num_hot, oc.num_warm, oc.num_cold)
+    kg, vg, _ = cache.materialize_window()
+    ko, vo, _ = oc.materialize_window()
+    np.testing.assert_array_equal(u16(kg), u16(ko))
+    np.testing.assert_array_equal(u16(vg), u16(vo))
+    q = rng.standard_normal((2, 4, 64)).astype(np.float16)
+    for pos in (89, 60):
+        for win in (None, 40, 17):
+            out = cache.attention_forward(torch.from_numpy(q).cuda(), causal=True, query_positions=[pos],
+                                          context_window=win)
+            ref = oc.attention_forward(q[:, None], causal=True, query_positions=[pos], context_window=win)
+            close(out.cpu().numpy(), ref[:, 0], f"position {pos} window {win}")
+    cache.close()
+
+
+def test_quantizer_api_golden():
+    """HybridQuantizerMLX encode/decode and the compressed-tensor helpers vs reference vectors."""
+    g = dict(np.load(GOLDEN / "quant_d128_m8x16_rvq3.npz"))
+    cfg = RFSNConfig(hidden_dim=512, num_heads=4, head_dim=128, num_subspaces=8, subspace_dim=16,
+                     num_rvq_layers=3, rvq_codebook_size=256, rvq_sparsity_threshold=float(g["threshold"]))
+    qz = golden_quantizer(cfg, g)
+    x = torch.from_numpy(g["x"]).cuda()
+    pq, rvq, mask, offs = qz.encode(x)
+    np.testing.assert_array_equal(pq.cpu().numpy(), g["pq_codes"])
+    np.testing.assert_array_equal(mask.cpu().numpy(), g["rvq_mask"])
+    np.testing.assert_array_equal(offs.cpu().numpy(), g["rvq_offsets"])
+    np.testing.assert_array_equal(rvq.cpu().numpy(), g["rvq_codes"].astype(np.int32))
+    np.testing.assert_array_equal(u16(qz.decode(pq, rvq, mask, offs)), u16(g["decoded"]))
+    np.testing.assert_array_equal(u16(qz.pq.decode(pq)), u16(g["pq_decoded"]))
+    codes, residual = qz.pq.quantize(x)
+    np.testing.assert_array_equal(u16(residual), u16(g["residual"]))
+    ct = _compress_tensor_sequence(x.view(24, 4, 128), qz)
+    np.testing.assert_array_equal(u16(_decode_compressed_tensor(ct, qz)), u16(g["decoded"].reshape(24, 4, 128)))
+    part = _slice_compressed_tensor(ct, 5, 17)
+    np.testing.assert_array_equal(u16(_decode_compressed_tensor(part, qz)),
+                                  u16(g["decoded"].reshape(24, 4, 128)[5:17]))
+
+
+def test_hybrid_attention_api_golden():
+    """RFSNHybridAttentionMLX and _blockwise_exact_attention vs the reference outputs."""
+    g = dict(np.load(GOLDEN / "attention_hybrid.npz"))
+    cfg = RFSNConfig(hidden_dim=512, num_heads=4, head_dim=128, num_subspaces=8, subspace_dim=16,
+                     num_rvq_layers=3, rvq_codebook_size=256, rvq_sparsity_threshold=float(g["threshold"]),
+                     block_size_seq=16)
+    qz = golden_quantizer(cfg, g)
+    ks = _compress_tensor_sequence(torch.from_numpy(g["keys"]).cuda(), qz)
+    vs = _compress_tensor_sequence(torch.from_numpy(g["values"]).cuda(), qz)
+    attn = RFSNHybridAttentionMLX(cfg)
+    q = torch.from_numpy(g["q"]).cuda()
+    close(attn(q, ks, vs, qz, causal=True, query_positions=g["positions"]).cpu().numpy(), g["out_causal"], "causal")
+    close(attn(q, ks, vs, qz, causal=False).cpu().numpy(), g["out_plain"], "plain")
+    close(attn(q, ks, vs, qz, causal=True, query_positions=g["positions_bh"]).cpu().numpy(), g["out_bh"], "bh")
+    dk = torch.from_numpy(g["decoded_keys"]).cuda()
+    dv = torch.from_numpy(g["decoded_values"]).cuda()
+    out = _blockwise_exact_attention(q, dk, dv, 128 ** -0.5, 16, True, g["positions"])
+    close(out.cpu().numpy(), g["out_causal"], "blockwise")
+
+
+def test_decoder_layer_cached_decode_matches_dense(tmp_path):
+    """RFSNDecoderLayerMLX: with every token in the exact hot tier, cache-backed decode
+    equals the dense causal layer on the full sequence (last position)."""
+    cfg = RFSNConfig(hidden_dim=512, num_heads=8, head_dim=64, num_subspaces=8, subspace_dim=8, num_rvq_layers=0,
+                     rvq_codebook_size=256, hot_capacity=4096, warm_capacity=64, block_size_seq=16,
+                     num_kv_heads=4, disk_cache_dir=str(tmp_path))
+    layer = RFSNDecoderLayerMLX(cfg, layer_idx=0, init="normal", seed=3)
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn((1, 40, 512), generator=g).cuda()
+    layer.prefill_cache(x[:, :32])
+    for t in range(32, 40):
+        y = layer(x[:, t:t + 1], use_cache=True)
+    dense = layer(x, use_cache=False)
+    close(y[0, 0].float().cpu().numpy(), dense[0, -1].float().cpu().numpy(), "decoder layer")
+    assert layer.cache_tokens == 40

@@ -145,3 +145,22 @@ def test_recent_policy_matches_prefix_arithmetic():
     full = qz.decode_f32(qz.compress(k[0, :8]))
     base = qz.decode_flat(*qz.encode_flat(k[0, :8].reshape(-1, 64))[:4]).reshape(8, 2, 64)
     assert np.abs(full - k[0, :8]).sum() < np.abs(base.astype(np.float32) - k[0, :8]).sum()
+
+
+def test_router_candidates_api_matches_golden(tmp_path):
+    """AsyncHierarchicalRouterMLX.candidates (the B200 router's selection) vs the reference's order."""
+    from apple_b200.storage import AsyncHierarchicalRouterMLX, RFSNConfig, register_cold_tier, unregister_cold_tier
+    g = load("router_order")
+    cs = int(g["chunk_size"])
+
+    class _Tier:  # only the chunk-id index is consulted when choosing candidates
+        chunks = {int(c): None for c in g["chunk_ids"]}
+
+    cfg = RFSNConfig(hidden_dim=512, num_heads=4, head_dim=128, block_size_seq=cs, disk_cache_dir=str(tmp_path))
+    register_cold_tier(tmp_path, 7, _Tier())
+    try:
+        router = AsyncHierarchicalRouterMLX(cfg, layer_idx=7)
+        for (pos, win, k), want in zip(g["queries"], g["loaded"]):
+            assert router.candidates(int(pos), int(win), int(k)) == [int(x) for x in want if x >= 0]
+    finally:
+        unregister_cold_tier(tmp_path, 7)
