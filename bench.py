@@ -28,7 +28,6 @@ import json
 import math
 import os
 import statistics
-import subprocess
 import sys
 import time
 from pathlib import Path
@@ -40,6 +39,7 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "decode attn steps/s per layer at 32K ctx"
 UNIT = "steps/s"
+DTYPE = "f16 operands, f32 accumulate"
 CFG = dict(batch=8, q_heads=32, kv_heads=8, head_dim=64, context=32768, hot=1024, M=16, ds=4, K=256, L=1, Kr=256,
            sparse=8, outliers=4, seed=1)
 
@@ -113,64 +113,104 @@ def build_workload(device, seed):
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle sampling during the timed region."""
+    """SM clock and throttle-reason samples (NVML) from a polling thread during the timed region.
 
-    def __init__(self, device_index: int):
-        self.proc = None
-        self.idx = device_index
-        self.path = ROOT / "gpurun_out" / f"clocks_{os.getpid()}.csv"
+    The torch device is matched to its NVML handle by UUID (NVML ignores
+    CUDA_VISIBLE_DEVICES).  Reasons reported: hw_slowdown, hw_thermal_slowdown,
+    sw_thermal_slowdown, sw_power_cap.  Falls back to no samples when NVML is absent.
+    """
+
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4}
+
+    def __init__(self, device, period_s: float = 0.002):
+        self.device = device
+        self.period = period_s
+        self.samples = []
+        self.max_mhz = None
+        self.error = None
+        self._stop = None
+        self._thread = None
+
+    def _handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        props = torch.cuda.get_device_properties(self.device)
+        uuid = str(getattr(props, "uuid", "") or "")
+        if uuid:
+            try:
+                return pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            except Exception:
+                pass
+        bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        return pynvml.nvmlDeviceGetHandleByPciBusId(bus)
 
     def __enter__(self):
+        import threading
         try:
-            self.path.parent.mkdir(exist_ok=True)
-            self.f = open(self.path, "w")
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.idx}",
-                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-                 "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=self.f, stderr=subprocess.DEVNULL)
-        except Exception:
-            self.proc = None
+            import pynvml
+            h = self._handle()
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        except Exception as e:  # NVML missing: report no samples
+            self.error = str(e)
+            return self
+        self._stop = threading.Event()
+
+        def poll():
+            while not self._stop.is_set():
+                try:
+                    self.samples.append((float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)), int(get_reasons(h))))
+                except Exception as e:  # pragma: no cover
+                    self.error = str(e)
+                    return
+                time.sleep(self.period)
+
+        self._thread = threading.Thread(target=poll, daemon=True)
+        self._thread.start()
         return self
 
     def __exit__(self, *a):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
-            self.f.close()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
 
     def summary(self) -> dict:
-        try:
-            rows = [l.split(",") for l in self.path.read_text().strip().splitlines() if l.strip()]
-            sm = [float(r[0]) for r in rows]
-            mx = [float(r[1]) for r in rows]
-            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-            reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[3 + i] and "Not" not in r[3 + i]})
-            return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                    "reasons": reasons, "samples": len(rows)}
-        except Exception as e:  # pragma: no cover - best effort
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": str(e)}
+        sm = [c for c, _ in self.samples]
+        reasons = sorted({name for _, bits in self.samples for name, bit in self.REASONS.items() if bits & bit})
+        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz, "reasons": reasons,
+               "samples": len(sm), "source": "nvml"}
+        if self.error:
+            out["error"] = self.error
+        return out
 
 
 # ---------------------------------------------------------------------------
-# CPU baseline: the numpy oracle on a sample of (sequence, KV-head) rows
+# CPU baseline: the numpy oracle (reference algorithm) on a sample of rows
 # ---------------------------------------------------------------------------
+# A row is one (sequence, KV head): decode its 31744 warm tokens the way the
+# reference materialises the window (cache.py:344-393) and run the fp32
+# blockwise attention of its 4 query heads (attention.py:39-105).  A CPU step
+# runs one row task per host core in a spawn process pool (tasks cycle over
+# CPU_ROWS distinct encoded rows; every task is a full row of work) and is
+# scaled to the 64 rows (8 sequences x 8 KV heads) of the batch.
 
-def build_cpu_sample(kv_heads_sample: int, seed: int = 1):
-    """Seeded synthetic rows of the same workload, encoded by the oracle (setup, untimed)."""
+CPU_ROWS = 2
+_ROW_SAMPLE = None
+
+
+def build_cpu_sample(rows: int = CPU_ROWS, seed: int = 1) -> dict:
+    """Seeded synthetic rows of the workload, encoded by the oracle (setup, untimed)."""
     from oracle import restate as R
     c = CFG
     D, T, hot, M, ds = c["head_dim"], c["context"], c["hot"], c["M"], c["ds"]
     warm = T - hot
     rng = np.random.default_rng(seed)
-    k = rng.standard_normal((T, kv_heads_sample, D)).astype(np.float32)
+    k = rng.standard_normal((T, rows, D)).astype(np.float32)
     k[..., rng.choice(D, c["outliers"], replace=False)] *= 10.0
     k = k.astype(np.float16)
-    v = rng.standard_normal((T, kv_heads_sample, D)).astype(np.float16)
+    v = rng.standard_normal((T, rows, D)).astype(np.float16)
     flat = np.concatenate([k.reshape(-1, D), v.reshape(-1, D)], 0)
     pq_cb = np.stack([flat[rng.integers(0, flat.shape[0], c["K"]), m * ds:(m + 1) * ds] for m in range(M)])
     _, res = R.pq_quantize(flat[rng.integers(0, flat.shape[0], 4096)], pq_cb)
@@ -179,48 +219,88 @@ def build_cpu_sample(kv_heads_sample: int, seed: int = 1):
     oq = R.Quantizer(pq_cb, rvq_cb, -1.0, c["sparse"])
     kc, vc = oq.compress(k[:warm]), oq.compress(v[:warm])
     G = c["q_heads"] // c["kv_heads"]
-    q = rng.standard_normal((1, kv_heads_sample * G, D)).astype(np.float16)
-    return dict(oq=oq, kc=kc, vc=vc, hot_k=k[warm:], hot_v=v[warm:], q=q, rows=kv_heads_sample)
+    q = rng.standard_normal((1, rows * G, D)).astype(np.float16)
+    return dict(oq=oq, kc=kc, vc=vc, hot_k=k[warm:], hot_v=v[warm:], q=q, rows=rows, G=G)
 
 
-def time_cpu_step(s) -> float:
-    """Seconds per full-batch decode step: materialise the window (decode) + fp32 blockwise
-    attention, as the reference does (cache.py:344-428, attention.py:39-105), scaled from
-    the sampled rows to batch x kv_heads rows."""
+def _row_init(sample: dict) -> None:
+    global _ROW_SAMPLE
+    _ROW_SAMPLE = sample
+
+
+def _row_codes(c, h: int):
     from oracle import restate as R
-    c = CFG
-    D, T = c["head_dim"], c["context"]
+    return R.Codes(c.pq[:, h:h + 1], c.rvq[:, h:h + 1], c.mask[:, h:h + 1], c.sp_idx[:, h:h + 1], c.sp_val[:, h:h + 1])
+
+
+def cpu_row(h: int) -> float:
+    """Decode + attention of KV-head row h of the sample; returns its seconds."""
+    from oracle import restate as R
+    s = _ROW_SAMPLE
+    D, T, G = CFG["head_dim"], CFG["context"], s["G"]
     t0 = time.perf_counter()
-    kw = np.concatenate([s["oq"].decode(s["kc"]), s["hot_k"]], 0)
-    vw = np.concatenate([s["oq"].decode(s["vc"]), s["hot_v"]], 0)
-    R.blockwise_exact_attention(s["q"], kw, vw, D ** -0.5, 128, True, np.full((1, s["q"].shape[1]), T - 1))
-    dt = time.perf_counter() - t0
-    return dt * (c["batch"] * c["kv_heads"]) / s["rows"]
+    kw = np.concatenate([s["oq"].decode(_row_codes(s["kc"], h)), s["hot_k"][:, h:h + 1]], 0)
+    vw = np.concatenate([s["oq"].decode(_row_codes(s["vc"], h)), s["hot_v"][:, h:h + 1]], 0)
+    R.blockwise_exact_attention(s["q"][:, h * G:(h + 1) * G], kw, vw, D ** -0.5, 128, True, np.full((1, G), T - 1))
+    return time.perf_counter() - t0
+
+
+class CpuBaseline:
+    """Spawned worker pool (started before any GPU work is needed; spawn is fork-safe)."""
+
+    def __init__(self, workers: int, rows: int = CPU_ROWS, seed: int = 1):
+        import multiprocessing as mp
+        self.rows = rows
+        self.workers = max(1, workers)
+        sample = build_cpu_sample(rows, seed)
+        env_keep = {k: os.environ.get(k) for k in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS")}
+        for k in env_keep:
+            os.environ[k] = "1"  # one thread per worker process
+        try:
+            self.pool = mp.get_context("spawn").Pool(self.workers, initializer=_row_init, initargs=(sample,))
+        finally:
+            for k, v in env_keep.items():
+                if v is None:
+                    os.environ.pop(k, None)
+                else:
+                    os.environ[k] = v
+
+    def step(self) -> float:
+        """Seconds per full-batch decode step (wall time of one sequence's rows, x batch)."""
+        t0 = time.perf_counter()
+        self.pool.map(cpu_row, [i % self.rows for i in range(self.workers)], chunksize=1)
+        return (time.perf_counter() - t0) * CFG["batch"] * CFG["kv_heads"] / self.workers
+
+    def close(self) -> None:
+        self.pool.close()
+        self.pool.join()
+
+    def describe(self) -> str:
+        return (f"numpy oracle port: {self.workers} row tasks per step (one per host core; a row = 1 KV head with "
+                f"4 query heads over the full 32K window), scaled to 64 rows by x{64 / self.workers:g}")
 
 
 def run_reference(args) -> None:
-    """CPU oracle port of the reference algorithm on the host cores (rank 0 only)."""
+    """CPU oracle port of the reference algorithm on all host cores (rank 0 only)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    cores = os.cpu_count() or 1
+    cb = CpuBaseline(cores)
     try:
-        import torch
-        torch.set_num_threads(os.cpu_count() or 1)
-    except ImportError:
-        pass
-    heads = 1
-    s = build_cpu_sample(heads, CFG["seed"])
-    for _ in range(max(0, args.warmup)):
-        time_cpu_step(s)
-    times = [time_cpu_step(s) for _ in range(args.steps)]
+        for _ in range(max(0, args.warmup)):
+            cb.step()
+        times = [cb.step() for _ in range(args.steps)]
+    finally:
+        cb.close()
     sec = statistics.mean(times)
     val = 1.0 / sec
-    sample = f"1 sequence x {heads} of 8 KV heads (4 query heads each), full 32K window; scaled x{64 // heads}"
     line = {"metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "vs_baseline": None, "dtype": DTYPE, "data": "synthetic", "impl": "reference",
             "config": workload_desc(args.gpus),
-            "cpu_baseline": {"value": val, "unit": UNIT, "cores": os.cpu_count(), "kind": "port", "sample": sample},
+            "cpu_baseline": {"value": val, "unit": UNIT, "cores": cb.workers, "kind": "port",
+                             "sample": cb.describe()},
             "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
 
@@ -228,6 +308,74 @@ def run_reference(args) -> None:
 # ---------------------------------------------------------------------------
 # B200 arm
 # ---------------------------------------------------------------------------
+
+def ncu_traffic() -> dict:
+    """DRAM bytes per launch of the fused kernel from the committed ncu summary (None if absent)."""
+    p = ROOT / "profiles" / "decode_attn_cfg2.md"
+    out = {"traffic": None, "source": None}
+    if p.exists():
+        for line in p.read_text().splitlines():
+            if line.strip().startswith("dram_bytes_per_launch:"):
+                out["traffic"] = float(line.split(":", 1)[1].strip().split()[0])
+                out["source"] = "profiles/decode_attn_cfg2.md"
+    return out
+
+
+def public_api_cache(w, dev):
+    """RFSNv10KVCacheMLX holding the workload (hot = newest 1024 tokens, warm = the rest)."""
+    import torch
+    from apple_b200.cache import RFSNv10KVCacheMLX
+    from apple_b200.quantization import HybridQuantizerMLX
+    from apple_b200.storage import RFSNConfig
+    c = CFG
+    cfg = RFSNConfig(hidden_dim=c["q_heads"] * c["head_dim"], num_heads=c["q_heads"], head_dim=c["head_dim"],
+                     num_subspaces=c["M"], subspace_dim=c["ds"], num_rvq_layers=c["L"], rvq_codebook_size=c["Kr"],
+                     rvq_sparsity_threshold=-1.0, hot_capacity=c["hot"], warm_capacity=c["context"] - c["hot"],
+                     block_size_seq=128, num_kv_heads=c["kv_heads"], batch_size=c["batch"], hot_policy="recent",
+                     sparse_topk=c["sparse"], device=str(dev), disk_cache_dir=str(ROOT / "gpurun_out" / "bench_cold"))
+    qz = HybridQuantizerMLX(cfg)
+    qz.pq.codebooks = w["qz"].pq_codebooks
+    qz.rvq.codebooks = w["qz"].rvq_codebooks
+    cache = RFSNv10KVCacheMLX(cfg, layer_idx=0)
+    cache.update(w["k"], w["v"], qz)
+    torch.cuda.synchronize()
+    assert (cache.num_hot, cache.num_warm, cache.num_cold) == (c["hot"], c["context"] - c["hot"], 0)
+    return cache
+
+
+def e2e_public_api(w, args, dev) -> dict:
+    """The decode step through the public API: pinned host query in, host output out, every step."""
+    import torch
+    cache = public_api_cache(w, dev)
+    h_q = w["q"][:, 0].cpu().pin_memory()          # [B, Hq, D]
+    h_out = torch.empty_like(h_q).pin_memory()
+
+    def step():
+        out = cache.attention_forward(h_q, causal=True)
+        h_out.copy_(out)  # device -> host read of the step's result
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(args.steps):
+        step()
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    # the public API's result equals the device-resident kernel call
+    ref = torch.empty_like(w["q"])
+    from apple_b200 import kernels as K
+    K.decode_attention(w["qz"], w["q"], ref, w["segs"], kv_heads=CFG["kv_heads"], qpos=w["qpos"], causal=True,
+                       hot=w["hot"], warm=w["warm"])
+    err = float((ref[:, 0].float().cpu() - h_out.float()).abs().max())
+    nb = h_q.numel() * h_q.element_size()
+    cache.close()
+    return {"value": 1e3 / ms, "unit": UNIT, "h2d_bytes_per_step": nb, "d2h_bytes_per_step": nb,
+            "api": "RFSNv10KVCacheMLX.attention_forward", "max_abs_diff_vs_kernel_call": err}
+
 
 def run_b200(args) -> None:
     import torch
@@ -237,6 +385,7 @@ def run_b200(args) -> None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    cpu = CpuBaseline(os.cpu_count() or 1) if (rank == 0 and world == 1) else None
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
@@ -244,14 +393,31 @@ def run_b200(args) -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     w = build_workload(dev, CFG["seed"] + rank)
     out = torch.empty_like(w["q"])
-    gathered = torch.empty((world,) + tuple(out.shape), dtype=out.dtype, device=dev) if world > 1 else None
-    launches_per_step = 2  # fused decode-attention + LSE merge
+    # weak scaling: global batch 8N split by sequence (apple_b200.sharding), outputs all-gathered
+    from apple_b200.sharding import gather_outputs, plan_shards
+    shards = plan_shards(CFG["batch"] * world, CFG["kv_heads"], world)
+    assert shards[rank].batch == CFG["batch"]
+    launches_per_step = 2  # fused decode attention + log-sum-exp merge
 
-    def step():
+    def attn():
         K.decode_attention(w["qz"], w["q"], out, w["segs"], kv_heads=CFG["kv_heads"], qpos=w["qpos"], causal=True,
                            hot=w["hot"], warm=w["warm"])
-        if gathered is not None:
-            dist.all_gather_into_tensor(gathered, out)
+
+    for _ in range(max(3, args.warmup)):
+        attn()
+    torch.cuda.synchronize()
+    # one decode step (attention + merge) captured as a CUDA graph; each timed step replays it
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        attn()
+    torch.cuda.synchronize()
+
+    def step():
+        graph.replay()
+        if world > 1:
+            gather_outputs(out, shards, rank, world, CFG["q_heads"] // CFG["kv_heads"])
 
     for _ in range(max(3, args.warmup)):
         step()
@@ -260,7 +426,7 @@ def run_b200(args) -> None:
         dist.barrier()
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
+    with ClockSampler(dev) as clocks:
         torch.cuda.synchronize()
         e0.record(stream)
         for _ in range(args.steps):
@@ -276,82 +442,45 @@ def run_b200(args) -> None:
     ms_per_step = ms / args.steps
     value = world * 1e3 / ms_per_step
 
-    # kernel-only timing for the roofline (no collective in between)
+    # kernel-only duration for the roofline: the same graph without the collective
     torch.cuda.synchronize()
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record(stream)
     for _ in range(args.steps):
-        K.decode_attention(w["qz"], w["q"], out, w["segs"], kv_heads=CFG["kv_heads"], qpos=w["qpos"], causal=True,
-                           hot=w["hot"], warm=w["warm"])
+        graph.replay()
     e3.record(stream)
     torch.cuda.synchronize()
     kern_ms = e2.elapsed_time(e3) / args.steps
 
-    # end-to-end through the public API with host buffers
     e2e = e2e_public_api(w, args, dev)
-
+    del graph
     if world > 1:
         dist.barrier()
     if rank == 0:
         peak, peak_kind = measured_peak()
         nbytes = algorithmic_bytes()
         achieved = nbytes / (kern_ms * 1e-3) / 1e9
-        cs = build_cpu_sample(2, CFG["seed"])
-        time_cpu_step(cs)
-        cpu_sec = statistics.mean([time_cpu_step(cs) for _ in range(3)])
+        traffic = ncu_traffic()
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": max(3, args.warmup), "ms_per_step": ms_per_step, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "scaling": "weak", "vs_baseline": None, "dtype": DTYPE, "data": "synthetic",
                 "config": workload_desc(world),
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                             "frac": achieved / peak, "traffic": None, "peak_source": peak_kind,
-                             "algorithmic_bytes_per_step": nbytes, "kernel_ms": kern_ms},
-                "cpu_baseline": {"value": 1.0 / cpu_sec, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
-                                 "sample": "numpy oracle: 1 sequence x 2 of 8 KV heads, full 32K window, "
-                                           "mean of 3 steps, scaled x32"},
+                             "frac": achieved / peak, "traffic": traffic["traffic"],
+                             "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, burst copy)",
+                             "traffic_source": traffic["source"],
+                             "algorithmic_bytes_per_step": nbytes, "kernel_ms": kern_ms,
+                             "kernel_ms_covers": "fused attention + LSE merge (one graph replay per step)"},
                 "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "clocks": clocks.summary()}
+        if cpu is not None:
+            cpu.step()
+            times = [cpu.step() for _ in range(3)]
+            cpu.close()
+            line["cpu_baseline"] = {"value": 1.0 / statistics.mean(times), "unit": UNIT, "cores": cpu.workers,
+                                    "kind": "port", "sample": cpu.describe() + "; mean of 3 steps"}
         print(json.dumps(line))
     if world > 1:
         dist.destroy_process_group()
-
-
-def e2e_public_api(w, args, dev) -> dict:
-    """Same decode step through the public cache API with pinned-host q in and output out."""
-    import torch
-    try:
-        from apple_b200.cache import RFSNv10KVCacheMLX  # noqa: F401
-        from apple_b200.bench_support import public_api_step
-    except ImportError:
-        public_api_step = None
-    c = CFG
-    h_q = w["q"].cpu().pin_memory()
-    h_out = torch.empty_like(h_q).pin_memory()
-    if public_api_step is None:
-        from apple_b200 import kernels as K
-        d_q = torch.empty_like(w["q"])
-        d_out = torch.empty_like(w["q"])
-
-        def step():
-            d_q.copy_(h_q, non_blocking=True)
-            K.decode_attention(w["qz"], d_q, d_out, w["segs"], kv_heads=c["kv_heads"], qpos=w["qpos"], causal=True,
-                               hot=w["hot"], warm=w["warm"])
-            h_out.copy_(d_out, non_blocking=True)
-        api = "kernels.decode_attention (C ABI)"
-    else:
-        step, api = public_api_step(w, h_q, h_out)
-    for _ in range(3):
-        step()
-    torch.cuda.synchronize()
-    s = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(s)
-    for _ in range(args.steps):
-        step()
-    e1.record(s)
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
-    nb = h_q.numel() * h_q.element_size()
-    return {"value": 1e3 / ms, "unit": UNIT, "h2d_bytes_per_step": nb, "d2h_bytes_per_step": nb, "api": api}
 
 
 def main() -> None:
