@@ -11,8 +11,11 @@
 // flattened (row, window-token) space is cut into equal contiguous ranges, one
 // per CTA (one CTA per SM by default), so every SM streams the same number of
 // tokens whatever the batch/head count.  A CTA emits one partial
-// (max, sum, unnormalised output) per row it touches; rfsn_merge_kernel combines
-// the partials of each row by log-sum-exp and writes fp16.
+// (max, sum, unnormalised output) per row piece it touches and then takes a
+// ticket for the row; the CTA that completes a row's last piece combines the
+// row's partials by log-sum-exp and writes fp16 (no separate merge launch).
+// Tickets carry the launch's call number in their upper 48 bits, so counts
+// left by earlier or aborted launches are never taken for this launch's.
 //
 // Inside a CTA.  Warp NW (the producer) walks the CTA's tiles and issues 1-D
 // bulk TMA copies (cp.async.bulk): a code tile is a run of whole 16-token
@@ -30,6 +33,8 @@
 #include <cuda_runtime.h>
 #include <math.h>
 
+#include <atomic>
+#include <chrono>
 #include <mutex>
 
 #include "rfsn_api_internal.h"
@@ -56,8 +61,11 @@ struct StoreDev {
 struct AttnParams {
   const uint16_t* q;
   const int32_t* qpos;
+  uint16_t* out;
   float* ws_o;
   float* ws_ml;
+  unsigned long long* tickets;  // one per row: (call number << 16) | pieces done
+  unsigned long long epoch;     // this launch's call number (< 2^48)
   int32_t* dev_status;
   int B, Q, Hq, Hkv, D, G, R, causal;
   float scale;
@@ -100,6 +108,57 @@ __device__ __forceinline__ bool consumer_sync(uint64_t* bar, uint32_t& phase, vo
   return ok;
 }
 
+// First and last CTA index whose token range touches row `row`: its pieces.
+__device__ __forceinline__ int row_pieces(const AttnParams& p, int64_t row, int64_t* first_cta) {
+  const int64_t c0 = (row * p.W) / p.per_cta;
+  const int64_t c1 = (row * p.W + p.W - 1) / p.per_cta;
+  *first_cta = c0;
+  return (int)(c1 - c0 + 1);
+}
+
+// Count this CTA's piece of `row` done; returns 1 if it was the row's last
+// piece of this launch, 0 if not, -1 if the ticket could not be taken.  A
+// ticket holding another launch's call number counts as zero.
+__device__ __forceinline__ int take_row_ticket(const AttnParams& p, int64_t row, int pieces) {
+  unsigned long long* t = p.tickets + row;
+  unsigned long long cur = *reinterpret_cast<volatile unsigned long long*>(t);
+  for (int it = 0; it < 4096; ++it) {  // each failed swap means another CTA's succeeded
+    const unsigned long long nxt = ((cur >> 16) == p.epoch) ? cur + 1ull : ((p.epoch << 16) | 1ull);
+    const unsigned long long prev = atomicCAS(t, cur, nxt);
+    if (prev == cur) return (int)(nxt & 0xffffull) == pieces ? 1 : 0;
+    cur = prev;
+  }
+  return -1;
+}
+
+// Log-sum-exp merge of a row's pieces (m in log2 units) and the fp16 output
+// (attention.py:104-105: a row whose every key is masked outputs zeros).
+__device__ __forceinline__ void merge_row(const AttnParams& p, int64_t row, int tid, int nthr) {
+  int64_t c0;
+  const int np = row_pieces(p, row, &c0);
+  const int b = (int)(row / p.Hkv), kvh = (int)(row % p.Hkv);
+  const float NEG_INF = __int_as_float(0xff800000);
+  for (int idx = tid; idx < p.R * p.D; idx += nthr) {
+    const int r = idx / p.D, d = idx - r * p.D;
+    float M = NEG_INF;
+    for (int k = 0; k < np; ++k) M = fmaxf(M, __ldcg(&p.ws_ml[((row * p.max_pieces + k) * p.R + r) * 2]));
+    float O = 0.f, L = 0.f;
+    if (M != NEG_INF) {
+      for (int k = 0; k < np; ++k) {
+        const int64_t pb = (row * p.max_pieces + k) * p.R + r;
+        const float mk = __ldcg(&p.ws_ml[pb * 2]);
+        if (mk == NEG_INF) continue;
+        const float sc = ex2_approx(mk - M);
+        O = __fmaf_rn(__ldcg(&p.ws_o[pb * p.D + d]), sc, O);
+        L = __fmaf_rn(__ldcg(&p.ws_ml[pb * 2 + 1]), sc, L);
+      }
+    }
+    const float o = L > 0.f ? O / L : 0.f;
+    const int qi = r / p.G, g = r - qi * p.G;
+    p.out[(((size_t)b * p.Q + qi) * p.Hq + kvh * p.G + g) * p.D + d] = f2h(o);
+  }
+}
+
 template <int D, int RMAX, int NW, int LP>
 __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -125,14 +184,16 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
     *abort = 0;
     fence_mbar_init();
   }
-  {  // stage codebooks
+  __syncthreads();  // barriers initialised; the producer starts streaming at once
+  if (warp < NW) {  // consumer warps stage the codebooks meanwhile
     // PQ codebook [M][K][ds] staged code-major [K][M][ds]: one code's centroids
     // for all subspaces form one row, so a token's lanes read distinct banks.
     // Consecutive threads write consecutive shared addresses (i = (c*M + m)*per + part).
     const int nc = p.M * p.K;
+    const int nthr = NW * 32;
     if (p.ds % 8 == 0) {
       const int per = p.ds / 8;
-      for (int i = threadIdx.x; i < nc * per; i += blockDim.x) {
+      for (int i = threadIdx.x; i < nc * per; i += nthr) {
         const int cen = i / per, part = i - cen * per;
         const int c = cen / p.M, m = cen - c * p.M;
         reinterpret_cast<uint4*>(s_pq)[i] = __ldg(reinterpret_cast<const uint4*>(p.pq_cb) + (m * p.K + c) * per + part);
@@ -140,14 +201,14 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
     } else if (p.ds == 4) {
       // 4-dim presets also stage a copy with subspace pairs swapped (position m holds m^1)
       const bool sw = LP != kGeneric && Preset<LP>::DS == 4;
-      for (int i = threadIdx.x; i < nc; i += blockDim.x) {
+      for (int i = threadIdx.x; i < nc; i += nthr) {
         const int c = i / p.M, m = i - c * p.M;
         const uint2 v = __ldg(reinterpret_cast<const uint2*>(p.pq_cb) + m * p.K + c);
         reinterpret_cast<uint2*>(s_pq)[i] = v;
         if (sw) reinterpret_cast<uint2*>(s_pqsw)[i ^ 1] = v;
       }
     } else {
-      for (int i = threadIdx.x; i < nc * p.ds; i += blockDim.x) {
+      for (int i = threadIdx.x; i < nc * p.ds; i += nthr) {
         const int cen = i / p.ds, k = i - cen * p.ds;
         const int c = cen / p.M, m = cen - c * p.M;
         s_pq[i] = p.pq_cb[(m * p.K + c) * p.ds + k];
@@ -155,11 +216,11 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
     }
     if (p.rvq_smem && p.L > 0) {
       const int r16 = p.L * p.Kr * D / 8;
-      for (int i = threadIdx.x; i < r16; i += blockDim.x)
+      for (int i = threadIdx.x; i < r16; i += nthr)
         reinterpret_cast<uint4*>(s_rvq)[i] = __ldg(reinterpret_cast<const uint4*>(p.rvq_cb) + i);
     }
+    named_bar_sync(1, nthr);  // consumers only
   }
-  __syncthreads();
 
   const int64_t total = p.rows * p.W;
   const int64_t cta_a = (int64_t)blockIdx.x * p.per_cta;
@@ -445,53 +506,31 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
           p.ws_ml[(pbase + r) * 2 + 1] = Ls;
         }
       }
+      __threadfence();  // the partials are visible device-wide before the row ticket is taken
       if (!consumer_sync(sync_bar, sync_phase, abort)) {
         set_status(p, abort, kDevStatusTimeoutFull);
         break;
+      }
+      volatile int* merge_flag = abort + 1;
+      if (warp == 0 && lane == 0) {
+        int64_t c0;
+        const int t = take_row_ticket(p, row, row_pieces(p, row, &c0));
+        if (t < 0) set_status(p, abort, kDevStatusTicket);
+        *merge_flag = t > 0;
+      }
+      if (!consumer_sync(sync_bar, sync_phase, abort)) {
+        set_status(p, abort, kDevStatusTimeoutFull);
+        break;
+      }
+      if (*merge_flag) {  // this CTA finished the row: merge its pieces
+        __threadfence();
+        merge_row(p, row, threadIdx.x, NW * 32);
       }
     }
     if (++stage == p.stages) {
       stage = 0;
       phase ^= 1u;
     }
-  }
-}
-
-struct MergeParams {
-  const float* ws_o;
-  const float* ws_ml;
-  uint16_t* out;
-  int B, Q, Hq, Hkv, D, G, R, max_pieces;
-  int64_t W, per_cta;
-};
-
-// One CTA per row: combine the row's partials by log-sum-exp and normalise
-// (attention.py:104-105: a row whose every key is masked outputs zeros).
-__global__ void rfsn_merge_kernel(const __grid_constant__ MergeParams p) {
-  const int64_t row = blockIdx.x;
-  const int64_t c0 = (row * p.W) / p.per_cta;
-  const int64_t c1 = (row * p.W + p.W - 1) / p.per_cta;
-  const int np = (int)(c1 - c0 + 1);
-  const int b = (int)(row / p.Hkv), kvh = (int)(row % p.Hkv);
-  const float NEG_INF = __int_as_float(0xff800000);
-  for (int idx = threadIdx.x; idx < p.R * p.D; idx += blockDim.x) {
-    const int r = idx / p.D, d = idx - r * p.D;
-    float M = NEG_INF;
-    for (int k = 0; k < np; ++k) M = fmaxf(M, p.ws_ml[(((size_t)row * p.max_pieces + k) * p.R + r) * 2]);
-    float O = 0.f, L = 0.f;
-    if (M != NEG_INF) {
-      for (int k = 0; k < np; ++k) {
-        const size_t pb = ((size_t)row * p.max_pieces + k) * p.R + r;
-        const float mk = p.ws_ml[pb * 2];
-        if (mk == NEG_INF) continue;
-        const float s = ex2_approx(mk - M);
-        O = __fmaf_rn(p.ws_o[pb * p.D + d], s, O);
-        L = __fmaf_rn(p.ws_ml[pb * 2 + 1], s, L);
-      }
-    }
-    const float o = L > 0.f ? O / L : 0.f;
-    const int qi = r / p.G, g = r - qi * p.G;
-    p.out[(((size_t)b * p.Q + qi) * p.Hq + kvh * p.G + g) * p.D + d] = f2h(o);
   }
 }
 
@@ -556,6 +595,8 @@ static void fill_store(StoreDev& d, const rfsn_code_store& s) {
   d.cap = s.cap;
   d.rows = s.rows;
 }
+
+static size_t workspace_layout(AttnParams& p, void* base);
 
 static int make_plan(const rfsn_attn_args* a, const rfsn_quantizer* qz, Plan& pl) {
   int st = validate_quantizer(qz);
@@ -671,8 +712,32 @@ static int make_plan(const rfsn_attn_args* a, const rfsn_quantizer* qz, Plan& pl
     pl.grid = 0;
     p.max_pieces = 1;
   }
-  pl.ws_bytes = (size_t)p.rows * p.max_pieces * R * (p.D + 2) * sizeof(float) + 256;
+  if (p.max_pieces > 0xffff) return RFSN_ERR_UNSUPPORTED;  // tickets count pieces in 16 bits
+  pl.ws_bytes = workspace_layout(p, nullptr);
   return RFSN_OK;
+}
+
+// Workspace: per (row, piece, query row) partial (max, sum) pairs, then the
+// unnormalised outputs, then one 8-byte ticket per row.  Returns the bytes
+// needed; with a base pointer, binds the regions into the parameters.
+static size_t workspace_layout(AttnParams& p, void* base) {
+  const int64_t n_ml = align_up((int64_t)p.rows * p.max_pieces * p.R * 2, 64);
+  const int64_t n_o = align_up((int64_t)p.rows * p.max_pieces * p.R * p.D, 64);
+  if (base) {
+    p.ws_ml = reinterpret_cast<float*>(base);
+    p.ws_o = p.ws_ml + n_ml;
+    p.tickets = reinterpret_cast<unsigned long long*>(p.ws_o + n_o);
+  }
+  return (size_t)(n_ml + n_o) * sizeof(float) + (size_t)p.rows * 8 + 256;
+}
+
+// Call numbers tag row tickets (48 bits); the start is taken from the clock so
+// that stale ticket values from another process's use of the same memory are
+// not mistaken for a current launch's.
+static unsigned long long next_epoch() {
+  static std::atomic<unsigned long long> counter{
+      ((unsigned long long)std::chrono::steady_clock::now().time_since_epoch().count() & ((1ull << 40) - 1)) + 1};
+  return counter.fetch_add(1) & ((1ull << 48) - 1);
 }
 
 template <int D, int RMAX, int NW, int LP>
@@ -741,16 +806,10 @@ extern "C" int rfsn_decode_attention(const rfsn_attn_args* args, const rfsn_quan
   }
   if (!args->workspace || args->workspace_bytes < pl.ws_bytes) return RFSN_ERR_WORKSPACE_TOO_SMALL;
   if (reinterpret_cast<uintptr_t>(args->workspace) & 15) return RFSN_ERR_ALIGNMENT;
-  pl.p.ws_ml = reinterpret_cast<float*>(args->workspace);
-  pl.p.ws_o = pl.p.ws_ml + align_up((int64_t)p.rows * p.max_pieces * p.R * 2, 64);
-  st = check_cuda(launch(pl, s));
-  if (st != RFSN_OK) return st;
-  MergeParams mp;
-  mp.ws_o = pl.p.ws_o; mp.ws_ml = pl.p.ws_ml; mp.out = args->out;
-  mp.B = p.B; mp.Q = p.Q; mp.Hq = p.Hq; mp.Hkv = p.Hkv; mp.D = p.D; mp.G = p.G; mp.R = p.R;
-  mp.max_pieces = p.max_pieces; mp.W = p.W; mp.per_cta = p.per_cta;
-  rfsn_merge_kernel<<<(int)p.rows, 256, 0, s>>>(mp);
-  return check_cuda(cudaGetLastError());
+  workspace_layout(pl.p, args->workspace);
+  pl.p.out = args->out;
+  pl.p.epoch = next_epoch();
+  return check_cuda(launch(pl, s));
 }
 
 // ---------------------------------------------------------------------------
@@ -766,8 +825,10 @@ extern "C" int rfsn_decode_attention(const rfsn_attn_args* args, const rfsn_quan
 // up once per device, on the first call made with that device current, and
 // cached; that first call may load the module, so make it before capturing
 // the stream into a graph.  Nothing here calls an allocator.  Every partial
-// the merge kernel reads is written by the attention kernel of the same call,
-// so the buffer needs no clearing.  Calls that overlap in time on one device
+// the merge reads is written by the attention kernel of the same call, and the
+// per-row completion tickets carry each launch's own call number, so values
+// left by earlier (or aborted) calls are never counted: the buffer needs no
+// clearing.  Calls that overlap in time on one device
 // (different streams, or threads without ordering) share the buffer and race;
 // calls on one stream are ordered and safe.
 // ---------------------------------------------------------------------------
@@ -817,14 +878,8 @@ extern "C" int rfsn_decode_attention_noalloc(const rfsn_attn_args* args, const r
   void* scratch = nullptr;
   st = noalloc_scratch(&scratch);
   if (st != RFSN_OK) return st;
-  pl.p.ws_ml = reinterpret_cast<float*>(scratch);
-  pl.p.ws_o = pl.p.ws_ml + align_up((int64_t)p.rows * p.max_pieces * p.R * 2, 64);
-  st = check_cuda(launch(pl, s));
-  if (st != RFSN_OK) return st;
-  MergeParams mp;
-  mp.ws_o = pl.p.ws_o; mp.ws_ml = pl.p.ws_ml; mp.out = args->out;
-  mp.B = p.B; mp.Q = p.Q; mp.Hq = p.Hq; mp.Hkv = p.Hkv; mp.D = p.D; mp.G = p.G; mp.R = p.R;
-  mp.max_pieces = p.max_pieces; mp.W = p.W; mp.per_cta = p.per_cta;
-  rfsn_merge_kernel<<<(int)p.rows, 256, 0, s>>>(mp);
-  return check_cuda(cudaGetLastError());
+  workspace_layout(pl.p, scratch);
+  pl.p.out = args->out;
+  pl.p.epoch = next_epoch();
+  return check_cuda(launch(pl, s));
 }

@@ -22,6 +22,7 @@ constexpr uint64_t kWaitLimitNs = 1000ull * 1000ull * 1000ull;
 constexpr int kDevStatusTimeoutFull = 1;
 constexpr int kDevStatusTimeoutEmpty = 2;
 constexpr int kDevStatusBadSegment = 3;
+constexpr int kDevStatusTicket = 4;
 
 __device__ __forceinline__ uint64_t global_timer_ns() {
   uint64_t t;

@@ -166,7 +166,8 @@ typedef struct rfsn_attn_args {
   int32_t num_ctas;                /* 0 = one CTA per SM */
   void* workspace;                 /* device scratch, >= rfsn_attention_workspace_size() bytes */
   size_t workspace_bytes;
-  int32_t* device_status;          /* optional device int32: set non-zero by a kernel that hit a bounded-wait timeout */
+  int32_t* device_status;          /* optional device int32, set non-zero on a device-side failure: 1/2 a bounded
+                                      wait timed out, 4 a row ticket could not be taken */
 } rfsn_attn_args;
 
 /* Bytes of device workspace rfsn_decode_attention needs for these arguments. */
