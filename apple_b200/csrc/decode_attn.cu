@@ -47,6 +47,15 @@ namespace rfsn {
 constexpr int kMaxStages = 8;                // mbarrier slots reserved per CTA
 constexpr int kMaxStageBytes = 48 * 1024;    // upper bound of one ring stage
 constexpr int kNoLimit = 1 << 30;         // position limit of a row that sees every token
+
+// Tokens a consumer lane rebuilds per round (all loads in flight together) and
+// the per-warp scratch that goes with it: two sets of sparse scatter rows
+// [tokens per round][4 slots][D] fp16, reused as the warp's fp32 [RMAX][D]
+// partial output when a piece ends.
+// (Four tokens per round, measured on B200, ran 1.9x slower than two: the
+// extra live registers cost more than the added load overlap.)
+__host__ __device__ constexpr int tokens_per_round(int) { return 2; }
+__host__ __device__ constexpr int scratch_bytes(int D) { return 2 * tokens_per_round(D) * 4 * D * 2; }
 constexpr int64_t kMaxSmem = 227 * 1024;  // opt-in shared memory per CTA on sm_100
 
 struct SegDev {
@@ -234,8 +243,8 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
   if (warp == NW) {
     int stage = 0;
     uint32_t phase = 0;
-    bool inflight[kMaxStages] = {};
-    uint32_t inflight_parity[kMaxStages] = {};
+    uint32_t inflight = 0;         // bit s: stage s has copies issued
+    uint32_t inflight_parity = 0;  // bit s: the phase parity those copies complete
     bool ok = true;
     for (int64_t a = cta_a; a < cta_e && ok;) {
       const int64_t row = a / p.W;
@@ -309,8 +318,8 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
           first = false;
           __syncwarp();  // the barrier is armed before any copy can complete
           if (my_len) bulk_g2s(my_dst, my_src, my_len, &full_bar[stage]);
-          inflight[stage] = true;
-          inflight_parity[stage] = phase;
+          inflight |= 1u << stage;
+          inflight_parity = (inflight_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == p.stages) {
             stage = 0;
             phase ^= 1u;
@@ -328,9 +337,9 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
       // Abort path: wait (bounded) for the copies issued into each stage so the
       // CTA never retires with bulk copies still writing its shared memory.
       for (int k = 0; k < p.stages; ++k) {
-        if (!inflight[k]) continue;
+        if (!((inflight >> k) & 1u)) continue;
         const uint64_t t0 = global_timer_ns();
-        while (!mbar_try_wait(&full_bar[k], inflight_parity[k])) {
+        while (!mbar_try_wait(&full_bar[k], (inflight_parity >> k) & 1u)) {
           if (global_timer_ns() - t0 > kWaitLimitNs) break;
         }
       }
@@ -356,6 +365,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
   float* s_ml = reinterpret_cast<float*>(smem + p.smem_ml);  // [NW][RMAX][2]
   const float NEG_INF = __int_as_float(0xff800000);
   constexpr int NMMA = DPL / 4;  // K mma k-steps per row-step
+  constexpr int kTpr = tokens_per_round(D);
   constexpr int kBlock = LP != kGeneric ? Preset<LP>::BLOCK : 0;
   const int block_bytes = LP != kGeneric ? kBlock : p.lay.block_bytes;
 
@@ -444,10 +454,10 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
       const int pos_base = pos0 - lead + ch * kBlockTokens;
       if (kind == 0) {
         const size_t r0 = (size_t)ch * kBlockTokens * D;
-        process_block<D, RMAX, LP, true>(c, nullptr, hot_k + r0, hot_v + r0, t_lo, t_hi, pos_base, aq, acc, m_run,
+        process_block<D, RMAX, LP, true, kTpr>(c, nullptr, hot_k + r0, hot_v + r0, t_lo, t_hi, pos_base, aq, acc, m_run,
                                          l_run);
       } else {
-        process_block<D, RMAX, LP, false>(c, sb + ch * block_bytes, nullptr, nullptr, t_lo, t_hi, pos_base, aq,
+        process_block<D, RMAX, LP, false, kTpr>(c, sb + ch * block_bytes, nullptr, nullptr, t_lo, t_hi, pos_base, aq,
                                           acc, m_run, l_run);
       }
     }
@@ -667,7 +677,7 @@ static int make_plan(const rfsn_attn_args* a, const rfsn_quantizer* qz, Plan& pl
   // Per-warp scratch: 32*D bytes = fp16 sparse scatter rows [2][2][4][D], reused
   // for the warp's fp32 partial output [RMAX][D] (RMAX <= 8).
   p.stages = 3;
-  p.scr_bytes = 32 * p.D;
+  p.scr_bytes = scratch_bytes(p.D);
   for (int attempt = 0; attempt < 2; ++attempt) {
     pl.rvq_smem = attempt == 0 && p.L > 0 && rvq_bytes <= 64 * 1024;
     pl.lp = pick_preset(p, pl.rvq_smem);

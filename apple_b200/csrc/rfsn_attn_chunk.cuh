@@ -14,9 +14,9 @@
 // token's entries into a per-warp fp16 scratch row [slot][D] (a token's
 // entries have distinct dims), the warp syncs, and every lane reads back its
 // own dims as 16-byte loads, adds them with __hadd2 and zeroes them.  Two
-// scratch buffers alternate between consecutive rounds, so the __syncwarp of
-// one round orders the previous round's zeroing before the next writes to the
-// same buffer.  fp32 addition of two fp16 values followed by one rounding to
+// sets of scatter rows alternate between consecutive rounds, so the __syncwarp
+// of one round orders the previous round's zeroing before the next writes to
+// the same set.  fp32 addition of two fp16 values followed by one rounding to
 // fp16 equals the correctly rounded fp16 sum (24 >= 2*11+1 bits), so __hadd2
 // reproduces the fp32-then-round decode exactly.
 //
@@ -76,7 +76,7 @@ struct ChunkCtx {
   const uint16_t* pq_sel;  // this lane's copy: pq_cm, or the pair-swapped copy for odd slots (4-dim presets)
   const uint16_t* rvq_s;   // RVQ codebook [L][Kr][D] (shared, when staged)
   const uint16_t* rvq_g;   // RVQ codebook (global)
-  uint16_t* scratch;       // this warp's sparse scatter rows [2 buffers][2 tokens][4 slots][D] fp16
+  uint16_t* scratch;       // this warp's sparse scatter rows [2 sets][tokens per round][4 slots][D] fp16
   BlockLayout lay;         // runtime block layout (generic path)
   int M, K, ds, L, Kr, S, rvq_u16, rvq_smem, has_mask;
   int qp_lim;              // score lane's row: last visible position (causal), huge (not causal), very negative (unused row)
@@ -167,112 +167,120 @@ __device__ __forceinline__ void recon_generic(const ChunkCtx& c, const unsigned 
   }
 }
 
-// Sparse residual of two tokens (row-steps 2hs, 2hs+1): scatter, then add this lane's dims.
-template <int D, int LP>
-__device__ __forceinline__ void sparse_apply2(const ChunkCtx& c, const unsigned char* blk, int kv, const int* tb,
-                                              const bool* valid, int round, int slot, int j, int dim0,
-                                              uint32_t (*w)[D / 16]) {
+// Sparse residual of TPR tokens of this lane (token tb[i] = row-step rs0+i):
+// scatter every entry into this round's fp16 rows, sync the warp, then add
+// this lane's dims and zero them.  Rows of a round: [TPR][4 slots][D]; two
+// row sets alternate by round parity (the sync of a round orders the previous
+// round's zeroing before this round's writes into the same set).
+template <int D, int LP, int TPR>
+__device__ __forceinline__ void sparse_round(const ChunkCtx& c, const unsigned char* blk, int kv, const int* tb,
+                                             const bool* valid, int round, int slot, int j, int dim0,
+                                             uint32_t (*w)[D / 16]) {
   constexpr int DPL = D / 8;
-  uint16_t* buf = c.scratch + (round & 1) * (2 * 4 * D);
+  uint16_t* set = c.scratch + (round & 1) * (TPR * 4 * D);
 #pragma unroll
-  for (int u = 0; u < 2; ++u) {
-    uint16_t* row = buf + (u * 4 + slot) * D;
+  for (int i = 0; i < TPR; ++i) {
+    uint16_t* row = set + (i * 4 + slot) * D;
     if constexpr (LP != kGeneric) {
       using P = Preset<LP>;
       const unsigned char* f = blk + kv * P::FB;
-      const int idx = f[P::OSPI + tb[u] * P::S + j] & (D - 1);
-      const uint16_t val = *reinterpret_cast<const uint16_t*>(f + P::OSPV + (tb[u] * P::S + j) * 2);
-      row[idx] = valid[u] ? val : (uint16_t)0;
+      const int idx = f[P::OSPI + tb[i] * P::S + j] & (D - 1);
+      const uint16_t val = *reinterpret_cast<const uint16_t*>(f + P::OSPV + (tb[i] * P::S + j) * 2);
+      row[idx] = valid[i] ? val : (uint16_t)0;
     } else {
-      const unsigned char* spi = blk + c.lay.off[kv * 5 + 3] + tb[u] * c.S;
-      const uint16_t* spv = reinterpret_cast<const uint16_t*>(blk + c.lay.off[kv * 5 + 4]) + tb[u] * c.S;
-      for (int e = j; e < c.S; e += 8) row[spi[e] & (D - 1)] = valid[u] ? spv[e] : (uint16_t)0;
+      const unsigned char* spi = blk + c.lay.off[kv * 5 + 3] + tb[i] * c.S;
+      const uint16_t* spv = reinterpret_cast<const uint16_t*>(blk + c.lay.off[kv * 5 + 4]) + tb[i] * c.S;
+      for (int e = j; e < c.S; e += 8) row[spi[e] & (D - 1)] = valid[i] ? spv[e] : (uint16_t)0;
     }
   }
   __syncwarp();
 #pragma unroll
-  for (int u = 0; u < 2; ++u) {
-    uint16_t* src = buf + (u * 4 + slot) * D + dim0;
+  for (int i = 0; i < TPR; ++i) {
+    uint16_t* src = set + (i * 4 + slot) * D + dim0;
 #pragma unroll
     for (int g8 = 0; g8 < DPL / 8; ++g8) {
       uint4* p4 = reinterpret_cast<uint4*>(src + 8 * g8);
       const uint4 d = *p4;
-      w[u][4 * g8 + 0] = hadd2_u32(w[u][4 * g8 + 0], d.x);
-      w[u][4 * g8 + 1] = hadd2_u32(w[u][4 * g8 + 1], d.y);
-      w[u][4 * g8 + 2] = hadd2_u32(w[u][4 * g8 + 2], d.z);
-      w[u][4 * g8 + 3] = hadd2_u32(w[u][4 * g8 + 3], d.w);
+      w[i][4 * g8 + 0] = hadd2_u32(w[i][4 * g8 + 0], d.x);
+      w[i][4 * g8 + 1] = hadd2_u32(w[i][4 * g8 + 1], d.y);
+      w[i][4 * g8 + 2] = hadd2_u32(w[i][4 * g8 + 2], d.z);
+      w[i][4 * g8 + 3] = hadd2_u32(w[i][4 * g8 + 3], d.w);
       *p4 = make_uint4(0u, 0u, 0u, 0u);
     }
   }
 }
 
-// Rebuild this lane's dims of the two tokens tb[0], tb[1] (K or V fields).
-template <int D, int LP, bool DENSE>
-__device__ __forceinline__ void load_pair(const ChunkCtx& c, const unsigned char* blk, const uint16_t* dense,
-                                          int kv, const int* tb, const bool* valid, int t_lo, int round, int slot,
-                                          int j, int dim0, bool odd, uint32_t (*w)[D / 16]) {
+// Rebuild this lane's dims of its TPR tokens tb[i] (K or V fields), all loads
+// of the round issued before any is used.
+template <int D, int LP, bool DENSE, int TPR>
+__device__ __forceinline__ void load_round(const ChunkCtx& c, const unsigned char* blk, const uint16_t* dense,
+                                           int kv, const int* tb, const bool* valid, int t_lo, int round, int slot,
+                                           int j, int dim0, bool odd, uint32_t (*w)[D / 16]) {
   constexpr int DPL = D / 8;
 #pragma unroll
-  for (int u = 0; u < 2; ++u) {
+  for (int i = 0; i < TPR; ++i) {
     if constexpr (DENSE) {
-      load_dense<DPL>(dense + (valid[u] ? tb[u] : t_lo) * D + dim0, w[u]);
+      load_dense<DPL>(dense + (valid[i] ? tb[i] : t_lo) * D + dim0, w[i]);
     } else if constexpr (LP != kGeneric) {
-      recon_fast<LP>(c, blk, kv, tb[u], j, odd, w[u]);
+      recon_fast<LP>(c, blk, kv, tb[i], j, odd, w[i]);
     } else {
-      recon_generic<D>(c, blk, kv, tb[u], dim0, w[u]);
+      recon_generic<D>(c, blk, kv, tb[i], dim0, w[i]);
     }
   }
   if constexpr (!DENSE) {
-    if (c.S > 0) sparse_apply2<D, LP>(c, blk, kv, tb, valid, round, slot, j, dim0, w);
+    if (c.S > 0) sparse_round<D, LP, TPR>(c, blk, kv, tb, valid, round, slot, j, dim0, w);
   }
 }
 
 // One 16-token chunk: K scores on tensor cores, online softmax, V accumulation.
 // blk: the block's bytes (code tiles); dense_k/dense_v: the chunk's 16 hot rows
-// (dense tiles).  Valid tokens are [t_lo, t_hi); token tb is at position pos_base + tb.
-template <int D, int RMAX, int LP, bool DENSE>
+// (dense tiles).  Valid tokens are [t_lo, t_hi); token tb is at position
+// pos_base + tb.  TPR tokens per lane are loaded per round (4 / TPR rounds per
+// phase); a round's loads are all in flight before its arithmetic.
+template <int D, int RMAX, int LP, bool DENSE, int TPR>
 __device__ __forceinline__ void process_block(const ChunkCtx& c, const unsigned char* blk, const uint16_t* dense_k,
                                               const uint16_t* dense_v, int t_lo, int t_hi, int pos_base,
                                               const uint32_t (*aq)[4], float (*acc)[D / 8], float& m_run,
                                               float& l_run) {
   constexpr int DPL = D / 8;
   constexpr int NMMA = DPL / 4;
+  constexpr int NR = 4 / TPR;  // rounds per phase
   const float NEG_INF = __int_as_float(0xff800000);
   const int lane = threadIdx.x & 31;
   const int slot = lane >> 3, j = lane & 7, dim0 = j * DPL;
   const int sslot = lane & 3;
   const bool odd = slot & 1;
-  // score lane (row srow, token slot sslot): visible tokens are [t_lo, s_hi)
+  // score lane (row lane/4, token slot sslot): visible tokens are [t_lo, s_hi)
   const int s_hi = min(t_hi, c.qp_lim - pos_base + 1);
 
   // ---------------- scores ----------------
   float sc[4];
 #pragma unroll
-  for (int hs = 0; hs < 2; ++hs) {
-    int tb[2];
-    bool valid[2];
+  for (int rr = 0; rr < NR; ++rr) {
+    int tb[TPR];
+    bool valid[TPR];
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      tb[u] = 4 * (2 * hs + u) + slot;
-      valid[u] = tb[u] >= t_lo && tb[u] < t_hi;
+    for (int i = 0; i < TPR; ++i) {
+      tb[i] = 4 * (rr * TPR + i) + slot;
+      valid[i] = tb[i] >= t_lo && tb[i] < t_hi;
     }
-    uint32_t w[2][DPL / 2];
-    load_pair<D, LP, DENSE>(c, blk, dense_k, 0, tb, valid, t_lo, hs, slot, j, dim0, odd, w);
-    float cfr[2][4];
+    uint32_t w[TPR][DPL / 2];
+    load_round<D, LP, DENSE, TPR>(c, blk, dense_k, 0, tb, valid, t_lo, rr, slot, j, dim0, odd, w);
+    float cfr[TPR][4];
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      cfr[u][0] = cfr[u][1] = cfr[u][2] = cfr[u][3] = 0.f;
+    for (int i = 0; i < TPR; ++i) {
+      cfr[i][0] = cfr[i][1] = cfr[i][2] = cfr[i][3] = 0.f;
 #pragma unroll
-      for (int s = 0; s < NMMA; ++s) mma16816(cfr[u], aq[s], w[u][2 * s], w[u][2 * s + 1]);
+      for (int s = 0; s < NMMA; ++s) mma16816(cfr[i], aq[s], w[i][2 * s], w[i][2 * s + 1]);
     }
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int stb = 4 * (2 * hs + u) + sslot;
-      sc[2 * hs + u] = (stb >= t_lo && stb < s_hi) ? (cfr[u][0] + cfr[u][3]) * c.sl2 : NEG_INF;
+    for (int i = 0; i < TPR; ++i) {
+      const int stb = 4 * (rr * TPR + i) + sslot;
+      sc[rr * TPR + i] = (stb >= t_lo && stb < s_hi) ? (cfr[i][0] + cfr[i][3]) * c.sl2 : NEG_INF;
     }
   }
 
-  // ---------------- online softmax of row srow over the 16 tokens ----------------
+  // ---------------- online softmax of row lane/4 over the 16 tokens ----------------
   float cmax = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
   cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 1));
   cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 2));
@@ -301,27 +309,28 @@ __device__ __forceinline__ void process_block(const ChunkCtx& c, const unsigned 
 
   // ---------------- values ----------------
 #pragma unroll
-  for (int hs = 0; hs < 2; ++hs) {
-    int tb[2];
-    bool valid[2];
-    float pv[2][RMAX];
+  for (int rr = 0; rr < NR; ++rr) {
+    int tb[TPR];
+    bool valid[TPR];
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      tb[u] = 4 * (2 * hs + u) + slot;
-      valid[u] = tb[u] >= t_lo && tb[u] < t_hi;
-#pragma unroll
-      for (int r = 0; r < RMAX; ++r) pv[u][r] = __shfl_sync(0xffffffffu, pr[2 * hs + u], 4 * r + slot);
+    for (int i = 0; i < TPR; ++i) {
+      tb[i] = 4 * (rr * TPR + i) + slot;
+      valid[i] = tb[i] >= t_lo && tb[i] < t_hi;
     }
-    uint32_t w[2][DPL / 2];
-    load_pair<D, LP, DENSE>(c, blk, dense_v, 1, tb, valid, t_lo, hs, slot, j, dim0, odd, w);
+    uint32_t w[TPR][DPL / 2];
+    load_round<D, LP, DENSE, TPR>(c, blk, dense_v, 1, tb, valid, t_lo, NR + rr, slot, j, dim0, odd, w);
 #pragma unroll
-    for (int u = 0; u < 2; ++u)
+    for (int i = 0; i < TPR; ++i) {
+      float pv[RMAX];
 #pragma unroll
-      for (int i = 0; i < DPL / 2; ++i) {
-        const float2 v2 = __half22float2(*reinterpret_cast<const __half2*>(&w[u][i]));
+      for (int r = 0; r < RMAX; ++r) pv[r] = __shfl_sync(0xffffffffu, pr[rr * TPR + i], 4 * r + slot);
 #pragma unroll
-        for (int r = 0; r < RMAX; ++r) ffma2(acc[r][2 * i], acc[r][2 * i + 1], pv[u][r], v2.x, v2.y);
+      for (int k = 0; k < DPL / 2; ++k) {
+        const float2 v2 = __half22float2(*reinterpret_cast<const __half2*>(&w[i][k]));
+#pragma unroll
+        for (int r = 0; r < RMAX; ++r) ffma2(acc[r][2 * k], acc[r][2 * k + 1], pv[r], v2.x, v2.y);
       }
+    }
   }
 }
 

@@ -113,77 +113,90 @@ def build_workload(device, seed):
 
 
 class ClockSampler:
-    """SM clock and throttle-reason samples (NVML) from a polling thread during the timed region.
+    """SM clock and throttle-reason samples (NVML) during the timed region.
 
-    The torch device is matched to its NVML handle by UUID (NVML ignores
-    CUDA_VISIBLE_DEVICES).  Reasons reported: hw_slowdown, hw_thermal_slowdown,
-    sw_thermal_slowdown, sw_power_cap.  Falls back to no samples when NVML is absent.
+    Sampling runs in a child process (``bench.py --clock-sampler``), so the
+    timed loop's host thread cannot starve it.  The torch device is matched to
+    its NVML handle by UUID, else PCI bus id (NVML ignores CUDA_VISIBLE_DEVICES).
+    Reasons reported: hw_slowdown, hw_thermal_slowdown, sw_thermal_slowdown,
+    sw_power_cap.
     """
 
     REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4}
 
-    def __init__(self, device, period_s: float = 0.002):
+    def __init__(self, device):
         self.device = device
-        self.period = period_s
-        self.samples = []
-        self.max_mhz = None
+        self.proc = None
+        self.path = ROOT / "gpurun_out" / f"clocks_{os.getpid()}.json"
         self.error = None
-        self._stop = None
-        self._thread = None
 
-    def _handle(self):
-        import pynvml
+    def _ident(self) -> str:
         import torch
-        pynvml.nvmlInit()
         props = torch.cuda.get_device_properties(self.device)
         uuid = str(getattr(props, "uuid", "") or "")
-        if uuid:
-            try:
-                return pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
-            except Exception:
-                pass
         bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
-        return pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        return f"{uuid},{bus}"
 
     def __enter__(self):
-        import threading
+        import subprocess
         try:
-            import pynvml
-            h = self._handle()
-            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
-            get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
-                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
-        except Exception as e:  # NVML missing: report no samples
+            self.path.parent.mkdir(exist_ok=True)
+            self.proc = subprocess.Popen([sys.executable, str(Path(__file__).resolve()), "--clock-sampler",
+                                          self._ident(), str(self.path)], stdout=subprocess.PIPE, text=True)
+            line = self.proc.stdout.readline().strip()  # "ready" once NVML answers
+            if line != "ready":
+                self.error = f"sampler did not start: {line!r}"
+        except Exception as e:
             self.error = str(e)
-            return self
-        self._stop = threading.Event()
-
-        def poll():
-            while not self._stop.is_set():
-                try:
-                    self.samples.append((float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)), int(get_reasons(h))))
-                except Exception as e:  # pragma: no cover
-                    self.error = str(e)
-                    return
-                time.sleep(self.period)
-
-        self._thread = threading.Thread(target=poll, daemon=True)
-        self._thread.start()
         return self
 
     def __exit__(self, *a):
-        if self._thread is not None:
-            self._stop.set()
-            self._thread.join(timeout=5)
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=10)
+            except Exception:
+                self.proc.kill()
 
     def summary(self) -> dict:
-        sm = [c for c, _ in self.samples]
-        reasons = sorted({name for _, bits in self.samples for name, bit in self.REASONS.items() if bits & bit})
-        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz, "reasons": reasons,
-               "samples": len(sm), "source": "nvml"}
+        try:
+            d = json.loads(self.path.read_text())
+            sm = [c for c, _ in d["samples"]]
+            reasons = sorted({n for _, bits in d["samples"] for n, bit in self.REASONS.items() if bits & bit})
+            out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": d.get("max_mhz"),
+                   "reasons": reasons, "samples": len(sm), "source": "nvml (sampler process, 1 ms)"}
+        except Exception as e:
+            out = {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "error": str(e)}
         if self.error:
             out["error"] = self.error
         return out
+
+
+def clock_sampler_main(ident: str, path: str) -> None:
+    """Child process: poll NVML every millisecond until SIGTERM, then write the samples."""
+    import signal
+    import pynvml
+    stop = []
+    signal.signal(signal.SIGTERM, lambda *a: stop.append(1))
+    pynvml.nvmlInit()
+    uuid, bus = ident.split(",", 1)
+    h = None
+    if uuid:
+        try:
+            h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        except Exception:
+            h = None
+    if h is None:
+        h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+    get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+        pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+    max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+    samples = []
+    print("ready", flush=True)
+    while not stop:
+        samples.append((float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)), int(get_reasons(h))))
+        time.sleep(0.001)
+    Path(path).write_text(json.dumps({"max_mhz": max_mhz, "samples": samples}))
 
 
 # ---------------------------------------------------------------------------
@@ -484,6 +497,9 @@ def run_b200(args) -> None:
 
 
 def main() -> None:
+    if len(sys.argv) == 4 and sys.argv[1] == "--clock-sampler":
+        clock_sampler_main(sys.argv[2], sys.argv[3])
+        return
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
