@@ -20,6 +20,7 @@
 
 #include "rfsn_api_internal.h"
 #include "rfsn_decode.cuh"
+#include "rfsn_encode_tc.h"
 
 namespace rfsn {
 
@@ -317,6 +318,11 @@ extern "C" int rfsn_encode(const rfsn_quantizer* qz, const uint16_t* x, int64_t 
   if (((uintptr_t)x & 15) || (stride_b & 7) || (stride_t & 7) || (stride_h & 7)) return RFSN_ERR_ALIGNMENT;
   const int64_t nvec = batch * tokens * heads;
   if (nvec == 0) return RFSN_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // tensor-core encoder for the configurations it covers (bit-identical codes up to fp32 ties)
+  if (encode_tc_supported(qz) && !((uintptr_t)residual_out & 15))
+    return encode_tc_launch(qz, x, batch, tokens, heads, stride_b, stride_t, stride_h, dst, kv, dst_slot, dst_first,
+                            residual_out, s);
 
   EncodeParams p{};
   p.x = x; p.batch = batch; p.tokens = tokens; p.heads = heads;
@@ -336,7 +342,6 @@ extern "C" int rfsn_encode(const rfsn_quantizer* qz, const uint16_t* x, int64_t 
   if (p.rvq_smem) smem += rvq_bytes;
   if (smem > 200 * 1024) return RFSN_ERR_UNSUPPORTED;
   const int blocks = (int)((nvec + kEncThreads - 1) / kEncThreads);
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   cudaError_t e;
   if (p.D == 64) {
     e = cudaFuncSetAttribute(encode_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

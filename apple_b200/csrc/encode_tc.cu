@@ -1,0 +1,418 @@
+// encode_tc.cu — spill encoder with nearest-centroid dot products on tensor cores.
+//
+// Same results as encode.cu's per-thread encoder (HybridQuantizerMLX.encode,
+// quantization.py:124-144 and 206-252, plus the top-S sparse extension) for
+// D = 64, 4- or 8-dim PQ subspaces, K <= 256 PQ centroids, at most one RVQ
+// layer of Kr <= 256 rows (uint8 codes).  A warp encodes 16 vectors at a time:
+//
+//   PQ   per subspace m: mma.m16n8k8 gives x_m . c for 16 vectors x 8 centroids
+//        (4-dim subspaces: the other half of k is zero in B); the epilogue forms
+//        d = (|x_m|^2 - 2 x_m.c) + |c|^2 in fp32 exactly as the reference does
+//        and keeps the first minimum (four independent chains per lane, merged
+//        by distance then index, then across the lane quad by shuffles).
+//   RVQ  residual r = fp16(x - c) (one rounding of the exact difference), norm
+//        gate sqrt(sum r^2) > threshold, then mma.m16n8k16 over the 64 dims for
+//        r . R[c] and the same epilogue.
+//   sparse / stores: one lane per vector, CUDA cores.
+//
+// Products of fp16 values are exact in fp32, so d differs from the reference
+// only through the dot products' summation order: codes can differ only where
+// two candidates tie to fp32 rounding.  Operand fragments are read straight
+// from shared memory with 32-bit loads; the x tile, residual tile and RVQ
+// codebook rows are stored with their 16-byte chunks XOR-swizzled by row, so
+// the 8 rows read by one load instruction fall in distinct banks.
+#include <cuda_runtime.h>
+
+#include "rfsn_api_internal.h"
+#include "rfsn_attn_util.cuh"
+#include "rfsn_common.cuh"
+#include "rfsn_encode_tc.h"
+
+namespace rfsn {
+
+constexpr int kTcWarps = 16;  // warps per CTA (one CTA per SM)
+constexpr int kTcD = 64;
+
+struct EncTcParams {
+  const uint16_t* x;
+  int64_t batch, tokens, heads, sb, st, sh, nvec;
+  uint8_t* data;
+  BlockLayout lay;
+  int kv;
+  int64_t cap, rows, slot, first;
+  uint16_t* residual_out;
+  const uint16_t* pq_cb;
+  const uint16_t* rvq_cb;
+  int M, K, L, Kr, S;
+  float thr;
+  int smem_pq, smem_pqcc, smem_rvq, smem_rcc, smem_warp, warp_bytes;
+};
+
+__device__ __forceinline__ void mma1688(float c[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm("mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(b0));
+}
+
+// 16-byte chunk q of row i of a swizzled [rows][64] fp16 tile (128 B rows).
+__device__ __forceinline__ int swz(int i, int q) { return i * 8 + (q ^ (i & 7)); }
+
+// Running first-minimum: take (d, idx) if strictly smaller.
+__device__ __forceinline__ void take_min(float d, int idx, float& best, int& bi) {
+  const bool p = d < best;
+  best = p ? d : best;
+  bi = p ? idx : bi;
+}
+
+// Merge two first-minima of disjoint index sets: smaller distance, then smaller index.
+__device__ __forceinline__ void merge_min(float& best, int& bi, float d2, int i2) {
+  const bool p = d2 < best || (d2 == best && i2 < bi);
+  best = p ? d2 : best;
+  bi = p ? i2 : bi;
+}
+
+// Lane-quad reduction (lanes 4r .. 4r+3 hold candidates for the same row).
+__device__ __forceinline__ void quad_min(float& best, int& bi) {
+#pragma unroll
+  for (int o = 1; o <= 2; o <<= 1) {
+    const float d2 = __shfl_xor_sync(0xffffffffu, best, o);
+    const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+    merge_min(best, bi, d2, i2);
+  }
+}
+
+template <int DS>
+__global__ void __launch_bounds__(kTcWarps * 32, 1) encode_tc_kernel(const __grid_constant__ EncTcParams p) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  constexpr int M = kTcD / DS;
+  uint16_t* s_pq = reinterpret_cast<uint16_t*>(smem + p.smem_pq);     // [M][K][DS] (global layout)
+  float* s_pqcc = reinterpret_cast<float*>(smem + p.smem_pqcc);       // [M][K]
+  uint4* s_rvq = reinterpret_cast<uint4*>(smem + p.smem_rvq);         // [Kr][8 chunks] swizzled
+  float* s_rcc = reinterpret_cast<float*>(smem + p.smem_rcc);         // [Kr]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nthr = blockDim.x;
+  const int K = p.K, Kr = p.Kr;
+
+  // ---- stage codebooks and their squared norms (sequential fp32 sums) ----
+  for (int i = threadIdx.x; i < M * K * DS / 8; i += nthr)
+    reinterpret_cast<uint4*>(s_pq)[i] = __ldg(reinterpret_cast<const uint4*>(p.pq_cb) + i);
+  for (int i = threadIdx.x; i < M * K; i += nthr) {
+    const uint16_t* c = p.pq_cb + (size_t)i * DS;
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < DS; ++k) {
+      const float v = h2f(c[k]);
+      s = __fmaf_rn(v, v, s);
+    }
+    s_pqcc[i] = s;
+  }
+  if (p.L > 0) {
+    for (int i = threadIdx.x; i < Kr * 8; i += nthr) {
+      const int c = i >> 3, q = i & 7;
+      s_rvq[swz(c, q)] = __ldg(reinterpret_cast<const uint4*>(p.rvq_cb) + i);
+    }
+    for (int i = threadIdx.x; i < Kr; i += nthr) {
+      const uint16_t* c = p.rvq_cb + (size_t)i * kTcD;
+      float s = 0.f;
+      for (int k = 0; k < kTcD; ++k) {
+        const float v = h2f(c[k]);
+        s = __fmaf_rn(v, v, s);
+      }
+      s_rcc[i] = s;
+    }
+  }
+  __syncthreads();
+
+  // per-warp tiles
+  unsigned char* wb = smem + p.smem_warp + (size_t)warp * p.warp_bytes;
+  uint4* xt = reinterpret_cast<uint4*>(wb);                    // [16][8 chunks] swizzled x
+  uint4* rt = xt + 16 * 8;                                     // [16][8 chunks] swizzled residual
+  float* s_xsq = reinterpret_cast<float*>(rt + 16 * 8);        // [16][M]
+  float* s_rr = s_xsq + 16 * M;                                // [16]
+  uint8_t* s_code = reinterpret_cast<uint8_t*>(s_rr + 16);    // [16][M]
+  uint8_t* s_rcode = s_code + 16 * M;                          // [16]
+  uint8_t* s_act = s_rcode + 16;                               // [16]
+
+  const int r0 = lane >> 2, qd = lane & 3;
+  const float INF = __int_as_float(0x7f800000);
+  const int64_t ngroups = (p.nvec + 15) / 16;
+
+  for (int64_t g = (int64_t)blockIdx.x * kTcWarps + warp; g < ngroups; g += (int64_t)gridDim.x * kTcWarps) {
+    // ---- x tile ----
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      const int i = (lane >> 3) + 4 * s, q = lane & 7;
+      const int64_t v = g * 16 + i;
+      uint4 val = make_uint4(0u, 0u, 0u, 0u);
+      if (v < p.nvec) {
+        const int64_t h = v % p.heads, t = (v / p.heads) % p.tokens, b = v / (p.heads * p.tokens);
+        val = __ldg(reinterpret_cast<const uint4*>(p.x + b * p.sb + t * p.st + h * p.sh) + q);
+      }
+      xt[swz(i, q)] = val;
+    }
+    __syncwarp();
+    // |x_m|^2 per (vector, subspace), sequential fp32 (quantization.py:94)
+    for (int idx = lane; idx < 16 * M; idx += 32) {
+      const int i = idx / M, m = idx - i * M;
+      const uint16_t* xr = reinterpret_cast<const uint16_t*>(&xt[swz(i, (m * DS) >> 3)]) + ((m * DS) & 7);
+      float s = 0.f;
+#pragma unroll
+      for (int k = 0; k < DS; ++k) {
+        const float v = h2f(xr[k]);
+        s = __fmaf_rn(v, v, s);
+      }
+      s_xsq[idx] = s;
+    }
+    __syncwarp();
+
+    // ---- PQ: per-subspace argmin over K centroids ----
+    for (int m = 0; m < M; ++m) {
+      const int chunk = (m * DS) >> 3;
+      const uint32_t* x0 = reinterpret_cast<const uint32_t*>(&xt[swz(r0, chunk)]);
+      const uint32_t* x1 = reinterpret_cast<const uint32_t*>(&xt[swz(r0 + 8, chunk)]);
+      const uint32_t a0 = x0[qd], a1 = x1[qd];
+      const float xx0 = s_xsq[r0 * M + m], xx1 = s_xsq[(r0 + 8) * M + m];
+      // B lanes that carry this subspace's dims (4-dim subspaces fill half of k)
+      const bool bl = DS == 8 || ((qd >> 1) == (m & 1));
+      const uint32_t* cbm = reinterpret_cast<const uint32_t*>(s_pq + (size_t)m * K * DS);
+      const float* ccm = s_pqcc + m * K;
+      float b00 = INF, b01 = INF, b10 = INF, b11 = INF;  // rows r0 / r0+8, column parity 0 / 1
+      int i00 = 0, i01 = 0, i10 = 0, i11 = 0;
+#pragma unroll 4
+      for (int nt = 0; nt < K / 8; ++nt) {
+        const int cb = nt * 8 + r0;  // centroid of this lane's B column
+        const uint32_t b = bl ? cbm[(cb * DS >> 1) + (DS == 8 ? qd : (qd & 1))] : 0u;
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
+        mma1688(c, a0, a1, b);
+        const int code = nt * 8 + 2 * qd;
+        const float2 cc = *reinterpret_cast<const float2*>(ccm + code);
+        take_min(__fadd_rn(__fmaf_rn(-2.f, c[0], xx0), cc.x), code, b00, i00);
+        take_min(__fadd_rn(__fmaf_rn(-2.f, c[1], xx0), cc.y), code + 1, b01, i01);
+        take_min(__fadd_rn(__fmaf_rn(-2.f, c[2], xx1), cc.x), code, b10, i10);
+        take_min(__fadd_rn(__fmaf_rn(-2.f, c[3], xx1), cc.y), code + 1, b11, i11);
+      }
+      merge_min(b00, i00, b01, i01);
+      merge_min(b10, i10, b11, i11);
+      quad_min(b00, i00);
+      quad_min(b10, i10);
+      if (qd == 0) {
+        s_code[r0 * M + m] = (uint8_t)i00;
+        s_code[(r0 + 8) * M + m] = (uint8_t)i10;
+      }
+    }
+    __syncwarp();
+
+    // ---- residual r = fp16(x - c): one rounding of the exact difference ----
+    for (int idx = lane; idx < 16 * 8; idx += 32) {
+      const int i = idx >> 3, q = idx & 7;
+      const uint4 xv = xt[swz(i, q)];
+      uint4 cv;
+      if constexpr (DS == 8) {
+        cv = *reinterpret_cast<const uint4*>(s_pq + ((size_t)q * K + s_code[i * M + q]) * 8);
+      } else {
+        const uint2 lo = *reinterpret_cast<const uint2*>(s_pq + ((size_t)(2 * q) * K + s_code[i * M + 2 * q]) * 4);
+        const uint2 hi =
+            *reinterpret_cast<const uint2*>(s_pq + ((size_t)(2 * q + 1) * K + s_code[i * M + 2 * q + 1]) * 4);
+        cv = make_uint4(lo.x, lo.y, hi.x, hi.y);
+      }
+      uint4 rv;
+      rv.x = hsub2_u32(xv.x, cv.x); rv.y = hsub2_u32(xv.y, cv.y);
+      rv.z = hsub2_u32(xv.z, cv.z); rv.w = hsub2_u32(xv.w, cv.w);
+      rt[swz(i, q)] = rv;
+      const int64_t v = g * 16 + i;
+      if (p.residual_out && v < p.nvec) {
+        const int64_t h = v % p.heads, t = (v / p.heads) % p.tokens, b = v / (p.heads * p.tokens);
+        reinterpret_cast<uint4*>(p.residual_out + b * p.sb + t * p.st + h * p.sh)[q] = rv;
+      }
+    }
+    __syncwarp();
+
+    // ---- RVQ, one layer (quantization.py:216-250) ----
+    if (p.L > 0) {
+      if (lane < 16) {  // norm gate, sequential fp32
+        float nn = 0.f;
+        for (int q = 0; q < 8; ++q) {
+          const uint4 rv = rt[swz(lane, q)];
+          const uint32_t w4[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[k]));
+            nn = __fmaf_rn(f.x, f.x, nn);
+            nn = __fmaf_rn(f.y, f.y, nn);
+          }
+        }
+        s_rr[lane] = nn;
+        s_act[lane] = __fsqrt_rn(nn) > p.thr ? 1 : 0;
+      }
+      __syncwarp();
+      uint32_t a[4][4];
+#pragma unroll
+      for (int s = 0; s < 4; ++s) {
+        a[s][0] = reinterpret_cast<const uint32_t*>(&rt[swz(r0, 2 * s)])[qd];
+        a[s][1] = reinterpret_cast<const uint32_t*>(&rt[swz(r0 + 8, 2 * s)])[qd];
+        a[s][2] = reinterpret_cast<const uint32_t*>(&rt[swz(r0, 2 * s + 1)])[qd];
+        a[s][3] = reinterpret_cast<const uint32_t*>(&rt[swz(r0 + 8, 2 * s + 1)])[qd];
+      }
+      const float rr0 = s_rr[r0], rr1 = s_rr[r0 + 8];
+      float b00 = INF, b01 = INF, b10 = INF, b11 = INF;
+      int i00 = 0, i01 = 0, i10 = 0, i11 = 0;
+#pragma unroll 2
+      for (int nt = 0; nt < Kr / 8; ++nt) {
+        const int cb = nt * 8 + r0;
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+          const uint32_t bb0 = reinterpret_cast<const uint32_t*>(&s_rvq[swz(cb, 2 * s)])[qd];
+          const uint32_t bb1 = reinterpret_cast<const uint32_t*>(&s_rvq[swz(cb, 2 * s + 1)])[qd];
+          mma16816(c, a[s], bb0, bb1);
+        }
+        const int code = nt * 8 + 2 * qd;
+        const float2 cc = *reinterpret_cast<const float2*>(s_rcc + code);
+        take_min(__fadd_rn(__fmaf_rn(-2.f, c[0], rr0), cc.x), code, b00, i00);
+        take_min(__fadd_rn(__fmaf_rn(-2.f, c[1], rr0), cc.y), code + 1, b01, i01);
+        take_min(__fadd_rn(__fmaf_rn(-2.f, c[2], rr1), cc.x), code, b10, i10);
+        take_min(__fadd_rn(__fmaf_rn(-2.f, c[3], rr1), cc.y), code + 1, b11, i11);
+      }
+      merge_min(b00, i00, b01, i01);
+      merge_min(b10, i10, b11, i11);
+      quad_min(b00, i00);
+      quad_min(b10, i10);
+      if (qd == 0) {
+        s_rcode[r0] = s_act[r0] ? (uint8_t)i00 : 0;
+        s_rcode[r0 + 8] = s_act[r0 + 8] ? (uint8_t)i10 : 0;
+      }
+      __syncwarp();
+    }
+
+    // ---- sparse top-S of the fp16 decode error, and the code stores: one lane per vector ----
+    if (lane < 16) {
+      const int i = lane;
+      const int64_t v = g * 16 + i;
+      if (v < p.nvec) {
+        const int64_t h = v % p.heads, t = (v / p.heads) % p.tokens, b = v / (p.heads * p.tokens);
+        const int64_t row = b * p.heads + h, tok = p.first + t;
+        const int fk = p.kv * 5;
+        uint8_t* f_pq = p.data + field_byte(p.lay, p.rows, p.cap, p.slot, row, tok, fk + 0);
+        for (int m = 0; m < M; ++m) f_pq[m] = s_code[i * M + m];
+        if (p.L > 0) {
+          p.data[field_byte(p.lay, p.rows, p.cap, p.slot, row, tok, fk + 1)] = s_rcode[i];
+          p.data[field_byte(p.lay, p.rows, p.cap, p.slot, row, tok, fk + 2)] = s_act[i];
+        }
+        if (p.S > 0) {
+          uint8_t* f_spi = p.data + field_byte(p.lay, p.rows, p.cap, p.slot, row, tok, fk + 3);
+          uint16_t* f_spv =
+              reinterpret_cast<uint16_t*>(p.data + field_byte(p.lay, p.rows, p.cap, p.slot, row, tok, fk + 4));
+          // err = x - fp16(pq + rvq) in fp32 (quantization.py:310-319 decode, then the error)
+          float err[kTcD];
+          const bool act = p.L > 0 && s_act[i];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const uint4 xv = xt[swz(i, q)];
+            uint4 cv;  // the decode: PQ centroid, plus the RVQ row in fp16 when active
+            if constexpr (DS == 8) {
+              cv = *reinterpret_cast<const uint4*>(s_pq + ((size_t)q * K + s_code[i * M + q]) * 8);
+            } else {
+              const uint2 lo =
+                  *reinterpret_cast<const uint2*>(s_pq + ((size_t)(2 * q) * K + s_code[i * M + 2 * q]) * 4);
+              const uint2 hi =
+                  *reinterpret_cast<const uint2*>(s_pq + ((size_t)(2 * q + 1) * K + s_code[i * M + 2 * q + 1]) * 4);
+              cv = make_uint4(lo.x, lo.y, hi.x, hi.y);
+            }
+            if (act) {
+              const uint4 rr = s_rvq[swz(s_rcode[i], q)];
+              cv.x = hadd2_u32(cv.x, rr.x); cv.y = hadd2_u32(cv.y, rr.y);
+              cv.z = hadd2_u32(cv.z, rr.z); cv.w = hadd2_u32(cv.w, rr.w);
+            }
+            const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+            const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float2 xf = __half22float2(*reinterpret_cast<const __half2*>(&xw[k]));
+              const float2 cf = __half22float2(*reinterpret_cast<const __half2*>(&cw[k]));
+              err[8 * q + 2 * k] = __fsub_rn(xf.x, cf.x);
+              err[8 * q + 2 * k + 1] = __fsub_rn(xf.y, cf.y);
+            }
+          }
+          unsigned long long taken = 0ull;
+          for (int s = 0; s < p.S; ++s) {  // largest |err| not yet taken, ties to the lower index
+            float bm = -1.f;
+            int bi = 0;
+#pragma unroll
+            for (int d = 0; d < kTcD; ++d) {
+              const float mg = ((taken >> d) & 1ull) ? -2.f : fabsf(err[d]);
+              if (mg > bm) {
+                bm = mg;
+                bi = d;
+              }
+            }
+            float ev = 0.f;
+#pragma unroll
+            for (int d = 0; d < kTcD; ++d) ev = d == bi ? err[d] : ev;
+            taken |= 1ull << bi;
+            f_spi[s] = (uint8_t)bi;
+            f_spv[s] = f2h(ev);
+          }
+        }
+      }
+    }
+    __syncwarp();
+  }
+}
+
+bool encode_tc_supported(const rfsn_quantizer* qz) {
+  return qz->head_dim == kTcD && (qz->subspace_dim == 4 || qz->subspace_dim == 8) && qz->pq_codebook_size % 8 == 0 &&
+         qz->pq_codebook_size <= 256 && (qz->rvq_layers == 0 || (qz->rvq_layers == 1 && qz->rvq_codebook_size % 8 == 0 &&
+                                                                  qz->rvq_codebook_size <= 256)) &&
+         qz->sparse_topk <= kTcD;
+}
+
+int encode_tc_launch(const rfsn_quantizer* qz, const uint16_t* x, int64_t batch, int64_t tokens, int64_t heads,
+                     int64_t sb, int64_t st, int64_t sh, const rfsn_code_store* dst, int kv, int64_t slot,
+                     int64_t first, uint16_t* residual_out, cudaStream_t stream) {
+  EncTcParams p{};
+  p.x = x;
+  p.batch = batch; p.tokens = tokens; p.heads = heads; p.sb = sb; p.st = st; p.sh = sh;
+  p.nvec = batch * tokens * heads;
+  p.data = dst->data;
+  p.lay = layout_of(qz);
+  p.kv = kv;
+  p.cap = dst->cap; p.rows = dst->rows; p.slot = slot; p.first = first;
+  p.residual_out = residual_out;
+  p.pq_cb = qz->pq_codebooks;
+  p.rvq_cb = qz->rvq_codebooks;
+  p.M = qz->num_subspaces; p.K = qz->pq_codebook_size; p.L = qz->rvq_layers; p.Kr = qz->rvq_codebook_size;
+  p.S = qz->sparse_topk;
+  p.thr = qz->rvq_threshold;
+  int64_t off = 0;
+  p.smem_pq = (int)off; off = align_up(off + (int64_t)p.M * p.K * qz->subspace_dim * 2, 128);
+  p.smem_pqcc = (int)off; off = align_up(off + (int64_t)p.M * p.K * 4, 128);
+  p.smem_rvq = (int)off; off = align_up(off + (int64_t)(p.L ? p.Kr : 0) * kTcD * 2, 128);
+  p.smem_rcc = (int)off; off = align_up(off + (int64_t)(p.L ? p.Kr : 0) * 4, 128);
+  p.warp_bytes = (int)align_up(2 * 16 * 128 + 16 * p.M * 4 + 16 * 4 + 16 * p.M + 16 + 16, 128);
+  p.smem_warp = (int)off; off += (int64_t)kTcWarps * p.warp_bytes;
+  if (off > 227 * 1024) return RFSN_ERR_UNSUPPORTED;
+  if (p.nvec == 0) return RFSN_OK;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t groups = (p.nvec + 15) / 16;
+  const int64_t want = (groups + kTcWarps - 1) / kTcWarps;
+  const int grid = (int)(want < sms ? want : sms);
+  cudaError_t e;
+  if (qz->subspace_dim == 8) {
+    e = cudaFuncSetAttribute(encode_tc_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)off);
+    if (e == cudaSuccess) {
+      encode_tc_kernel<8><<<grid, kTcWarps * 32, off, stream>>>(p);
+      e = cudaGetLastError();
+    }
+  } else {
+    e = cudaFuncSetAttribute(encode_tc_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)off);
+    if (e == cudaSuccess) {
+      encode_tc_kernel<4><<<grid, kTcWarps * 32, off, stream>>>(p);
+      e = cudaGetLastError();
+    }
+  }
+  return check_cuda(e);
+}
+
+}  // namespace rfsn

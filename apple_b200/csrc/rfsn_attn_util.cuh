@@ -53,6 +53,11 @@ __device__ __forceinline__ void load_dense(const uint16_t* src, uint32_t* w) {
   }
 }
 
+__device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
+  const __half2 s = __hsub2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+  return *reinterpret_cast<const uint32_t*>(&s);
+}
+
 __device__ __forceinline__ uint32_t hadd2_u32(uint32_t a, uint32_t b) {
   const __half2 s = __hadd2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
   return *reinterpret_cast<const uint32_t*>(&s);

@@ -245,6 +245,29 @@ def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
     return buf
 
 
+class _AttnCall:
+    """Argument structs of one decode-attention call shape, kept for reuse: a
+    decode loop calls with the same stores, window and shapes step after step,
+    so only the tensor pointers are rewritten."""
+
+    __slots__ = ("args", "segs", "qs", "ws")
+
+    def __init__(self, args, segs, qs, ws):
+        self.args, self.segs, self.qs, self.ws = args, segs, qs, ws
+
+
+_ATTN_CALLS: "dict" = {}
+
+
+def _qz_key(qz: QuantizerBuffers) -> tuple:
+    return (_ptr(qz.pq_codebooks), _ptr(qz.rvq_codebooks), qz.M, qz.K, qz.ds, qz.L, qz.Kr, float(qz.threshold),
+            int(qz.sparse_topk))
+
+
+def _store_key(st: Optional[CodeStoreBuffers]) -> Optional[tuple]:
+    return None if st is None else (_ptr(st.data), st.cap, st.rows, st.slots)
+
+
 def decode_attention(qz: QuantizerBuffers, q: torch.Tensor, out: torch.Tensor, segments: Sequence[Tuple],
                      kv_heads: int, qpos: Optional[torch.Tensor] = None, causal: bool = True, scale: Optional[float] = None,
                      hot: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
@@ -264,35 +287,46 @@ def decode_attention(qz: QuantizerBuffers, q: torch.Tensor, out: torch.Tensor, s
     B, Qn, Hq, D = q.shape
     if len(segments) > _lib.RFSN_MAX_SEGMENTS:
         raise ValueError(f"at most {_lib.RFSN_MAX_SEGMENTS} segments per call")
-    a = AttnArgs()
-    a.q, a.out = _ptr(q), _ptr(out)
-    if causal:
-        if qpos is None or qpos.dtype != torch.int32 or tuple(qpos.shape) != (B, Qn, Hq) or not qpos.is_contiguous():
-            raise ValueError("causal attention needs contiguous int32 qpos [B, Q, Hq]")
-        a.qpos = _ptr(qpos)
-    a.batch, a.queries, a.q_heads, a.kv_heads = B, Qn, Hq, kv_heads
-    if hot is not None:
-        a.hot = DenseStore(_ptr(hot[0]), _ptr(hot[1]), hot[0].shape[1], hot[0].shape[0])
-    if warm is not None:
-        a.warm = warm.struct()
-    if cold is not None:
-        a.cold = cold.struct()
-    a.head_dim = D
-    a.causal = int(bool(causal))
-    a.scale = float(D ** -0.5 if scale is None else scale)
-    segs = (Segment * max(1, len(segments)))()
-    for i, (st, slot, first, count, pos0) in enumerate(segments):
-        segs[i].store, segs[i].slot, segs[i].first, segs[i].count, segs[i].pos0 = st, slot, first, count, pos0
-    a.segments = segs
-    a.num_segments = len(segments)
-    a.num_ctas = num_ctas
+    if causal and (qpos is None or qpos.dtype != torch.int32 or tuple(qpos.shape) != (B, Qn, Hq)
+                   or not qpos.is_contiguous()):
+        raise ValueError("causal attention needs contiguous int32 qpos [B, Q, Hq]")
+    scale = float(D ** -0.5 if scale is None else scale)
+    hot_key = None if hot is None else (_ptr(hot[0]), _ptr(hot[1]), hot[0].shape[1], hot[0].shape[0])
+    key = (q.device.index, B, Qn, Hq, D, kv_heads, bool(causal), scale, num_ctas, tuple(map(tuple, segments)),
+           hot_key, _store_key(warm), _store_key(cold), _qz_key(qz))
+    entry = _ATTN_CALLS.get(key)
+    if entry is None:
+        a = AttnArgs()
+        a.batch, a.queries, a.q_heads, a.kv_heads = B, Qn, Hq, kv_heads
+        if hot is not None:
+            a.hot = DenseStore(*hot_key)
+        if warm is not None:
+            a.warm = warm.struct()
+        if cold is not None:
+            a.cold = cold.struct()
+        a.head_dim = D
+        a.causal = int(bool(causal))
+        a.scale = scale
+        segs = (Segment * max(1, len(segments)))()
+        for i, (st, slot, first, count, pos0) in enumerate(segments):
+            segs[i].store, segs[i].slot, segs[i].first, segs[i].count, segs[i].pos0 = st, slot, first, count, pos0
+        a.segments = segs
+        a.num_segments = len(segments)
+        a.num_ctas = num_ctas
+        qs = qz.struct()
+        a.q, a.out, a.qpos = _ptr(q), _ptr(out), _ptr(qpos) if causal else None
+        nbytes = C.c_size_t(0)
+        call("rfsn_attention_workspace_size", C.byref(a), C.byref(qs), C.byref(nbytes))
+        ws = workspace(nbytes.value, q.device)
+        a.workspace, a.workspace_bytes = _ptr(ws), ws.numel()
+        if len(_ATTN_CALLS) >= 256:
+            _ATTN_CALLS.clear()
+        entry = _ATTN_CALLS[key] = _AttnCall(a, segs, qs, ws)
+    a = entry.args
+    a.q, a.out = q.data_ptr(), out.data_ptr()
+    a.qpos = qpos.data_ptr() if causal else None
     a.device_status = _ptr(device_status)
-    qs = qz.struct()
-    nbytes = C.c_size_t(0)
-    call("rfsn_attention_workspace_size", C.byref(a), C.byref(qs), C.byref(nbytes))
-    ws = workspace(nbytes.value, q.device)
-    a.workspace, a.workspace_bytes = _ptr(ws), ws.numel()
-    call("rfsn_decode_attention", C.byref(a), C.byref(qs), _stream())
+    call("rfsn_decode_attention", C.byref(a), C.byref(entry.qs), _stream())
     return out
 
 

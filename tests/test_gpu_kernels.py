@@ -274,3 +274,53 @@ def test_abi_rejects_out_of_range_segment():
     from apple_b200 import RFSNError
     with pytest.raises(RFSNError):
         K.decode_attention(qz, q, out, [(K.STORE_WARM, 0, 20, 20, 0)], kv_heads=4, causal=False, warm=st)
+
+
+@pytest.mark.parametrize("ds,L,thr,S", [(8, 1, 0.5, 0), (4, 1, -1.0, 8), (8, 0, 0.0, 0), (4, 1, 0.5, 0), (8, 1, -1.0, 4)])
+def test_tensor_core_encoder_vs_oracle(ds, L, thr, S):
+    """Spill encoder on tensor cores (D = 64 presets) vs the oracle on strided, ragged input:
+    B=2 sequences x 1249 tokens x 2 heads (not a multiple of the 16-vector tile)."""
+    rng = np.random.default_rng(100 * ds + 10 * L + S)
+    D, M = 64, 64 // ds
+    pq_cb = (rng.standard_normal((M, 256, ds)) * 0.8).astype(np.float16)
+    rvq_cb = (rng.standard_normal((1, 256, D)) * 0.3).astype(np.float16)
+    rvq_cb[:, 0] = 0
+    big = rng.standard_normal((2, 1300, 2, D)).astype(np.float32)
+    big[..., rng.choice(D, 4, replace=False)] *= 6.0
+    big = big.astype(np.float16)
+    T0, T = 30, 1249
+    x = big[:, T0:T0 + T]
+    oq = R.Quantizer(pq_cb, rvq_cb if L else np.zeros((0, 256, D), np.float16), thr, sparse_topk=S)
+    qz = K.QuantizerBuffers(to_dev(pq_cb), to_dev(rvq_cb) if L else None, thr, S)
+    xd = to_dev(big)[:, T0:T0 + T]  # strided view: stride_t = 2*D, stride_b = 1300*2*D
+    store = K.CodeStoreBuffers(qz, rows=2 * 2, cap=T + 7)
+    res = torch.empty_like(to_dev(big))[:, T0:T0 + T]
+    K.encode(qz, xd, store, 0, 7, residual_out=res)
+    torch.cuda.synchronize()
+    for b in range(2):
+        ref = oq.compress(x[b])
+        _, residual = R.pq_quantize(x[b].reshape(-1, D), pq_cb)
+        for h in range(2):
+            row = b * 2 + h
+            pq = store.read(0, "pq", 0, row, 7, T).cpu().numpy()
+            pq_tie_ok(x[b, :, h], pq_cb, pq, ref.pq[:, h])
+            agree = (pq == ref.pq[:, h]).all(axis=1)
+            assert agree.mean() > 0.99
+            got_res = res[b, :, h].cpu().numpy()
+            np.testing.assert_array_equal(got_res[agree].view(np.uint16),
+                                          residual.reshape(T, 2, D)[agree, h].view(np.uint16))
+            if L:
+                act = store.read(0, "active", 0, row, 7, T)[:, 0].cpu().numpy().astype(bool)
+                np.testing.assert_array_equal(act[agree], ref.mask[agree, h])
+                rv = store.read(0, "rvq", 0, row, 7, T).cpu().numpy()[:, 0].astype(np.int64)
+                sel = agree & ref.mask[:, h]
+                assert (rv[sel] == ref.rvq[sel, h, 0]).mean() > 0.99
+                sel = sel & (rv == ref.rvq[:, h, 0])
+            else:
+                sel = agree
+            if S:
+                np.testing.assert_array_equal(store.read(0, "sp_idx", 0, row, 7, T).cpu().numpy()[sel],
+                                              ref.sp_idx[sel, h])
+                np.testing.assert_array_equal(
+                    store.read(0, "sp_val", 0, row, 7, T).cpu().numpy()[sel].view(np.uint16),
+                    ref.sp_val[sel, h].view(np.uint16))
