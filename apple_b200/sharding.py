@@ -18,7 +18,7 @@ gloo for the CPU tests); shards of unequal size are padded to the largest.
 from __future__ import annotations
 
 from dataclasses import dataclass
-from typing import List
+from typing import List, Optional
 
 import torch
 
@@ -61,10 +61,12 @@ def plan_shards(batch: int, kv_heads: int, world: int) -> List[Shard]:
 
 
 def gather_outputs(local: torch.Tensor, shards: List[Shard], rank: int, group_size: int, q_per_kv: int,
-                   group=None) -> torch.Tensor:
+                   group=None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """All-gather each rank's attention output [b_r, Q, Hq_r, D] into the full [B, Q, Hq, D].
 
-    Hq_r = shard.kv_heads * q_per_kv (query head h reads KV head h // q_per_kv)."""
+    Hq_r = shard.kv_heads * q_per_kv (query head h reads KV head h // q_per_kv).  ``out``
+    (contiguous, [B, Q, Hq, D]) receives the result when given; a decode loop passes the
+    same buffer every step."""
     import torch.distributed as dist
     if len(shards) != group_size:
         raise ValueError("one shard per rank")
@@ -77,7 +79,7 @@ def gather_outputs(local: torch.Tensor, shards: List[Shard], rank: int, group_si
     if all(s.batch == me.batch and s.head0 == 0 and s.head1 * q_per_kv == Hq and s.batch0 == r * me.batch
            for r, s in enumerate(shards)):
         # equal batch shards in rank order: gather straight into the full output
-        full = torch.empty((B, Q, Hq, D), dtype=local.dtype, device=local.device)
+        full = out if out is not None else torch.empty((B, Q, Hq, D), dtype=local.dtype, device=local.device)
         dist.all_gather_into_tensor(full, local.contiguous(), group=group)
         return full
     max_b = max(s.batch for s in shards)
@@ -87,7 +89,7 @@ def gather_outputs(local: torch.Tensor, shards: List[Shard], rank: int, group_si
     flat = torch.empty((group_size * max_b,) + tuple(buf.shape[1:]), dtype=buf.dtype, device=buf.device)
     dist.all_gather_into_tensor(flat, buf, group=group)  # rank r's shard at rows [r*max_b, (r+1)*max_b)
     allbuf = flat.view((group_size,) + tuple(buf.shape))
-    full = torch.empty((B, Q, Hq, D), dtype=local.dtype, device=local.device)
+    full = out if out is not None else torch.empty((B, Q, Hq, D), dtype=local.dtype, device=local.device)
     for r, s in enumerate(shards):
         full[s.batch0:s.batch1, :, s.head0 * q_per_kv:s.head1 * q_per_kv] = \
             allbuf[r, : s.batch, :, : s.kv_heads * q_per_kv]

@@ -116,6 +116,11 @@ def build_workload(device, seed):
     return dict(qz=qz, warm=ws, hot=(hot_k, hot_v), q=q, qpos=qpos, segs=segs, k=k, v=v)
 
 
+# NVML polling period.  Only rank 0 samples: NVML polling from every rank measurably
+# slowed the per-step NCCL gather at N > 1.
+CLOCK_PERIOD_S = float(os.environ.get("RFSN_CLOCK_PERIOD_MS", "20")) / 1e3
+
+
 class ClockSampler:
     """SM clock and throttle-reason samples (NVML) during the timed region.
 
@@ -128,25 +133,37 @@ class ClockSampler:
 
     REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4}
 
-    def __init__(self, device):
+    def __init__(self, device, active: bool = True, devices: int = 1):
         self.device = device
+        self.active = active
+        self.devices = devices  # sample cuda:0 .. cuda:devices-1 (one rank per local GPU)
         self.proc = None
         self.path = ROOT / "gpurun_out" / f"clocks_{os.getpid()}.json"
         self.error = None
 
     def _ident(self) -> str:
         import torch
-        props = torch.cuda.get_device_properties(self.device)
-        uuid = str(getattr(props, "uuid", "") or "")
-        bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
-        return f"{uuid},{bus}"
+        idents = []
+        devs = [self.device] if self.devices <= 1 else [torch.device("cuda", i) for i in range(self.devices)]
+        for d in devs:
+            props = torch.cuda.get_device_properties(d)
+            uuid = str(getattr(props, "uuid", "") or "")
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            idents.append(f"{uuid},{bus}")
+        return ";".join(idents)
 
     def __enter__(self):
         import subprocess
+        if not self.active:
+            return self
+        if CLOCK_PERIOD_S <= 0:
+            self.error = "clock sampling disabled (RFSN_CLOCK_PERIOD_MS <= 0)"
+            return self
         try:
             self.path.parent.mkdir(exist_ok=True)
             self.proc = subprocess.Popen([sys.executable, str(Path(__file__).resolve()), "--clock-sampler",
-                                          self._ident(), str(self.path)], stdout=subprocess.PIPE, text=True)
+                                          self._ident(), str(self.path)], stdout=subprocess.PIPE, text=True,
+                                         env=dict(os.environ))
             line = self.proc.stdout.readline().strip()  # "ready" once NVML answers
             if line != "ready":
                 self.error = f"sampler did not start: {line!r}"
@@ -167,8 +184,9 @@ class ClockSampler:
             d = json.loads(self.path.read_text())
             sm = [c for c, _ in d["samples"]]
             reasons = sorted({n for _, bits in d["samples"] for n, bit in self.REASONS.items() if bits & bit})
-            out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": d.get("max_mhz"),
-                   "reasons": reasons, "samples": len(sm), "source": "nvml (sampler process, 1 ms)"}
+            out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_min_mhz": min(sm) if sm else None,
+                   "sm_max_mhz": d.get("max_mhz"), "reasons": reasons, "samples": len(sm), "gpus": d.get("gpus", 1),
+                   "source": f"nvml (sampler process, every {CLOCK_PERIOD_S * 1e3:g} ms, all local GPUs)"}
         except Exception as e:
             out = {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "error": str(e)}
         if self.error:
@@ -177,30 +195,34 @@ class ClockSampler:
 
 
 def clock_sampler_main(ident: str, path: str) -> None:
-    """Child process: poll NVML every millisecond until SIGTERM, then write the samples."""
+    """Child process: poll NVML every CLOCK_PERIOD_S until SIGTERM, then write the samples."""
     import signal
     import pynvml
     stop = []
     signal.signal(signal.SIGTERM, lambda *a: stop.append(1))
     pynvml.nvmlInit()
-    uuid, bus = ident.split(",", 1)
-    h = None
-    if uuid:
-        try:
-            h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
-        except Exception:
-            h = None
-    if h is None:
-        h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+    handles = []
+    for one in ident.split(";"):
+        uuid, bus = one.split(",", 1)
+        h = None
+        if uuid:
+            try:
+                h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            except Exception:
+                h = None
+        if h is None:
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        handles.append(h)
     get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
         pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
-    max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+    max_mhz = max(float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)) for h in handles)
     samples = []
     print("ready", flush=True)
     while not stop:
-        samples.append((float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)), int(get_reasons(h))))
-        time.sleep(0.001)
-    Path(path).write_text(json.dumps({"max_mhz": max_mhz, "samples": samples}))
+        for h in handles:
+            samples.append((float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)), int(get_reasons(h))))
+        time.sleep(CLOCK_PERIOD_S)
+    Path(path).write_text(json.dumps({"max_mhz": max_mhz, "samples": samples, "gpus": len(handles)}))
 
 
 # ---------------------------------------------------------------------------
@@ -360,16 +382,28 @@ def public_api_cache(w, dev):
     return cache
 
 
-def e2e_public_api(w, args, dev) -> dict:
-    """The decode step through the public API: pinned host query in, host output out, every step."""
+def e2e_public_api(w, args, dev, world: int = 1, rank: int = 0, shards=None) -> dict:
+    """The decode step through the public API: pinned host query in, host output out, every step.
+
+    With N ranks each rank runs its own sequences and the outputs are all-gathered
+    (NCCL) before the host read, so every rank reads the whole batch's output."""
     import torch
     cache = public_api_cache(w, dev)
     h_q = w["q"][:, 0].cpu().pin_memory()          # [B, Hq, D]
     h_out = torch.empty_like(h_q).pin_memory()
+    if world > 1:
+        from apple_b200.sharding import gather_outputs
+        h_full = torch.empty((world * h_q.shape[0],) + tuple(h_q.shape[1:]), dtype=h_q.dtype).pin_memory()
+        G = CFG["q_heads"] // CFG["kv_heads"]
 
     def step():
         out = cache.attention_forward(h_q, causal=True)
-        h_out.copy_(out)  # device -> host read of the step's result
+        if world > 1:
+            full = gather_outputs(out.unsqueeze(1), shards, rank, world, G)
+            h_full.copy_(full[:, 0])
+            h_out.copy_(out)
+        else:
+            h_out.copy_(out)  # device -> host read of the step's result
 
     for _ in range(max(3, args.warmup)):
         step()
@@ -382,6 +416,11 @@ def e2e_public_api(w, args, dev) -> dict:
     e1.record(s)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
     # the public API's result equals the device-resident kernel call
     ref = torch.empty_like(w["q"])
     from apple_b200 import kernels as K
@@ -390,8 +429,10 @@ def e2e_public_api(w, args, dev) -> dict:
     err = float((ref[:, 0].float().cpu() - h_out.float()).abs().max())
     nb = h_q.numel() * h_q.element_size()
     cache.close()
-    return {"value": 1e3 / ms, "unit": UNIT, "h2d_bytes_per_step": nb, "d2h_bytes_per_step": nb,
-            "api": "RFSNv10KVCacheMLX.attention_forward", "max_abs_diff_vs_kernel_call": err}
+    return {"value": world * 1e3 / ms, "unit": UNIT, "h2d_bytes_per_step": nb,
+            "d2h_bytes_per_step": nb * (world if world > 1 else 1),
+            "api": "RFSNv10KVCacheMLX.attention_forward" + (" + NCCL all-gather of outputs" if world > 1 else ""),
+            "max_abs_diff_vs_kernel_call": err}
 
 
 def run_b200(args) -> None:
@@ -431,19 +472,21 @@ def run_b200(args) -> None:
         attn()
     torch.cuda.synchronize()
 
+    full = torch.empty((world * CFG["batch"],) + tuple(out.shape[1:]), dtype=out.dtype, device=dev) if world > 1 else None
+
     def step():
         graph.replay()
         if world > 1:
-            gather_outputs(out, shards, rank, world, CFG["q_heads"] // CFG["kv_heads"])
+            gather_outputs(out, shards, rank, world, CFG["q_heads"] // CFG["kv_heads"], out=full)
 
     for _ in range(max(3, args.warmup)):
         step()
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(dev) as clocks:
+    with ClockSampler(dev, active=rank == 0, devices=world) as clocks:
+        if world > 1:
+            dist.barrier()  # after the sampler started, so every rank enters the timed region together
         torch.cuda.synchronize()
         e0.record(stream)
         for _ in range(args.steps):
@@ -469,7 +512,7 @@ def run_b200(args) -> None:
     torch.cuda.synchronize()
     kern_ms = e2.elapsed_time(e3) / args.steps
 
-    e2e = e2e_public_api(w, args, dev)
+    e2e = e2e_public_api(w, args, dev, world, rank, shards)
     del graph
     if world > 1:
         dist.barrier()
@@ -551,11 +594,11 @@ def run_encode(args) -> None:
     for _ in range(max(3, args.warmup)):
         K.encode(qz, xv, st, 0, 0)
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(dev) as clocks:
+    with ClockSampler(dev, active=rank == 0, devices=world) as clocks:
+        if world > 1:
+            dist.barrier()  # after the sampler started, so every rank enters the timed region together
         torch.cuda.synchronize()
         e0.record(stream)
         for _ in range(args.steps):
