@@ -26,7 +26,8 @@ logger = logging.getLogger("RFSN_MLX_APPLE")
 
 
 class _Linear:
-    """y = x @ W^T (no bias); W ~ U(-1/sqrt(in), 1/sqrt(in)) like mlx.nn.Linear, or N(0, 1/in)."""
+    """y = x @ W^T (no bias); W ~ U(-1/sqrt(in), 1/sqrt(in)) like mlx.nn.Linear, or N(0, 1/in).
+    The product runs in the activations' dtype, as mlx.nn.Linear casts W to x's dtype."""
 
     def __init__(self, in_dim: int, out_dim: int, device, dtype, gen: torch.Generator, init: str):
         if init == "normal":
@@ -34,9 +35,14 @@ class _Linear:
         else:
             w = (torch.rand((out_dim, in_dim), generator=gen) * 2 - 1) / math.sqrt(in_dim)
         self.weight = w.to(device=device, dtype=dtype)
+        self._cast = None  # weight in the activations' dtype, refreshed when the weight is replaced
+        self._src = None
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
-        return torch.matmul(x.to(self.weight.dtype), self.weight.t())
+        # like mlx.nn.Linear: the weight is cast to the activations' dtype (fp16 in the layer)
+        if self._cast is None or self._cast.dtype != x.dtype or self._src is not self.weight:
+            self._cast, self._src = self.weight.to(x.dtype), self.weight
+        return torch.matmul(x, self._cast.t())
 
 
 class _RMSNorm:

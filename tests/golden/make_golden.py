@@ -198,21 +198,103 @@ def case_router(ref, name):
         shutil.rmtree(tmp, ignore_errors=True)
 
 
+def case_decoder_layer(ref, name, seed):
+    """RFSNDecoderLayerMLX (rfsn_v10_mlx_ane_complete.py:55-172): prefill, then cache-backed
+    decode steps through hot, warm and cold tiers, plus the dense (no-cache) path.
+    Weights are seeded N(0, 1/in) and injected; they are stored as fp16 because the
+    reference's Linear casts its weights to the fp16 activations (mlx.nn.Linear)."""
+    mx = sys.modules["mlx.core"]
+    rng = np.random.default_rng(seed)
+    tmp = Path(tempfile.mkdtemp(prefix="rfsn_layer_"))
+    try:
+        hidden, heads, hd = 256, 4, 64
+        config = make_config(ref, hidden_dim=hidden, num_heads=heads, head_dim=hd, num_subspaces=8, subspace_dim=8,
+                             num_rvq_layers=1, rvq_codebook_size=64, rvq_sparsity_threshold=0.3, hot_capacity=16,
+                             warm_capacity=24, block_size_seq=16, disk_cache_dir=str(tmp))
+        layer = ref["rfsn_v10_mlx_ane_complete"].RFSNDecoderLayerMLX(config, layer_idx=0)
+        rec = {}
+        for nm, (o, i) in dict(q_proj=(hidden, hidden), k_proj=(hidden, hidden), v_proj=(hidden, hidden),
+                               o_proj=(hidden, hidden), ffn_up=(2 * hidden, hidden),
+                               ffn_down=(hidden, 2 * hidden)).items():
+            w = (rng.standard_normal((o, i)) / np.sqrt(i)).astype(np.float16)
+            getattr(layer, nm).weight = mx.array(w.astype(np.float32), dtype=mx.float32)
+            rec[f"w_{nm}"] = w
+        pq_cb, rvq_cb = seeded_codebooks(rng, 8, 256, 8, 1, 64, hd)
+        layer.quantizer.pq.codebooks = mx.array(pq_cb, dtype=mx.float16)
+        layer.quantizer.rvq.codebooks = mx.array(rvq_cb, dtype=mx.float16)
+        rec.update(pq_codebooks=pq_cb, rvq_codebooks=rvq_cb)
+        n_prefill, n_decode = 40, 24
+        x = rng.standard_normal((1, n_prefill + n_decode, hidden)).astype(np.float16)
+        layer.prefill_cache(mx.array(x[:, :n_prefill]))
+        outs = []
+        for t in range(n_prefill, n_prefill + n_decode):
+            outs.append(np.asarray(layer(mx.array(x[:, t:t + 1]), use_cache=True)))
+        stats = layer.cache.get_last_access_stats()
+        x2 = rng.standard_normal((2, 6, hidden)).astype(np.float16)
+        dense = np.asarray(layer(mx.array(x2), use_cache=False))
+        rec.update(x=x, n_prefill=np.int32(n_prefill), decode_out=np.concatenate(outs, 1), x_dense=x2,
+                   dense_out=dense, last_stats=np.array([stats[k] for k in STAT_KEYS], np.int64),
+                   tiers=np.array([layer.cache.num_hot, layer.cache.num_warm, layer.cache.num_cold], np.int32))
+        np.savez_compressed(OUT / f"{name}.npz", **rec)
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+
+
+def case_calibration(ref, name, seed, n=2048, iters=10):
+    """calibrate_quantizer (rfsn_v10_mlx_ane_complete.py:175-225): k-means PQ codebooks from
+    sampled initial centroids.  The sample indices the reference draws are recorded so the
+    B200 build can start from the same centroids."""
+    mx = sys.modules["mlx.core"]
+    rng = np.random.default_rng(seed)
+    config = make_config(ref, hidden_dim=512, num_heads=8, head_dim=64, num_subspaces=8, subspace_dim=8,
+                         num_rvq_layers=0, rvq_sparsity_threshold=0.5)
+    hq = ref["quantization"].HybridQuantizerMLX(config)
+    vectors = rng.standard_normal((n, 64)).astype(np.float16)
+    drawn = []
+    orig = mx.random.randint
+
+    def recording_randint(*a, **kw):
+        out = orig(*a, **kw)
+        drawn.append(np.asarray(out).astype(np.int64))
+        return out
+
+    mx.random.randint = recording_randint
+    try:
+        metrics = ref["rfsn_v10_mlx_ane_complete"].calibrate_quantizer(hq, mx.array(vectors), num_iterations=iters)
+    finally:
+        mx.random.randint = orig
+    np.savez_compressed(OUT / f"{name}.npz", vectors=vectors, sample_idx=np.stack(drawn),
+                        codebooks=np.asarray(hq.pq.codebooks), iters=np.int32(iters),
+                        avg_distortion=np.array(metrics["avg_distortion"], np.float64),
+                        sparsity_fraction=np.array(metrics["sparsity_fraction"], np.float64), threshold=np.float32(0.5))
+
+
+CASES = {
+    "quant": lambda ref: (
+        case_quantizer(ref, "quant_d128_m8x16_rvq3", seed=11, cfg_kw={}, n=96, scale_half=0.01),
+        case_quantizer(ref, "quant_d64_m16x4_rvq1_dense", seed=12,
+                       cfg_kw=dict(head_dim=64, num_subspaces=16, subspace_dim=4, num_rvq_layers=1,
+                                   rvq_sparsity_threshold=-1.0), n=512, outliers=4),
+        case_quantizer(ref, "quant_d64_m8x8_rvq1", seed=13,
+                       cfg_kw=dict(head_dim=64, num_subspaces=8, subspace_dim=8, num_rvq_layers=1,
+                                   rvq_sparsity_threshold=0.5), n=512),
+        case_quantizer(ref, "quant_d64_m8x8_pqonly", seed=14,
+                       cfg_kw=dict(head_dim=64, num_subspaces=8, subspace_dim=8, num_rvq_layers=1,
+                                   rvq_sparsity_threshold=float("inf")), n=256)),
+    "attention": lambda ref: case_attention(ref, "attention_hybrid", seed=21),
+    "cache": lambda ref: case_cache(ref, "cache_tiers", seed=31, n_tokens=60, queries=[59, 50, 20],
+                                    windows=[None, 8, 30]),
+    "router": lambda ref: case_router(ref, "router_order"),
+    "layer": lambda ref: case_decoder_layer(ref, "decoder_layer", seed=41),
+    "calibration": lambda ref: case_calibration(ref, "calibration_kmeans", seed=51),
+}
+
+
 def main() -> None:
+    """python tests/golden/make_golden.py [case ...]  (default: every case)."""
     ref = load_reference()
-    case_quantizer(ref, "quant_d128_m8x16_rvq3", seed=11, cfg_kw={}, n=96, scale_half=0.01)
-    case_quantizer(ref, "quant_d64_m16x4_rvq1_dense", seed=12,
-                   cfg_kw=dict(head_dim=64, num_subspaces=16, subspace_dim=4, num_rvq_layers=1,
-                               rvq_sparsity_threshold=-1.0), n=512, outliers=4)
-    case_quantizer(ref, "quant_d64_m8x8_rvq1", seed=13,
-                   cfg_kw=dict(head_dim=64, num_subspaces=8, subspace_dim=8, num_rvq_layers=1,
-                               rvq_sparsity_threshold=0.5), n=512)
-    case_quantizer(ref, "quant_d64_m8x8_pqonly", seed=14,
-                   cfg_kw=dict(head_dim=64, num_subspaces=8, subspace_dim=8, num_rvq_layers=1,
-                               rvq_sparsity_threshold=float("inf")), n=256)
-    case_attention(ref, "attention_hybrid", seed=21)
-    case_cache(ref, "cache_tiers", seed=31, n_tokens=60, queries=[59, 50, 20], windows=[None, 8, 30])
-    case_router(ref, "router_order")
+    for name in (sys.argv[1:] or list(CASES)):
+        CASES[name](ref)
     print("wrote", sorted(p.name for p in OUT.glob("*.npz")))
 
 

@@ -220,3 +220,44 @@ def test_decoder_layer_cached_decode_matches_dense(tmp_path):
     dense = layer(x, use_cache=False)
     close(y[0, 0].float().cpu().numpy(), dense[0, -1].float().cpu().numpy(), "decoder layer")
     assert layer.cache_tokens == 40
+
+
+def test_decoder_layer_golden(tmp_path):
+    """RFSNDecoderLayerMLX vs the reference layer (rfsn_v10_mlx_ane_complete.py:55-172): prefill 40
+    tokens, 24 cache-backed decode steps through hot, warm and cold tiers, and the dense path."""
+    g = dict(np.load(GOLDEN / "decoder_layer.npz"))
+    cfg = RFSNConfig(hidden_dim=256, num_heads=4, head_dim=64, num_subspaces=8, subspace_dim=8, num_rvq_layers=1,
+                     rvq_codebook_size=64, rvq_sparsity_threshold=0.3, hot_capacity=16, warm_capacity=24,
+                     block_size_seq=16, disk_cache_dir=str(tmp_path))
+    layer = RFSNDecoderLayerMLX(cfg, layer_idx=0)
+    for nm in ("q_proj", "k_proj", "v_proj", "o_proj", "ffn_up", "ffn_down"):
+        getattr(layer, nm).weight = torch.from_numpy(g[f"w_{nm}"].astype(np.float32)).cuda()
+    layer.quantizer.pq.codebooks = torch.from_numpy(g["pq_codebooks"]).cuda()
+    layer.quantizer.rvq.codebooks = torch.from_numpy(g["rvq_codebooks"]).cuda()
+    x = torch.from_numpy(g["x"]).cuda()
+    P = int(g["n_prefill"])
+    layer.prefill_cache(x[:, :P])
+    outs = [layer(x[:, t:t + 1], use_cache=True) for t in range(P, x.shape[1])]
+    got = torch.cat(outs, 1).float().cpu().numpy()
+    close(got, g["decode_out"], "cache-backed decode")
+    assert [layer.cache.last_access_stats[k] for k in STAT_KEYS] == list(g["last_stats"])
+    assert [layer.cache.num_hot, layer.cache.num_warm, layer.cache.num_cold] == list(g["tiers"])
+    dense = layer(torch.from_numpy(g["x_dense"]).cuda(), use_cache=False).float().cpu().numpy()
+    close(dense, g["dense_out"], "dense path")
+    layer.cache.close()
+
+
+def test_calibration_golden():
+    """calibrate_quantizer on the GPU (PQ encoder kernel + mean updates) from the reference's samples."""
+    from apple_b200.layer import calibrate_quantizer
+    g = dict(np.load(GOLDEN / "calibration_kmeans.npz"))
+    cfg = RFSNConfig(hidden_dim=512, num_heads=8, head_dim=64, num_subspaces=8, subspace_dim=8, num_rvq_layers=0,
+                     rvq_sparsity_threshold=float(g["threshold"]))
+    hq = HybridQuantizerMLX(cfg)
+    metrics = calibrate_quantizer(hq, torch.from_numpy(g["vectors"]).cuda(), num_iterations=int(g["iters"]),
+                                  sample_idx=torch.from_numpy(g["sample_idx"]))
+    cb = hq.pq.codebooks.cpu().numpy()
+    assert (cb.view(np.uint16) == g["codebooks"].view(np.uint16)).mean() > 0.995
+    np.testing.assert_allclose(cb.astype(np.float32), g["codebooks"].astype(np.float32), atol=4e-3, rtol=0)
+    np.testing.assert_allclose(metrics["avg_distortion"], g["avg_distortion"], rtol=1e-3)
+    np.testing.assert_allclose(metrics["sparsity_fraction"], g["sparsity_fraction"], atol=1e-3)

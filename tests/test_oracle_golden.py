@@ -164,3 +164,13 @@ def test_router_candidates_api_matches_golden(tmp_path):
             assert router.candidates(int(pos), int(win), int(k)) == [int(x) for x in want if x >= 0]
     finally:
         unregister_cold_tier(tmp_path, 7)
+
+
+def test_calibration_matches_reference():
+    """calibrate_quantizer (rfsn_v10_mlx_ane_complete.py:175-225) from the reference's own initial samples."""
+    g = load("calibration_kmeans")
+    cbs, dist = R.calibrate_pq(g["vectors"], 8, 256, int(g["iters"]), g["sample_idx"])
+    same = (cbs.view(np.uint16) == g["codebooks"].view(np.uint16)).mean()
+    assert same > 0.999, same
+    np.testing.assert_allclose(cbs.astype(np.float32), g["codebooks"].astype(np.float32), atol=2e-3, rtol=0)
+    np.testing.assert_allclose(dist, g["avg_distortion"], rtol=1e-4)
