@@ -85,6 +85,7 @@ class RFSNv10KVCacheMLX:
         self._cold: Optional[ColdTier] = None
         self._cold_root: Optional[Path] = None
         self._qpos_cache: Dict[Tuple, torch.Tensor] = {}
+        self._plan_cache: Dict[Tuple, Tuple[List, Dict[str, int]]] = {}
 
     # ------------------------------------------------------------------ stats
     def _empty_access_stats(self) -> Dict[str, int]:
@@ -514,7 +515,9 @@ class RFSNv10KVCacheMLX:
         return keys, values, (None if adjusted is None else torch.as_tensor(adjusted, device=self.device))
 
     def _queries(self, q: torch.Tensor) -> Tuple[torch.Tensor, bool]:
-        q = q.to(device=self.device, dtype=torch.float16)
+        # a pinned host query is uploaded asynchronously on the current stream (ordered
+        # before the attention kernel); keep it unchanged until the call's result is read
+        q = q.to(device=self.device, dtype=torch.float16, non_blocking=bool(not q.is_cuda and q.is_pinned()))
         if self.batch == 1 and q.dim() == 3:
             return q.unsqueeze(0).contiguous(), True          # [1, Q, Hq, D]
         if q.dim() == 3 and q.shape[0] == self.batch:
@@ -563,8 +566,22 @@ class RFSNv10KVCacheMLX:
             raise RuntimeError("Cache cannot run attention before update() provides a quantizer")
         qb, squeeze = self._queries(q)
         start, end, _ = self._window_bounds(query_positions, context_window, current_position)
-        stats = self._begin_stats(start, end, context_window, router)
-        segs = self._plan(start, end, router, current_position, context_window, stats)
+        # without a cold tier or router the plan depends only on the window and the tier
+        # layout, so a decode loop that reads the same window reuses it
+        key = None
+        if router is None and not self.cold_chunk_metadata:
+            key = (start, end, context_window, self.total_tokens, self.num_hot, self.num_warm, self._hot_start,
+                   self._warm_start)
+        cached = self._plan_cache.get(key) if key is not None else None
+        if cached is not None:
+            segs, stats = cached[0], dict(cached[1])
+        else:
+            stats = self._begin_stats(start, end, context_window, router)
+            segs = self._plan(start, end, router, current_position, context_window, stats)
+            if key is not None:
+                if len(self._plan_cache) > 32:
+                    self._plan_cache.clear()
+                self._plan_cache[key] = (segs, dict(stats))
         stats["query_tokens"] = int(q.shape[0])
         self.last_access_stats = stats
         if out is None:

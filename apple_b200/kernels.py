@@ -22,7 +22,13 @@ def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
 
-def _stream() -> int:
+_RAW_STREAM = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _stream(device_index: Optional[int] = None) -> int:
+    """Handle of the current torch CUDA stream (of ``device_index``, default the current device)."""
+    if _RAW_STREAM is not None:
+        return _RAW_STREAM(torch.cuda.current_device() if device_index is None else device_index)
     return torch.cuda.current_stream().cuda_stream
 
 
@@ -326,7 +332,7 @@ def decode_attention(qz: QuantizerBuffers, q: torch.Tensor, out: torch.Tensor, s
     a.q, a.out = q.data_ptr(), out.data_ptr()
     a.qpos = qpos.data_ptr() if causal else None
     a.device_status = _ptr(device_status)
-    call("rfsn_decode_attention", C.byref(a), C.byref(entry.qs), _stream())
+    call("rfsn_decode_attention", C.byref(a), C.byref(entry.qs), _stream(q.device.index))
     return out
 
 

@@ -118,7 +118,7 @@ def build_workload(device, seed):
 
 # NVML polling period.  Only rank 0 samples: NVML polling from every rank measurably
 # slowed the per-step NCCL gather at N > 1.
-CLOCK_PERIOD_S = float(os.environ.get("RFSN_CLOCK_PERIOD_MS", "20")) / 1e3
+CLOCK_PERIOD_S = float(os.environ.get("RFSN_CLOCK_PERIOD_MS", "5")) / 1e3
 
 
 class ClockSampler:
