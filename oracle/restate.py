@@ -669,3 +669,65 @@ def calibrate_pq(vectors: np.ndarray, num_subspaces: int, codebook_size: int, it
         recon = pq_decode(codes, cbs)
         distortion.append(float(np.mean((x32 - recon.astype(F32)) ** 2)))
     return cbs, distortion
+
+
+# ---------------------------------------------------------------------------
+# Decoder layer (rfsn_v10_mlx_ane_complete.py:55-172)
+# ---------------------------------------------------------------------------
+
+def rms_norm(x: np.ndarray, eps: float = 1e-5) -> np.ndarray:
+    """mlx.nn.RMSNorm with unit weight: fp32 x * rsqrt(mean(x^2) + eps), back to x's dtype."""
+    xf = x.astype(F32)
+    y = xf * (F32(1.0) / np.sqrt(np.mean(xf * xf, axis=-1, keepdims=True, dtype=F32) + F32(eps)))
+    return y.astype(x.dtype)
+
+
+def linear(x: np.ndarray, w: np.ndarray) -> np.ndarray:
+    """mlx.nn.Linear without bias: W cast to x's dtype (fp16), products summed in fp32."""
+    return (x.astype(F32) @ w.astype(x.dtype).astype(F32).T).astype(x.dtype)
+
+
+class OracleDecoderLayer:
+    """RFSNDecoderLayerMLX restated: RMSNorm -> q/k/v -> cache update -> cache attention (or
+    dense causal attention) -> o_proj + residual -> RMSNorm -> GELU FFN (2x) + residual.
+    Weights are fp16 [out, in]; batch 1 as in the reference's cache path."""
+
+    def __init__(self, config: OracleConfig, quantizer: Quantizer, weights: Dict[str, np.ndarray]):
+        self.cfg = config
+        self.w = weights
+        self.h = config.num_heads
+        self.hkv = config.num_kv_heads
+        self.d = config.head_dim
+        self.cache = OracleCache(config, quantizer, batch=1)
+
+    def _heads(self, y: np.ndarray, heads: int) -> np.ndarray:
+        b, s, _ = y.shape
+        return y.reshape(b, s, heads, self.d).astype(F16)
+
+    def prefill_cache(self, x: np.ndarray) -> None:
+        """rfsn_v10_mlx_ane_complete.py:90-104."""
+        a = rms_norm(x.astype(F16))
+        self.cache.update(self._heads(linear(a, self.w["k_proj"]), self.hkv),
+                          self._heads(linear(a, self.w["v_proj"]), self.hkv))
+
+    def __call__(self, x: np.ndarray, use_cache: bool = False, context_window: Optional[int] = None) -> np.ndarray:
+        """rfsn_v10_mlx_ane_complete.py:114-172."""
+        residual = x.astype(F16)
+        a = rms_norm(residual)
+        q = self._heads(linear(a, self.w["q_proj"]), self.h)
+        k = self._heads(linear(a, self.w["k_proj"]), self.hkv)
+        v = self._heads(linear(a, self.w["v_proj"]), self.hkv)
+        b, s = x.shape[:2]
+        if use_cache:
+            self.cache.update(k, v)
+            total = self.cache.total_tokens
+            win = context_window if context_window is not None else \
+                max(self.cfg.block_size_seq, min(total, self.cfg.warm_capacity))
+            att = self.cache.attention_forward(q[:, :1], causal=True, query_positions=[total - 1],
+                                               current_position=total - 1, context_window=win)
+            att = att.reshape(b, 1, self.h, self.d)
+        else:
+            att = dense_exact_attention(q, k, v, self.d ** -0.5, causal=True)
+        hidden = residual + linear(att.reshape(b, s, self.h * self.d).astype(F16), self.w["o_proj"])
+        f = rms_norm(hidden)
+        return hidden + linear(gelu(linear(f, self.w["ffn_up"])), self.w["ffn_down"])

@@ -174,3 +174,29 @@ def test_calibration_matches_reference():
     assert same > 0.999, same
     np.testing.assert_allclose(cbs.astype(np.float32), g["codebooks"].astype(np.float32), atol=2e-3, rtol=0)
     np.testing.assert_allclose(dist, g["avg_distortion"], rtol=1e-4)
+
+
+def test_oracle_decoder_layer_matches_reference():
+    """OracleDecoderLayer vs the reference layer's outputs (prefill, 24 cache decode steps, dense)."""
+    g = load("decoder_layer")
+    cfg = R.OracleConfig(hidden_dim=256, num_heads=4, head_dim=64, num_subspaces=8, subspace_dim=8,
+                         num_rvq_layers=1, rvq_codebook_size=64, rvq_sparsity_threshold=0.3, hot_capacity=16,
+                         warm_capacity=24, block_size_seq=16)
+    qz = R.Quantizer(g["pq_codebooks"], g["rvq_codebooks"], 0.3)
+    w = {k[2:]: g[k] for k in g if k.startswith("w_")}
+    layer = R.OracleDecoderLayer(cfg, qz, w)
+    P = int(g["n_prefill"])
+    layer.prefill_cache(g["x"][:, :P])
+    outs = np.concatenate([layer(g["x"][:, t:t + 1], use_cache=True) for t in range(P, g["x"].shape[1])], 1)
+    _layer_close(outs, g["decode_out"])
+    assert [layer.cache.num_hot, layer.cache.num_warm, layer.cache.num_cold] == list(g["tiers"])
+    assert [layer.cache.last_access_stats[k] for k in STAT_KEYS] == list(g["last_stats"])
+    _layer_close(layer(g["x_dense"], use_cache=False), g["dense_out"])
+
+
+def _layer_close(out, ref):
+    """|out - ref| <= 2e-3 |ref| + 2e-3 rms(ref): fp16 outputs of fp16 GEMMs whose fp32 summation
+    order differs from the reference's."""
+    out, ref = np.asarray(out, np.float32), np.asarray(ref, np.float32)
+    tol = 2e-3 * np.abs(ref) + 2e-3 * float(np.sqrt(np.mean(ref ** 2)))
+    assert (np.abs(out - ref) <= tol).all(), float(np.abs(out - ref).max())
