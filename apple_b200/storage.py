@@ -357,7 +357,10 @@ class ColdTier:
             return slot
 
     def wait_ready(self, slot: int, stream: torch.cuda.Stream) -> None:
-        ev = self.slot_ready.get(slot)
+        """Order `stream` after the copy into `slot`.  The compute stream is the only reader of
+        pool slots, so once it has waited the event is dropped: later work on the stream
+        is already ordered after the copy."""
+        ev = self.slot_ready.pop(slot, None)
         if ev is not None:
             stream.wait_event(ev)
 
@@ -366,15 +369,19 @@ _COLD_REGISTRY: Dict[Tuple[str, int], ColdTier] = {}
 
 
 def register_cold_tier(root: Path, layer_idx: int, tier: ColdTier) -> None:
-    _COLD_REGISTRY[(str(Path(root).resolve()), int(layer_idx))] = tier
+    _COLD_REGISTRY[cold_tier_key(root, layer_idx)] = tier
+
+
+def cold_tier_key(root: Path, layer_idx: int) -> Tuple[str, int]:
+    return str(Path(root).resolve()), int(layer_idx)
 
 
 def lookup_cold_tier(root: Path, layer_idx: int) -> Optional[ColdTier]:
-    return _COLD_REGISTRY.get((str(Path(root).resolve()), int(layer_idx)))
+    return _COLD_REGISTRY.get(cold_tier_key(root, layer_idx))
 
 
 def unregister_cold_tier(root: Path, layer_idx: int) -> None:
-    _COLD_REGISTRY.pop((str(Path(root).resolve()), int(layer_idx)), None)
+    _COLD_REGISTRY.pop(cold_tier_key(root, layer_idx), None)
 
 
 class AsyncHierarchicalRouterMLX:
@@ -393,6 +400,8 @@ class AsyncHierarchicalRouterMLX:
         self.config = config
         self.layer_idx = layer_idx
         self.disk_dir = Path(config.disk_cache_dir)
+        # resolved once: a per-lookup Path.resolve() costs filesystem calls on every candidate
+        self._tier_key = cold_tier_key(self.disk_dir, layer_idx)
         self.throttle = config.prefetch_throttle_s
         self._cache: "OrderedDict[int, Dict[str, object]]" = OrderedDict()
         self._max_cache_size = 16
@@ -400,7 +409,7 @@ class AsyncHierarchicalRouterMLX:
         self._stream: Optional[torch.cuda.Stream] = None
 
     def _tier(self) -> Optional[ColdTier]:
-        return lookup_cold_tier(self.disk_dir, self.layer_idx)
+        return _COLD_REGISTRY.get(self._tier_key)
 
     @property
     def stream(self) -> torch.cuda.Stream:
@@ -421,9 +430,9 @@ class AsyncHierarchicalRouterMLX:
 
     async def predict_and_prefetch(self, current_position: int, context_window: int, top_k: int = 2) -> List[int]:
         loaded: List[int] = []
+        tier = self._tier()
         for chunk_id in self.candidates(current_position, context_window, top_k):
             entry = self._cache.get(chunk_id)
-            tier = self._tier()
             if entry is not None and tier is not None and tier.resident(chunk_id):
                 loaded.append(chunk_id)
                 continue
@@ -437,15 +446,26 @@ class AsyncHierarchicalRouterMLX:
                 await asyncio.sleep(self.throttle)
         while len(self._cache) > self._max_cache_size:
             old, _ = self._cache.popitem(last=False)
-            tier = self._tier()
             if tier is not None:
                 tier.pinned_by_router.discard(old)
         return loaded
 
     def prefetch_sync(self, current_position: int, context_window: int, top_k: int = 2) -> List[int]:
+        coro = self.predict_and_prefetch(current_position, context_window, top_k)
+        if self.throttle <= 0:
+            # With no throttle sleep the coroutine has no suspension point (chunk copies are
+            # queued on the router's CUDA stream, not awaited), so one send() runs it to the end
+            # without building an event loop per decode step.
+            try:
+                coro.send(None)
+            except StopIteration as done:
+                return done.value
+            coro.close()
+            raise RuntimeError("router prefetch suspended with throttle disabled")
         try:
-            return asyncio.run(self.predict_and_prefetch(current_position, context_window, top_k))
+            return asyncio.run(coro)
         except RuntimeError:
+            coro.close()
             loop = asyncio.new_event_loop()
             try:
                 return loop.run_until_complete(self.predict_and_prefetch(current_position, context_window, top_k))

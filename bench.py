@@ -676,6 +676,263 @@ def encode_cpu_baseline(sample: int = 16384) -> dict:
             "sample": f"numpy oracle encode_flat of {sample} of the {e['N']} vectors (one core)"}
 
 
+# ---------------------------------------------------------------------------
+# Single decoder layer (the reference's CPU-runnable case)
+# ---------------------------------------------------------------------------
+# hidden 512, 8 q / 8 KV heads, head_dim 64, batch 1: a 1024-token prefix, then
+# 64 cache-backed decode steps.  Hot tier = the newest 128 tokens (fp16); warm
+# tier = PQ 8x8, K=256, k-means (10 iterations) on the prefix's K and V; no RVQ,
+# no cold tier.  Weights N(0,1)/sqrt(512) fp16, inputs N(0,1) fp16, seed 0.  A
+# step is one decode step of the layer through its public API.
+
+LAYER = dict(hidden=512, heads=8, head_dim=64, prefix=1024, decode=64, hot=128, M=8, ds=8, K=256, iters=10, seed=0)
+
+
+def layer_setup():
+    """Seeded weights, inputs, prefix K/V vectors and k-means initial samples (shared by both arms)."""
+    from oracle import restate as R  # noqa: F401  (rms_norm / linear only; same arithmetic as the layer)
+    c = LAYER
+    rng = np.random.default_rng(c["seed"])
+    h = c["hidden"]
+    shapes = dict(q_proj=(h, h), k_proj=(h, h), v_proj=(h, h), o_proj=(h, h), ffn_up=(2 * h, h), ffn_down=(h, 2 * h))
+    w = {k: (rng.standard_normal(sh) / np.sqrt(sh[1])).astype(np.float16) for k, sh in shapes.items()}
+    x = rng.standard_normal((1, c["prefix"] + c["decode"], h)).astype(np.float16)
+    a = R.rms_norm(x[:, : c["prefix"]])
+    vecs = np.concatenate([R.linear(a, w["k_proj"]).reshape(-1, c["head_dim"]),
+                           R.linear(a, w["v_proj"]).reshape(-1, c["head_dim"])], 0)
+    sample_idx = rng.integers(0, vecs.shape[0], (c["M"], c["K"]))
+    return w, x, vecs, sample_idx
+
+
+def run_layer(args) -> None:
+    import torch
+    from apple_b200.layer import RFSNDecoderLayerMLX, calibrate_quantizer
+    from apple_b200.storage import RFSNConfig
+    c = LAYER
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    w, x, vecs, sample_idx = layer_setup()
+    steps = c["decode"]
+
+    def fresh_layer():
+        cfg = RFSNConfig(hidden_dim=c["hidden"], num_heads=c["heads"], head_dim=c["head_dim"], num_subspaces=c["M"],
+                         subspace_dim=c["ds"], num_rvq_layers=0, hot_capacity=c["hot"], warm_capacity=4096,
+                         block_size_seq=128, hot_policy="recent", device=str(dev),
+                         disk_cache_dir=str(ROOT / "gpurun_out" / "bench_layer_cold"))
+        layer = RFSNDecoderLayerMLX(cfg, layer_idx=0)
+        for k, v in w.items():
+            getattr(layer, k).weight = torch.from_numpy(v.astype(np.float32)).to(dev)
+        calibrate_quantizer(layer.quantizer, torch.from_numpy(vecs).to(dev), num_iterations=c["iters"],
+                            sample_idx=torch.from_numpy(sample_idx))
+        layer.prefill_cache(torch.from_numpy(x[:, : c["prefix"]]).to(dev))
+        torch.cuda.synchronize()
+        return layer
+
+    xd = torch.from_numpy(x).to(dev)
+    layer = fresh_layer()
+    for t in range(min(3, steps)):  # warm-up on a throwaway layer
+        layer(xd[:, c["prefix"] + t: c["prefix"] + t + 1], use_cache=True)
+    layer = fresh_layer()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clocks:
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for t in range(steps):
+            y = layer(xd[:, c["prefix"] + t: c["prefix"] + t + 1], use_cache=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    # e2e: host input row in, host output row out, every step
+    layer = fresh_layer()
+    hx = torch.from_numpy(x).pin_memory()
+    hout = torch.empty((1, 1, c["hidden"]), dtype=torch.float16).pin_memory()
+    t0 = time.perf_counter()
+    for t in range(steps):
+        hout.copy_(layer(hx[:, c["prefix"] + t: c["prefix"] + t + 1], use_cache=True))
+    e2e_s = (time.perf_counter() - t0) / steps
+    weights = sum(v.size for v in w.values()) * 2
+    kv = c["heads"] * 2 * (c["hot"] * c["head_dim"] * 2 + (c["prefix"] + steps // 2 - c["hot"]) * c["M"])
+    nbytes = weights + kv
+    peak, _ = measured_peak()
+    cpu = layer_cpu_baseline(min(16, steps))
+    print(json.dumps({
+        "metric": "single-layer decode steps/s (1K prefix, PQ 8x8, hot 128)", "value": 1e3 / ms, "unit": "steps/s",
+        "n_gpus": 1, "steps": steps, "warmup": 3, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16 operands, f32 accumulate", "data": "synthetic",
+        "config": {"workload": "BASELINE configs[0]: hidden 512, 8 heads, D64, batch 1, 1024 prefix + 64 decode steps",
+                   "hot": "newest 128 tokens", "warm": "PQ 8x8 K256, k-means 10 iters on the prefix K/V"},
+        "roofline": {"bound": "hbm", "achieved": nbytes / (ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": nbytes / (ms * 1e-3) / 1e9 / peak, "traffic": None, "bytes_per_step": nbytes,
+                     "note": "latency-bound: about 10 kernel launches per step on a 4.4 MB working set"},
+        "e2e": {"value": 1.0 / e2e_s, "unit": "steps/s", "h2d_bytes_per_step": c["hidden"] * 2,
+                "d2h_bytes_per_step": c["hidden"] * 2, "api": "RFSNDecoderLayerMLX.__call__(use_cache=True)"},
+        "clocks": clocks.summary(), "cpu_baseline": cpu}))
+    layer.cache.close()
+
+
+def layer_cpu_baseline(steps: int) -> dict:
+    """The numpy decoder layer (oracle/restate.py, RFSNDecoderLayerMLX restated) on the same config."""
+    from oracle import restate as R
+    c = LAYER
+    w, x, vecs, sample_idx = layer_setup()
+    cbs, _ = R.calibrate_pq(vecs, c["M"], c["K"], c["iters"], sample_idx)
+    cfg = R.OracleConfig(hidden_dim=c["hidden"], num_heads=c["heads"], head_dim=c["head_dim"], num_subspaces=c["M"],
+                         subspace_dim=c["ds"], num_rvq_layers=0, hot_capacity=c["hot"], warm_capacity=4096,
+                         block_size_seq=128, hot_policy="recent")
+    layer = R.OracleDecoderLayer(cfg, R.Quantizer(cbs, np.zeros((0, 256, c["head_dim"]), np.float16), 0.0), w)
+    layer.prefill_cache(x[:, : c["prefix"]])
+    t0 = time.perf_counter()
+    for t in range(steps):
+        layer(x[:, c["prefix"] + t: c["prefix"] + t + 1], use_cache=True)
+    dt = (time.perf_counter() - t0) / steps
+    return {"value": 1.0 / dt, "unit": "steps/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"numpy decoder layer, first {steps} of the {c['decode']} decode steps (numpy BLAS threads)"}
+
+
+# ---------------------------------------------------------------------------
+# Long-context three-tier decode (BASELINE configs[3])
+# ---------------------------------------------------------------------------
+# Llama-3.2-1B layer shape, batch 4, 131072-token context: hot = newest 2048
+# tokens, warm = the next 32768 (PQ 16x4 + RVQ + top-8 sparse as configs[1]),
+# cold = the oldest 96256 tokens in 188 chunks of 512 tokens, kept in pinned host
+# memory and copied into a device chunk pool on demand.  Keys follow a per-chunk
+# mean that drifts as a random walk (step sigma 0.05) plus N(0,1) noise; seed 3.
+# A step is one exact decode-attention pass over the whole window.
+
+LONG = dict(batch=4, q_heads=32, kv_heads=8, head_dim=64, context=131072, hot=2048, warm=32768, chunk=512, M=16,
+            ds=4, K=256, Kr=256, sparse=8, seed=3)
+
+
+def long_bytes() -> int:
+    c = LONG
+    rows = c["batch"] * c["kv_heads"]
+    coded = c["context"] - c["hot"]
+    return rows * (c["hot"] * 2 * c["head_dim"] * 2 + coded * 2 * (c["M"] + 1 + 3 * c["sparse"])) + \
+        2 * c["batch"] * c["q_heads"] * c["head_dim"] * 2
+
+
+def longctx_setup(dev):
+    """Build the configs[3] cache (hot/warm/cold tiers filled) on `dev`; returns (cfg, cache, q)."""
+    import torch
+    from apple_b200.cache import RFSNv10KVCacheMLX
+    from apple_b200.quantization import HybridQuantizerMLX
+    from apple_b200.storage import RFSNConfig
+    c = LONG
+    g = torch.Generator(device=dev).manual_seed(c["seed"])
+    B, Hkv, D, T, ch = c["batch"], c["kv_heads"], c["head_dim"], c["context"], c["chunk"]
+    nchunks = T // ch
+    steps_walk = torch.randn((B, nchunks, Hkv, D), generator=g, device=dev) * 0.05
+    means = torch.cumsum(steps_walk, dim=1)
+    k = (means.repeat_interleave(ch, dim=1) + torch.randn((B, T, Hkv, D), generator=g, device=dev)).half()
+    v = torch.randn((B, T, Hkv, D), generator=g, device=dev).half()
+    cfg = RFSNConfig(hidden_dim=c["q_heads"] * D, num_heads=c["q_heads"], num_kv_heads=Hkv, head_dim=D,
+                     num_subspaces=c["M"], subspace_dim=c["ds"], num_rvq_layers=1, rvq_codebook_size=c["Kr"],
+                     rvq_sparsity_threshold=-1.0, sparse_topk=c["sparse"], hot_capacity=c["hot"],
+                     warm_capacity=c["warm"], block_size_seq=128, cold_chunk_tokens=ch,
+                     cold_pool_chunks=nchunks, batch_size=B, hot_policy="recent", device=str(dev),
+                     prefetch_throttle_s=0.0, disk_cache_dir=str(ROOT / "gpurun_out" / "bench_long_cold"))
+    hq = HybridQuantizerMLX(cfg)
+    flat = torch.cat([k[:, ::97].reshape(-1, D), v[:, ::97].reshape(-1, D)], 0)
+    idx = torch.randint(0, flat.shape[0], (c["M"], c["K"]), generator=g, device=dev)
+    hq.pq.codebooks = torch.stack([flat[idx[m], m * c["ds"]:(m + 1) * c["ds"]] for m in range(c["M"])]).contiguous()
+    samp = flat[torch.randint(0, flat.shape[0], (c["Kr"],), generator=g, device=dev)]
+    codes, res = hq.pq.quantize(samp)
+    rvq = res.reshape(1, c["Kr"], D).clone()
+    rvq[:, 0] = 0
+    hq.rvq.codebooks = rvq
+    cache = RFSNv10KVCacheMLX(cfg, layer_idx=0)
+    for a in range(0, T, 8192):
+        cache.update(k[:, a:a + 8192], v[:, a:a + 8192], hq)
+    torch.cuda.synchronize()
+    assert (cache.num_hot, cache.num_warm) == (c["hot"], c["warm"]), (cache.num_hot, cache.num_warm)
+    q = torch.randn((B, c["q_heads"], D), generator=g, device=dev).half()
+    return cfg, cache, q
+
+
+def run_longctx(args) -> None:
+    import torch
+    from apple_b200 import kernels as K
+    from apple_b200.storage import AsyncHierarchicalRouterMLX
+    c = LONG
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    cfg, cache, q = longctx_setup(dev)
+    B, Hkv, T = c["batch"], c["kv_heads"], c["context"]
+    router = AsyncHierarchicalRouterMLX(cfg, layer_idx=0)
+    # first pass: the router prefetches, misses copy chunk images host -> device
+    h2d0 = cache._cold.h2d_bytes
+    t0 = time.perf_counter()
+    out_api = cache.attention_forward(q, causal=True, router=router, current_position=T - 1, context_window=T)
+    torch.cuda.synchronize()
+    cold_fill_s = time.perf_counter() - t0
+    cold_fill_bytes = cache._cold.h2d_bytes - h2d0
+    stats = cache.get_last_access_stats()
+    # device-resident steady state: the window's segments replayed from a captured graph
+    start, end, _ = cache._window_bounds(None, T, T - 1)
+    segs = cache._plan(start, end, None, None, None, cache._begin_stats(start, end, T, None))
+    qb = q.unsqueeze(1).contiguous()
+    out = torch.empty_like(qb)
+    qpos = torch.full((B, 1, c["q_heads"]), T - 1, dtype=torch.int32, device=dev)
+
+    def attn():
+        K.decode_attention(cache._qz, qb, out, segs, kv_heads=Hkv, qpos=qpos, causal=True,
+                           hot=(cache._hot_k, cache._hot_v), warm=cache._warm, cold=cache._cold.pool)
+
+    for _ in range(3):
+        attn()
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        attn()
+    for _ in range(3):
+        graph.replay()
+    steps = max(10, args.steps)
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clocks:
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    err = float((out[:, 0].float() - out_api.float()).abs().max())
+    # e2e: public API with the router every step, pinned host query in, host output out
+    hqh = q.cpu().pin_memory()
+    hout = torch.empty_like(hqh).pin_memory()
+    for _ in range(2):
+        hout.copy_(cache.attention_forward(hqh, causal=True, router=router, current_position=T - 1, context_window=T))
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    n_e2e = 10
+    for _ in range(n_e2e):
+        hout.copy_(cache.attention_forward(hqh, causal=True, router=router, current_position=T - 1, context_window=T))
+    e2e_s = (time.perf_counter() - t0) / n_e2e
+    nbytes = long_bytes()
+    peak, _ = measured_peak()
+    del graph
+    print(json.dumps({
+        "metric": "long-context decode attn steps/s (131K ctx, three tiers)", "value": 1e3 / ms, "unit": "steps/s",
+        "n_gpus": 1, "steps": steps, "warmup": 3, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16 operands, f32 accumulate", "data": "synthetic",
+        "config": {"workload": "BASELINE configs[3]: batch 4, 131072 ctx, hot 2048 / warm 32768 / cold 188 x 512",
+                   "segments": len(segs), "cold_pool": "all 188 chunks device-resident after the first pass"},
+        "roofline": {"bound": "hbm", "achieved": nbytes / (ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": nbytes / (ms * 1e-3) / 1e9 / peak, "traffic": None, "algorithmic_bytes_per_step": nbytes},
+        "cold_fill": {"seconds": cold_fill_s, "h2d_bytes": cold_fill_bytes,
+                      "h2d_gbs": cold_fill_bytes / cold_fill_s / 1e9 if cold_fill_s > 0 else None,
+                      "stats": {k2: stats[k2] for k2 in ("cold_chunks_touched", "cold_chunk_cache_hits",
+                                                          "cold_chunk_cache_misses", "cold_tokens_materialized")}},
+        "e2e": {"value": 1.0 / e2e_s, "unit": "steps/s", "h2d_bytes_per_step": hqh.numel() * 2,
+                "d2h_bytes_per_step": hqh.numel() * 2, "api": "RFSNv10KVCacheMLX.attention_forward with router"},
+        "max_abs_diff_api_vs_graph": err, "gpu_launches": steps, "clocks": clocks.summary()}))
+    cache.close()
+
+
 def main() -> None:
     if len(sys.argv) == 4 and sys.argv[1] == "--clock-sampler":
         clock_sampler_main(sys.argv[2], sys.argv[3])
@@ -685,10 +942,28 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "encode"],
-                    help="decode: fused decode attention (configs[1], the headline); encode: spill encoder (configs[4])")
+    ap.add_argument("--workload", default="decode", choices=["decode", "encode", "layer", "longctx"],
+                    help="decode: fused decode attention (configs[1], the headline); encode: spill encoder "
+                         "(configs[4]); layer: single decoder layer decode (configs[0])")
     args = ap.parse_args()
-    if args.workload == "encode":
+    if args.workload == "longctx":
+        if args.impl == "reference":
+            if int(os.environ.get("RANK", "0")) == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "no CPU arm for the 131K three-tier workload: "
+                                  "the numpy port needs minutes per step at this size"}))
+        else:
+            run_longctx(args)
+    elif args.workload == "layer":
+        if args.impl == "reference":
+            if int(os.environ.get("RANK", "0")) == 0:
+                cb = layer_cpu_baseline(LAYER["decode"])
+                print(json.dumps({"metric": "single-layer decode steps/s (1K prefix, PQ 8x8, hot 128)",
+                                  "value": cb["value"], "unit": "steps/s", "n_gpus": args.gpus, "impl": "reference",
+                                  "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": "steps/s",
+                                                               "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+        else:
+            run_layer(args)
+    elif args.workload == "encode":
         if args.impl == "reference":
             if int(os.environ.get("RANK", "0")) == 0:
                 cb = encode_cpu_baseline()
