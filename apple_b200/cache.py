@@ -554,6 +554,10 @@ class RFSNv10KVCacheMLX:
                 pos = np.broadcast_to(pos[:, None, :], (B, Qn, Hq))
             elif pos.shape != (B, Qn, Hq):
                 raise ValueError("query_positions must be [B], [B, H] or [B, Q, H]")
+        if pos.size and bool((pos == end - 1).all()):
+            # the decode case (every query at the newest token): reuse the cached device tensor
+            # instead of uploading positions each step
+            return self._qpos(None, start, end, qb)
         return torch.as_tensor(np.ascontiguousarray(pos, dtype=np.int32)).to(self.device, non_blocking=True)
 
     def attention_forward(self, q: torch.Tensor, pq_codebook=None, rvq_codebook=None, causal: bool = True,

@@ -353,10 +353,10 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
   // lanes' reconstructed half2 registers as the B fragment (column = lane/4 =
   // (slot, dim half h = j/4), k = dims); A holds the query rows twice: rows
   // 0..7 matched to the h=0 dims, rows 8..15 to the h=1 dims.  Score(slot, r)
-  // is then c0 + c3 of lane 4r + slot.  V is accumulated on CUDA cores.
+  // is then c0 + c3 of lane 4r + slot.  P.V runs on tensor cores as well
+  // (O^T = V^T P^T, see process_block), so the output state is D/16 x 4 floats
+  // per lane whatever the number of query rows.
   const int slot = lane >> 3;
-  const int j = lane & 7;
-  const int dim0 = j * DPL;
   const int srow = lane >> 2;   // score lane: query row r
   const int sslot = lane & 3;   // score lane: token slot
   // per-warp scratch: fp16 sparse scatter rows while a piece runs, then the
@@ -381,7 +381,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
   c.qp_lim = 0;
   c.sl2 = p.scale * 1.4426950408889634f;  // scores kept in log2 units
   uint32_t aq[NMMA][4];  // query A fragments
-  float acc[RMAX][DPL];
+  float acc[D / 16][4];
   float m_run = NEG_INF, l_run = 0.f;  // online state of row srow (replicated over its 4 lanes)
   int stage = 0;
   uint32_t phase = 0, sync_phase = 0;
@@ -412,9 +412,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
       m_run = NEG_INF;
       l_run = 0.f;
 #pragma unroll
-      for (int r = 0; r < RMAX; ++r)
-#pragma unroll
-        for (int i = 0; i < DPL; ++i) acc[r][i] = 0.f;
+      for (int u = 0; u < D / 16; ++u) acc[u][0] = acc[u][1] = acc[u][2] = acc[u][3] = 0.f;
       {  // A fragments: lane (gA, tA) = (lane/4, lane%4); row gA is query row gA
         const int gA = lane >> 2, tA = lane & 3;
         const uint16_t* qrow = nullptr;
@@ -466,24 +464,18 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
     if (lane == 0) mbar_arrive(&empty_bar[stage]);
 
     if (last_of_piece) {
-      // reduce over the 4 token slots, then lay the warp's partial out as [RMAX][D]
-#pragma unroll
-      for (int r = 0; r < RMAX; ++r)
-#pragma unroll
-        for (int i = 0; i < DPL; ++i) {
-          float v = acc[r][i];
-          v += __shfl_xor_sync(0xffffffffu, v, 8);
-          v += __shfl_xor_sync(0xffffffffu, v, 16);
-          acc[r][i] = v;
-        }
+      // lay the warp's partial out as [RMAX][D]: lane (g, q) holds rows 2q, 2q+1 at dims
+      // DPL*g + 2u and DPL*g + 2u + 1
       float* part = reinterpret_cast<float*>(scr);
-      if (slot == 0) {
+      {
+        const int r0 = 2 * sslot, dg = srow * DPL;
 #pragma unroll
-        for (int r = 0; r < RMAX; ++r)
-#pragma unroll
-          for (int i = 0; i < DPL; i += 4)
-            *reinterpret_cast<float4*>(part + r * D + dim0 + i) =
-                make_float4(acc[r][i], acc[r][i + 1], acc[r][i + 2], acc[r][i + 3]);
+        for (int u = 0; u < D / 16; ++u) {
+          if (r0 < RMAX)
+            *reinterpret_cast<float2*>(part + r0 * D + dg + 2 * u) = make_float2(acc[u][0], acc[u][2]);
+          if (r0 + 1 < RMAX)
+            *reinterpret_cast<float2*>(part + (r0 + 1) * D + dg + 2 * u) = make_float2(acc[u][1], acc[u][3]);
+        }
       }
       if (sslot == 0 && srow < RMAX) {
         s_ml[(warp * RMAX + srow) * 2 + 0] = m_run;
@@ -566,7 +558,8 @@ struct Plan {
 // CTA per SM covers q and the output accumulator without spilling.
 static constexpr int consumer_warps(int D, int rmax) {
   // total warps (NW + producer) a multiple of 4 so each SM sub-partition gets the same count
-  return D == 64 ? (rmax <= 4 ? 15 : 11) : (rmax <= 2 ? 15 : 11);
+  // (the output state no longer depends on rmax; D = 128 keeps 16 dims per lane in flight)
+  return D == 64 ? 15 : (rmax <= 2 ? 15 : 11);
 }
 
 static int sm_count_cached() {
@@ -667,7 +660,6 @@ static int make_plan(const rfsn_attn_args* a, const rfsn_quantizer* qz, Plan& pl
   // (tile sizes are chosen after the shared-memory layout fixes the stage size)
   // kernel variant
   pl.rmax = R <= 1 ? 1 : R <= 2 ? 2 : R <= 4 ? 4 : 8;
-  if (p.D == 128 && pl.rmax > 4) return RFSN_ERR_UNSUPPORTED;
   pl.nw = consumer_warps(p.D, pl.rmax);
   const int64_t pq_bytes = (int64_t)p.M * p.K * p.ds * 2;
   const int64_t rvq_bytes = (int64_t)p.L * p.Kr * p.D * 2;
@@ -786,7 +778,8 @@ static cudaError_t launch(const Plan& pl, cudaStream_t s) {
   switch (pl.rmax) {
     case 1: return launch_ds<128, 1, consumer_warps(128, 1)>(pl, s);
     case 2: return launch_ds<128, 2, consumer_warps(128, 2)>(pl, s);
-    default: return launch_ds<128, 4, consumer_warps(128, 4)>(pl, s);
+    case 4: return launch_ds<128, 4, consumer_warps(128, 4)>(pl, s);
+    default: return launch_ds<128, 8, consumer_warps(128, 8)>(pl, s);
   }
 }
 

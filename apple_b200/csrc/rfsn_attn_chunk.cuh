@@ -232,19 +232,27 @@ __device__ __forceinline__ void load_round(const ChunkCtx& c, const unsigned cha
   }
 }
 
-// One 16-token chunk: K scores on tensor cores, online softmax, V accumulation.
-// blk: the block's bytes (code tiles); dense_k/dense_v: the chunk's 16 hot rows
-// (dense tiles).  Valid tokens are [t_lo, t_hi); token tb is at position
-// pos_base + tb.  TPR tokens per lane are loaded per round (4 / TPR rounds per
-// phase); a round's loads are all in flight before its arithmetic.
+// One 16-token chunk: K scores on tensor cores, online softmax, then P.V on
+// tensor cores.  blk: the block's bytes (code tiles); dense_k/dense_v: the
+// chunk's 16 hot rows (dense tiles).  Valid tokens are [t_lo, t_hi); token tb is
+// at position pos_base + tb.  TPR tokens per lane are loaded per round (4 / TPR
+// rounds per phase); a round's loads are all in flight before its arithmetic.
+//
+// Output accumulators (D/16 tiles x 4 per lane): lane (g = lane/4, q = lane%4)
+// holds acc[u] = {O[2q][DPL*g+2u], O[2q+1][DPL*g+2u], O[2q][DPL*g+2u+1],
+// O[2q+1][DPL*g+2u+1]} for query rows 2q, 2q+1 (unnormalised, online-softmax
+// scaled) -- the D fragment of O^T = V^T P^T.
 template <int D, int RMAX, int LP, bool DENSE, int TPR>
 __device__ __forceinline__ void process_block(const ChunkCtx& c, const unsigned char* blk, const uint16_t* dense_k,
                                               const uint16_t* dense_v, int t_lo, int t_hi, int pos_base,
-                                              const uint32_t (*aq)[4], float (*acc)[D / 8], float& m_run,
+                                              const uint32_t (*aq)[4], float (*acc)[4], float& m_run,
                                               float& l_run) {
   constexpr int DPL = D / 8;
+  constexpr int NT = D / 16;   // P.V tiles of 16 dims
   constexpr int NMMA = DPL / 4;
   constexpr int NR = 4 / TPR;  // rounds per phase
+  static_assert(TPR == 2, "P.V pairs the two tokens of a round");
+  static_assert(RMAX <= 8, "P.V covers at most 8 query rows");
   const float NEG_INF = __int_as_float(0xff800000);
   const int lane = threadIdx.x & 31;
   const int slot = lane >> 3, j = lane & 7, dim0 = j * DPL;
@@ -299,15 +307,24 @@ __device__ __forceinline__ void process_block(const ChunkCtx& c, const unsigned 
   l_run = l_run * alpha + lsum;
   m_run = m_new;
   if (__any_sync(0xffffffffu, alpha != 1.f)) {  // a row's max grew: rescale its sums
+    // this lane accumulates rows 2q and 2q+1, whose factors sit in score lanes 8q and 8q+4
+    const float a0 = __shfl_sync(0xffffffffu, alpha, 8 * sslot);
+    const float a1 = __shfl_sync(0xffffffffu, alpha, 8 * sslot + 4);
 #pragma unroll
-    for (int r = 0; r < RMAX; ++r) {
-      const float ar = __shfl_sync(0xffffffffu, alpha, 4 * r);
-#pragma unroll
-      for (int i = 0; i < DPL; ++i) acc[r][i] *= ar;
+    for (int u = 0; u < NT; ++u) {
+      acc[u][0] *= a0; acc[u][2] *= a0;
+      acc[u][1] *= a1; acc[u][3] *= a1;
     }
   }
 
-  // ---------------- values ----------------
+  // ---------------- values: O^T += V^T P^T, one mma.m16n8k8 per tile and round ----------------
+  // Round rr rebuilds tokens 8rr + slot and 8rr + 4 + slot in lane (slot, j).  In the mma, k index
+  // 2q + e (q = lane%4) is token 8rr + q + 4e, A rows g and g+8 (g = lane/4) of tile u are dims
+  // DPL*g + 2u and DPL*g + 2u + 1, and B column g is query row g.  Lane (g, q) therefore takes the
+  // values rebuilt by lane (slot q, j g) = 8q + g, pairs them by token with byte permutes, and
+  // supplies its own probabilities P[row g][tokens 8rr + q, 8rr + q + 4] (left here by the score
+  // phase) split into fp16 hi + lo halves.
+  const int src = (sslot << 3) | (lane >> 2);
 #pragma unroll
   for (int rr = 0; rr < NR; ++rr) {
     int tb[TPR];
@@ -319,17 +336,16 @@ __device__ __forceinline__ void process_block(const ChunkCtx& c, const unsigned 
     }
     uint32_t w[TPR][DPL / 2];
     load_round<D, LP, DENSE, TPR>(c, blk, dense_v, 1, tb, valid, t_lo, NR + rr, slot, j, dim0, odd, w);
+    uint32_t bhi, blo;
+    split_h2(pr[2 * rr], pr[2 * rr + 1], bhi, blo);
 #pragma unroll
-    for (int i = 0; i < TPR; ++i) {
-      float pv[RMAX];
-#pragma unroll
-      for (int r = 0; r < RMAX; ++r) pv[r] = __shfl_sync(0xffffffffu, pr[rr * TPR + i], 4 * r + slot);
-#pragma unroll
-      for (int k = 0; k < DPL / 2; ++k) {
-        const float2 v2 = __half22float2(*reinterpret_cast<const __half2*>(&w[i][k]));
-#pragma unroll
-        for (int r = 0; r < RMAX; ++r) ffma2(acc[r][2 * k], acc[r][2 * k + 1], pv[r], v2.x, v2.y);
-      }
+    for (int u = 0; u < NT; ++u) {
+      const uint32_t x0 = __shfl_sync(0xffffffffu, w[0][u], src);
+      const uint32_t x1 = __shfl_sync(0xffffffffu, w[1][u], src);
+      const uint32_t a0 = prmt(x0, x1, 0x5410u);  // dim DPL*g + 2u of the round's two tokens
+      const uint32_t a1 = prmt(x0, x1, 0x7632u);  // dim DPL*g + 2u + 1
+      mma16808(acc[u], a0, a1, bhi);
+      mma16808(acc[u], a0, a1, blo);
     }
   }
 }

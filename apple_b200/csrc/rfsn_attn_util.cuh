@@ -3,7 +3,9 @@
 // * mma16816: one mma.sync.m16n8k16 (f16 x f16 -> f32 accumulate).  Products of
 //   fp16 values are exact in fp32, so scores equal fp32 dot products up to the
 //   accumulation order.
-// * ffma2: two independent round-to-nearest fp32 FMAs in one fma.rn.f32x2.
+// * mma16808: one mma.sync.m16n8k8 (f16 x f16 -> f32 accumulate), used for P.V.
+// * split_h2: two fp32 probabilities as fp16 hi + lo pairs (p = hi + lo to about
+//   22 bits), so P.V on tensor cores keeps near-fp32 weights.
 // * rvq_add8: fp16 RVQ correction of 8 dims (one layer: fp16 row; several:
 //   fp16 of the fp32 sum of rows, as rfsn_decode.cuh::recon8), added in fp16.
 #pragma once
@@ -25,21 +27,31 @@ __device__ __forceinline__ void mma16816(float c[4], const uint32_t a[4], uint32
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+__device__ __forceinline__ void mma16808(float c[4], uint32_t a0, uint32_t a1, uint32_t b) {
+  asm("mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(b));
+}
+
+// byte permute: result byte i = byte (sel >> 4i) & 7 of the 8-byte value {b, a}
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
+// (p0, p1) -> hi = fp16x2 of (p0, p1), lo = fp16x2 of the remainders p - float(hi)
+__device__ __forceinline__ void split_h2(float p0, float p1, uint32_t& hi, uint32_t& lo) {
+  const __half2 h = __floats2half2_rn(p0, p1);
+  const float2 hf = __half22float2(h);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = pack_h2(p0 - hf.x, p1 - hf.y);
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-__device__ __forceinline__ void ffma2(float& a0, float& a1, float p, float x0, float x1) {
-  asm("{\n\t.reg .b64 A, P, X;\n\t"
-      "mov.b64 A, {%0, %1};\n\t"
-      "mov.b64 P, {%2, %2};\n\t"
-      "mov.b64 X, {%3, %4};\n\t"
-      "fma.rn.f32x2 A, P, X, A;\n\t"
-      "mov.b64 {%0, %1}, A;\n\t}"
-      : "+f"(a0), "+f"(a1)
-      : "f"(p), "f"(x0), "f"(x1));
 }
 
 __device__ __forceinline__ uint32_t ldg_u32(const uint16_t* p) { return __ldg(reinterpret_cast<const unsigned int*>(p)); }

@@ -1,10 +1,13 @@
 """Decode-attention benchmark for the B200 RFSN compressed-KV path.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload decode|encode]
+                    [--workload decode|encode|layer|longctx|stack]
 
-The default (decode) workload is the headline metric; --workload encode times
-the tensor-core spill encoder on BASELINE configs[4] (see run_encode).
+The default (decode) workload is the headline metric.  The others time the
+remaining BASELINE configurations: encode = the tensor-core spill encoder
+(configs[4], run_encode), layer = one decoder layer (configs[0], run_layer),
+longctx = the 131K three-tier cache (configs[3], run_longctx), stack = the
+22-layer decode stack (configs[2], run_stack).
 
 Workload (Llama-3.2-1B-shaped layer): batch 8, 32 query
 heads, 8 KV heads (GQA 4), head_dim 64, 32768-token context = 1024 hot fp16
@@ -933,6 +936,220 @@ def run_longctx(args) -> None:
     cache.close()
 
 
+# ---------------------------------------------------------------------------
+# 22-layer decode stack
+# ---------------------------------------------------------------------------
+# TinyLlama-1.1B-shaped stack of RFSNDecoderLayerMLX, random init: hidden 2048,
+# 32 q heads, 4 KV heads, D 64, global batch 32, 16384-token context per
+# sequence (hot = first 512 fp16 tokens, warm = the rest as PQ 8x8 K=256, no
+# RVQ), seed 2.  A step decodes one token for the whole batch through all 22
+# layers: RMSNorm, q/k/v projections, spill-encode of the new K/V into the warm
+# store, fused decode attention, o_proj, RMSNorm, GELU FFN, residuals.
+# Strong scaling: the global batch of 32 is split by sequence over the ranks
+# (32/N each); every rank holds all 22 layers' weights; after each step the
+# final hidden states are all-gathered over NCCL.
+
+STACK = dict(layers=22, hidden=2048, q_heads=32, kv_heads=4, head_dim=64, batch=32, context=16384, hot=512, M=8,
+             ds=8, K=256, seed=2)
+
+
+def stack_weight_bytes() -> int:
+    c = STACK
+    h, qd, kd = c["hidden"], c["q_heads"] * c["head_dim"], c["kv_heads"] * c["head_dim"]
+    per_layer = 2 * h * qd + 2 * h * kd + 2 * h * (2 * h)  # q, o; k, v; FFN up, down (2x)
+    return c["layers"] * per_layer * 2
+
+
+def stack_attn_bytes(b_local: int) -> int:
+    c = STACK
+    warm = c["context"] - c["hot"]
+    per_row = c["hot"] * 2 * c["head_dim"] * 2 + warm * 2 * c["M"]
+    return c["layers"] * (b_local * c["kv_heads"] * per_row + 2 * b_local * c["q_heads"] * c["head_dim"] * 2)
+
+
+def stack_config(b_local: int, world: int, dev) -> "object":
+    from apple_b200.storage import RFSNConfig
+    c = STACK
+    return RFSNConfig(hidden_dim=c["hidden"], num_heads=c["q_heads"], num_kv_heads=c["kv_heads"],
+                      head_dim=c["head_dim"], num_layers=c["layers"], num_subspaces=c["M"], subspace_dim=c["ds"],
+                      num_rvq_layers=0, hot_capacity=c["hot"], warm_capacity=c["context"] + 512, block_size_seq=128,
+                      batch_size=b_local, device=str(dev),
+                      disk_cache_dir=str(ROOT / "gpurun_out" / "bench_stack_cold"))
+
+
+def stack_setup(dev, b_local: int, rank: int, world: int, prefill: int):
+    """22 layers with caches holding `prefill` tokens of seeded N(0,1) K/V per sequence; PQ
+    codebooks are seeded samples of each layer's own prefill vectors (k-means init)."""
+    import torch
+    from apple_b200.layer import RFSNDecoderLayerMLX
+    c = STACK
+    cfg = stack_config(b_local, world, dev)
+    g = torch.Generator(device=dev).manual_seed(c["seed"] * 1000 + rank)
+    D, M, ds = c["head_dim"], c["M"], c["ds"]
+    layers = []
+    for i in range(c["layers"]):
+        layer = RFSNDecoderLayerMLX(cfg, layer_idx=i, weight_dtype=torch.float16, init="normal", seed=c["seed"])
+        k = torch.randn((b_local, prefill, c["kv_heads"], D), generator=g, device=dev).half()
+        v = torch.randn((b_local, prefill, c["kv_heads"], D), generator=g, device=dev).half()
+        flat = torch.cat([k[:, ::31].reshape(-1, D), v[:, ::31].reshape(-1, D)], 0)
+        idx = torch.randint(0, flat.shape[0], (M, c["K"]), generator=g, device=dev)
+        layer.quantizer.pq.codebooks = torch.stack([flat[idx[m], m * ds:(m + 1) * ds] for m in range(M)]).contiguous()
+        layer.cache.update(k, v, layer.quantizer)
+        del k, v, flat
+        layers.append(layer)
+    torch.cuda.synchronize()
+    return cfg, layers
+
+
+def stack_cpu_baseline(prefill: int = 16380, steps: int = 2) -> dict:
+    """The numpy decoder layer (oracle/restate.py) at the configs[2] layer shape for ONE
+    sequence and ONE layer; the 22-layer x 32-sequence step time is extrapolated from it."""
+    from oracle import restate as R
+    c = STACK
+    rng = np.random.default_rng(c["seed"])
+    h, D = c["hidden"], c["head_dim"]
+    qd, kd = c["q_heads"] * D, c["kv_heads"] * D
+    shapes = dict(q_proj=(qd, h), k_proj=(kd, h), v_proj=(kd, h), o_proj=(h, qd), ffn_up=(2 * h, h),
+                  ffn_down=(h, 2 * h))
+    w = {k: (rng.standard_normal(sh, dtype=np.float32) / np.sqrt(sh[1])).astype(np.float16) for k, sh in shapes.items()}
+    k = rng.standard_normal((1, prefill, c["kv_heads"], D), dtype=np.float32).astype(np.float16)
+    v = rng.standard_normal((1, prefill, c["kv_heads"], D), dtype=np.float32).astype(np.float16)
+    flat = k[0].reshape(-1, D)
+    idx = rng.integers(0, flat.shape[0], (c["M"], c["K"]))
+    cbs = np.stack([flat[idx[m], m * c["ds"]:(m + 1) * c["ds"]] for m in range(c["M"])]).astype(np.float16)
+    cfg = R.OracleConfig(hidden_dim=h, num_heads=c["q_heads"], num_kv_heads=c["kv_heads"], head_dim=D,
+                         num_subspaces=c["M"], subspace_dim=c["ds"], num_rvq_layers=0, hot_capacity=c["hot"],
+                         warm_capacity=c["context"] + 512, block_size_seq=128)
+    layer = R.OracleDecoderLayer(cfg, R.Quantizer(cbs, np.zeros((0, 256, D), np.float16), 0.0), w)
+    layer.cache.update(k, v)
+    x = rng.standard_normal((1, steps + 1, h), dtype=np.float32).astype(np.float16)
+    layer(x[:, :1], use_cache=True)  # warm-up
+    t0 = time.perf_counter()
+    for t in range(steps):
+        layer(x[:, t + 1:t + 2], use_cache=True)
+    dt = (time.perf_counter() - t0) / steps
+    full = dt * c["layers"] * c["batch"]
+    return {"value": 1.0 / full, "unit": "steps/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"numpy decoder layer (configs[2] shape), one sequence x one layer at {prefill + 1} tokens, "
+                      f"mean of {steps} decode steps = {dt * 1e3:.1f} ms; step time extrapolated x{c['layers']} "
+                      f"layers x{c['batch']} sequences"}
+
+
+def run_stack(args) -> None:
+    import torch
+    import torch.distributed as dist
+    c = STACK
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if c["batch"] % world:
+        raise SystemExit(f"global batch {c['batch']} does not split over {world} ranks")
+    b_local = c["batch"] // world
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    warm_steps = max(3, args.warmup)
+    # prefill so that the captured step attends over exactly `context` tokens
+    prefill = c["context"] - warm_steps - 1
+    cfg, layers = stack_setup(dev, b_local, rank, world, prefill)
+    gx = torch.Generator().manual_seed(c["seed"])
+    x_all = torch.randn((c["batch"], 1, c["hidden"]), generator=gx).half()
+    x = x_all[rank * b_local:(rank + 1) * b_local].to(dev)
+    out = torch.empty_like(x)
+    gathered = torch.empty((c["batch"], 1, c["hidden"]), dtype=torch.float16, device=dev) if world > 1 else None
+
+    def step(inp):
+        hcur = inp
+        for layer in layers:
+            hcur = layer(hcur, use_cache=True)
+        return hcur
+
+    for _ in range(warm_steps):  # eager steps: sizes workspaces, casts weights, advances the caches
+        out.copy_(step(x))
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        out.copy_(step(x))
+    ctx = layers[0].cache.total_tokens
+    torch.cuda.synchronize()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev, active=(rank == 0), devices=world) as clocks:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+            if world > 1:
+                dist.all_gather_into_tensor(gathered, out)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    # e2e: public API, each step's input row from pinned host memory, output read back to host;
+    # the caches advance one token per step (eager launches, no graph)
+    hx = x_all[rank * b_local:(rank + 1) * b_local].pin_memory()
+    hout = torch.empty_like(hx).pin_memory()
+    n_e2e = 5
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(n_e2e):
+        y = step(hx.to(dev, non_blocking=True))
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, y)
+        hout.copy_(y)
+    e2e_s = (time.perf_counter() - t0) / n_e2e
+    if world > 1:
+        t = torch.tensor([e2e_s], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    del graph
+    nbytes = stack_weight_bytes() + stack_attn_bytes(b_local)
+    peak, _ = measured_peak()
+    achieved = nbytes / (ms * 1e-3) / 1e9
+    if rank == 0:
+        line = {
+            "metric": "22-layer decode tokens/s (16K ctx, batch 32, PQ 8x8)", "value": c["batch"] * 1e3 / ms,
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": warm_steps, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f16 operands, f32 accumulate", "data": "synthetic",
+            "config": {"workload": "BASELINE configs[2]: TinyLlama-1.1B-shaped 22-layer stack, random init",
+                       "global_batch": c["batch"], "batch_per_gpu": b_local, "seq_len": ctx,
+                       "hot": "first 512 tokens fp16", "warm": "PQ 8x8 K256", "parallelism": f"batch-shard dp{world}",
+                       "step": "one decode token for the batch through 22 RFSNDecoderLayerMLX layers, replayed "
+                               "from a CUDA graph (each replay re-encodes the step's token into the same warm slot)",
+                       "l2": f"weights {stack_weight_bytes() / 1e9:.2f} GB per step > L2, no flush"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": None, "bytes_per_step": nbytes, "weight_bytes": stack_weight_bytes(),
+                         "kv_bytes": stack_attn_bytes(b_local)},
+            "e2e": {"value": c["batch"] / e2e_s, "unit": "tokens/s",
+                    "h2d_bytes_per_step": hx.numel() * 2, "d2h_bytes_per_step": hx.numel() * 2,
+                    "api": "RFSNDecoderLayerMLX.__call__(use_cache=True) x 22, eager, caches advancing"},
+            "gpu_launches": args.steps * c["layers"] * 3, "clocks": clocks.summary()}
+        if world == 1:
+            line["cpu_baseline"] = stack_cpu_baseline()
+            line["cpu_baseline"]["value"] *= c["batch"]
+            line["cpu_baseline"]["unit"] = "tokens/s"
+        print(json.dumps(line))
+    for layer in layers:
+        layer.cache.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main() -> None:
     if len(sys.argv) == 4 and sys.argv[1] == "--clock-sampler":
         clock_sampler_main(sys.argv[2], sys.argv[3])
@@ -942,11 +1159,25 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "encode", "layer", "longctx"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "encode", "layer", "longctx", "stack"],
                     help="decode: fused decode attention (configs[1], the headline); encode: spill encoder "
-                         "(configs[4]); layer: single decoder layer decode (configs[0])")
+                         "(configs[4]); layer: single decoder layer decode (configs[0]); longctx: 131K three-tier "
+                         "decode (configs[3]); stack: 22-layer decode stack (configs[2])")
     args = ap.parse_args()
-    if args.workload == "longctx":
+    if args.workload == "stack":
+        if args.impl == "reference":
+            if int(os.environ.get("RANK", "0")) == 0:
+                cb = stack_cpu_baseline()
+                cb["value"] *= STACK["batch"]
+                cb["unit"] = "tokens/s"
+                print(json.dumps({"metric": "22-layer decode tokens/s (16K ctx, batch 32, PQ 8x8)",
+                                  "value": cb["value"], "unit": "tokens/s", "n_gpus": args.gpus,
+                                  "impl": "reference", "cpu_baseline": cb,
+                                  "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                                          "d2h_bytes_per_step": 0}}))
+        else:
+            run_stack(args)
+    elif args.workload == "longctx":
         if args.impl == "reference":
             if int(os.environ.get("RANK", "0")) == 0:
                 print(json.dumps({"impl": "reference", "unavailable": "no CPU arm for the 131K three-tier workload: "

@@ -261,3 +261,59 @@ def test_calibration_golden():
     np.testing.assert_allclose(cb.astype(np.float32), g["codebooks"].astype(np.float32), atol=4e-3, rtol=0)
     np.testing.assert_allclose(metrics["avg_distortion"], g["avg_distortion"], rtol=1e-3)
     np.testing.assert_allclose(metrics["sparsity_fraction"], g["sparsity_fraction"], atol=1e-3)
+
+
+def _stack(tmp_path, n_layers, batch, prefill):
+    cfg = RFSNConfig(hidden_dim=256, num_heads=8, num_kv_heads=2, head_dim=64, num_subspaces=8, subspace_dim=8,
+                     num_rvq_layers=0, hot_capacity=32, warm_capacity=1024, block_size_seq=16, batch_size=batch,
+                     disk_cache_dir=str(tmp_path))
+    g = torch.Generator(device="cuda").manual_seed(7)
+    layers = []
+    for i in range(n_layers):
+        layer = RFSNDecoderLayerMLX(cfg, layer_idx=i, weight_dtype=torch.float16, init="normal", seed=2)
+        k = torch.randn((batch, prefill, 2, 64), generator=g, device="cuda").half()
+        v = torch.randn((batch, prefill, 2, 64), generator=g, device="cuda").half()
+        idx = torch.randint(0, batch * prefill * 2, (8, 256), generator=g, device="cuda")
+        flat = k.reshape(-1, 64)
+        layer.quantizer.pq.codebooks = torch.stack([flat[idx[m], 8 * m:8 * m + 8] for m in range(8)]).contiguous()
+        layer.cache.update(k, v, layer.quantizer)
+        layers.append(layer)
+    return layers
+
+
+def test_decoder_stack_graph_replay_matches_eager(tmp_path):
+    """A multi-layer cache-backed decode step through the public layer API captures into one
+    CUDA graph (no host syncs or pageable uploads on the path); its replay equals the eager
+    step at the same position, and a second replay reproduces it."""
+    eager = _stack(tmp_path / "a", 3, 2, 200)
+    graphed = _stack(tmp_path / "b", 3, 2, 200)
+    g = torch.Generator().manual_seed(11)
+    xs = torch.randn((4, 2, 1, 256), generator=g).half().cuda()
+
+    def step(layers, x):
+        for layer in layers:
+            x = layer(x, use_cache=True)
+        return x
+
+    ref = [step(eager, xs[t]) for t in range(4)]
+    for t in range(3):
+        step(graphed, xs[t])
+    torch.cuda.synchronize()
+    xin = xs[3].clone()
+    out = torch.empty_like(xin)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        out.copy_(step(graphed, xin))
+    graph.replay()
+    torch.cuda.synchronize()
+    first = out.clone()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(first, out)
+    close(first.float().cpu().numpy(), ref[3].float().cpu().numpy(), "graph replay vs eager")
+    assert graphed[0].cache.total_tokens == eager[0].cache.total_tokens == 204
+    del graph
+    for layer in eager + graphed:
+        layer.cache.close()
