@@ -691,9 +691,11 @@ static int make_plan(const rfsn_attn_args* a, const rfsn_quantizer* qz, Plan& pl
   if (p.stage_bytes < 8 * 1024 || pl.smem > kMaxSmem) return RFSN_ERR_UNSUPPORTED;
   // the ring sits after the fixed regions
   p.ring_off = (int)(pl.smem - (int64_t)p.stages * p.stage_bytes);
-  // compressed tile: whole 16-token blocks (<= 64) that fit one stage
+  // compressed tile: the whole 16-token blocks that fit one stage (small blocks, e.g.
+  // PQ-only codes at 256 B per block, make tiles of up to 192 blocks: every tile
+  // costs a ring round trip, so tiles are as large as the stage allows)
   p.tile_blocks = p.stage_bytes / p.lay.block_bytes;
-  if (p.tile_blocks > 64) p.tile_blocks = 64;
+  if (p.tile_blocks > 1024) p.tile_blocks = 1024;
   if (p.tile_blocks < 2) return RFSN_ERR_UNSUPPORTED;
   p.tile_dense = (p.stage_bytes / (4 * p.D)) / 16 * 16;  // K and V rows of fp16
   if (p.tile_dense < 16) return RFSN_ERR_UNSUPPORTED;

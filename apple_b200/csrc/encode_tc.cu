@@ -15,6 +15,11 @@
 //        r . R[c] and the same epilogue.
 //   sparse / stores: one lane per vector, CUDA cores.
 //
+// Small batches (a decode step appends one token per row: a few groups) run in
+// split mode: the M warps of a group search one subspace each into the group
+// leader's tiles, then the leader finishes the group, so the serial PQ search
+// per warp is 1/M as long.  Large batches keep one warp per group.
+//
 // Products of fp16 values are exact in fp32, so d differs from the reference
 // only through the dot products' summation order: codes can differ only where
 // two candidates tie to fp32 rounding.  Operand fragments are read straight
@@ -45,6 +50,7 @@ struct EncTcParams {
   const uint16_t* rvq_cb;
   int M, K, L, Kr, S;
   float thr;
+  int split;  // warps per 16-vector group: 1, or M (one warp per PQ subspace, small batches)
   int smem_pq, smem_pqcc, smem_rvq, smem_rcc, smem_warp, warp_bytes;
 };
 
@@ -96,8 +102,15 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1) encode_tc_kernel(const __gri
   // ---- stage codebooks and their squared norms (sequential fp32 sums) ----
   for (int i = threadIdx.x; i < M * K * DS / 8; i += nthr)
     reinterpret_cast<uint4*>(s_pq)[i] = __ldg(reinterpret_cast<const uint4*>(p.pq_cb) + i);
+  if (p.L > 0) {
+    for (int i = threadIdx.x; i < Kr * 8; i += nthr) {
+      const int c = i >> 3, q = i & 7;
+      s_rvq[swz(c, q)] = __ldg(reinterpret_cast<const uint4*>(p.rvq_cb) + i);
+    }
+  }
+  __syncthreads();  // norms are summed from the staged copies
   for (int i = threadIdx.x; i < M * K; i += nthr) {
-    const uint16_t* c = p.pq_cb + (size_t)i * DS;
+    const uint16_t* c = s_pq + (size_t)i * DS;
     float s = 0.f;
 #pragma unroll
     for (int k = 0; k < DS; ++k) {
@@ -107,24 +120,30 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1) encode_tc_kernel(const __gri
     s_pqcc[i] = s;
   }
   if (p.L > 0) {
-    for (int i = threadIdx.x; i < Kr * 8; i += nthr) {
-      const int c = i >> 3, q = i & 7;
-      s_rvq[swz(c, q)] = __ldg(reinterpret_cast<const uint4*>(p.rvq_cb) + i);
-    }
     for (int i = threadIdx.x; i < Kr; i += nthr) {
-      const uint16_t* c = p.rvq_cb + (size_t)i * kTcD;
       float s = 0.f;
-      for (int k = 0; k < kTcD; ++k) {
-        const float v = h2f(c[k]);
-        s = __fmaf_rn(v, v, s);
+      for (int q = 0; q < 8; ++q) {
+        const uint4 r = s_rvq[swz(i, q)];
+        const uint32_t w4[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[k]));
+          s = __fmaf_rn(f.x, f.x, s);
+          s = __fmaf_rn(f.y, f.y, s);
+        }
       }
       s_rcc[i] = s;
     }
   }
   __syncthreads();
 
-  // per-warp tiles
-  unsigned char* wb = smem + p.smem_warp + (size_t)warp * p.warp_bytes;
+  // tiles: each group's leader warp (part 0) owns them; in split mode the group's
+  // other warps write their subspaces' codes into the leader's s_code
+  const int split = p.split;
+  const int gpc = kTcWarps / split;  // groups per CTA and round
+  const int gslot = warp / split, part = warp - gslot * split;
+  const bool lead = part == 0;
+  unsigned char* wb = smem + p.smem_warp + (size_t)(gslot * split) * p.warp_bytes;
   uint4* xt = reinterpret_cast<uint4*>(wb);                    // [16][8 chunks] swizzled x
   uint4* rt = xt + 16 * 8;                                     // [16][8 chunks] swizzled residual
   float* s_xsq = reinterpret_cast<float*>(rt + 16 * 8);        // [16][M]
@@ -137,225 +156,236 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1) encode_tc_kernel(const __gri
   const float INF = __int_as_float(0x7f800000);
   const int64_t ngroups = (p.nvec + 15) / 16;
 
-  for (int64_t g = (int64_t)blockIdx.x * kTcWarps + warp; g < ngroups; g += (int64_t)gridDim.x * kTcWarps) {
-    // ---- x tile ----
-#pragma unroll
-    for (int s = 0; s < 4; ++s) {
-      const int i = (lane >> 3) + 4 * s, q = lane & 7;
-      const int64_t v = g * 16 + i;
-      uint4 val = make_uint4(0u, 0u, 0u, 0u);
-      if (v < p.nvec) {
-        const int64_t h = v % p.heads, t = (v / p.heads) % p.tokens, b = v / (p.heads * p.tokens);
-        val = __ldg(reinterpret_cast<const uint4*>(p.x + b * p.sb + t * p.st + h * p.sh) + q);
-      }
-      xt[swz(i, q)] = val;
-    }
-    __syncwarp();
-    // |x_m|^2 per (vector, subspace), sequential fp32 (quantization.py:94)
-    for (int idx = lane; idx < 16 * M; idx += 32) {
-      const int i = idx / M, m = idx - i * M;
-      const uint16_t* xr = reinterpret_cast<const uint16_t*>(&xt[swz(i, (m * DS) >> 3)]) + ((m * DS) & 7);
-      float s = 0.f;
-#pragma unroll
-      for (int k = 0; k < DS; ++k) {
-        const float v = h2f(xr[k]);
-        s = __fmaf_rn(v, v, s);
-      }
-      s_xsq[idx] = s;
-    }
-    __syncwarp();
-
-    // ---- PQ: per-subspace argmin over K centroids ----
-    for (int m = 0; m < M; ++m) {
-      const int chunk = (m * DS) >> 3;
-      const uint32_t* x0 = reinterpret_cast<const uint32_t*>(&xt[swz(r0, chunk)]);
-      const uint32_t* x1 = reinterpret_cast<const uint32_t*>(&xt[swz(r0 + 8, chunk)]);
-      const uint32_t a0 = x0[qd], a1 = x1[qd];
-      const float xx0 = s_xsq[r0 * M + m], xx1 = s_xsq[(r0 + 8) * M + m];
-      // B lanes that carry this subspace's dims (4-dim subspaces fill half of k)
-      const bool bl = DS == 8 || ((qd >> 1) == (m & 1));
-      const uint32_t* cbm = reinterpret_cast<const uint32_t*>(s_pq + (size_t)m * K * DS);
-      const float* ccm = s_pqcc + m * K;
-      float b00 = INF, b01 = INF, b10 = INF, b11 = INF;  // rows r0 / r0+8, column parity 0 / 1
-      int i00 = 0, i01 = 0, i10 = 0, i11 = 0;
-#pragma unroll 4
-      for (int nt = 0; nt < K / 8; ++nt) {
-        const int cb = nt * 8 + r0;  // centroid of this lane's B column
-        const uint32_t b = bl ? cbm[(cb * DS >> 1) + (DS == 8 ? qd : (qd & 1))] : 0u;
-        float c[4] = {0.f, 0.f, 0.f, 0.f};
-        mma1688(c, a0, a1, b);
-        const int code = nt * 8 + 2 * qd;
-        const float2 cc = *reinterpret_cast<const float2*>(ccm + code);
-        take_min(__fadd_rn(__fmaf_rn(-2.f, c[0], xx0), cc.x), code, b00, i00);
-        take_min(__fadd_rn(__fmaf_rn(-2.f, c[1], xx0), cc.y), code + 1, b01, i01);
-        take_min(__fadd_rn(__fmaf_rn(-2.f, c[2], xx1), cc.x), code, b10, i10);
-        take_min(__fadd_rn(__fmaf_rn(-2.f, c[3], xx1), cc.y), code + 1, b11, i11);
-      }
-      merge_min(b00, i00, b01, i01);
-      merge_min(b10, i10, b11, i11);
-      quad_min(b00, i00);
-      quad_min(b10, i10);
-      if (qd == 0) {
-        s_code[r0 * M + m] = (uint8_t)i00;
-        s_code[(r0 + 8) * M + m] = (uint8_t)i10;
-      }
-    }
-    __syncwarp();
-
-    // ---- residual r = fp16(x - c): one rounding of the exact difference ----
-    for (int idx = lane; idx < 16 * 8; idx += 32) {
-      const int i = idx >> 3, q = idx & 7;
-      const uint4 xv = xt[swz(i, q)];
-      uint4 cv;
-      if constexpr (DS == 8) {
-        cv = *reinterpret_cast<const uint4*>(s_pq + ((size_t)q * K + s_code[i * M + q]) * 8);
-      } else {
-        const uint2 lo = *reinterpret_cast<const uint2*>(s_pq + ((size_t)(2 * q) * K + s_code[i * M + 2 * q]) * 4);
-        const uint2 hi =
-            *reinterpret_cast<const uint2*>(s_pq + ((size_t)(2 * q + 1) * K + s_code[i * M + 2 * q + 1]) * 4);
-        cv = make_uint4(lo.x, lo.y, hi.x, hi.y);
-      }
-      uint4 rv;
-      rv.x = hsub2_u32(xv.x, cv.x); rv.y = hsub2_u32(xv.y, cv.y);
-      rv.z = hsub2_u32(xv.z, cv.z); rv.w = hsub2_u32(xv.w, cv.w);
-      rt[swz(i, q)] = rv;
-      const int64_t v = g * 16 + i;
-      if (p.residual_out && v < p.nvec) {
-        const int64_t h = v % p.heads, t = (v / p.heads) % p.tokens, b = v / (p.heads * p.tokens);
-        reinterpret_cast<uint4*>(p.residual_out + b * p.sb + t * p.st + h * p.sh)[q] = rv;
-      }
-    }
-    __syncwarp();
-
-    // ---- RVQ, one layer (quantization.py:216-250) ----
-    if (p.L > 0) {
-      if (lane < 16) {  // norm gate, sequential fp32
-        float nn = 0.f;
-        for (int q = 0; q < 8; ++q) {
-          const uint4 rv = rt[swz(lane, q)];
-          const uint32_t w4[4] = {rv.x, rv.y, rv.z, rv.w};
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[k]));
-            nn = __fmaf_rn(f.x, f.x, nn);
-            nn = __fmaf_rn(f.y, f.y, nn);
-          }
-        }
-        s_rr[lane] = nn;
-        s_act[lane] = __fsqrt_rn(nn) > p.thr ? 1 : 0;
-      }
-      __syncwarp();
-      uint32_t a[4][4];
+  // the round count is the same for every warp of the CTA (split mode syncs the CTA)
+  for (int64_t base = (int64_t)blockIdx.x * gpc; base < ngroups; base += (int64_t)gridDim.x * gpc) {
+    const int64_t g = base + gslot;
+    const bool live = g < ngroups;
+    // ---- x tile (leader) ----
+    if (live && lead) {
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
-        a[s][0] = reinterpret_cast<const uint32_t*>(&rt[swz(r0, 2 * s)])[qd];
-        a[s][1] = reinterpret_cast<const uint32_t*>(&rt[swz(r0 + 8, 2 * s)])[qd];
-        a[s][2] = reinterpret_cast<const uint32_t*>(&rt[swz(r0, 2 * s + 1)])[qd];
-        a[s][3] = reinterpret_cast<const uint32_t*>(&rt[swz(r0 + 8, 2 * s + 1)])[qd];
-      }
-      const float rr0 = s_rr[r0], rr1 = s_rr[r0 + 8];
-      float b00 = INF, b01 = INF, b10 = INF, b11 = INF;
-      int i00 = 0, i01 = 0, i10 = 0, i11 = 0;
-#pragma unroll 2
-      for (int nt = 0; nt < Kr / 8; ++nt) {
-        const int cb = nt * 8 + r0;
-        float c[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int s = 0; s < 4; ++s) {
-          const uint32_t bb0 = reinterpret_cast<const uint32_t*>(&s_rvq[swz(cb, 2 * s)])[qd];
-          const uint32_t bb1 = reinterpret_cast<const uint32_t*>(&s_rvq[swz(cb, 2 * s + 1)])[qd];
-          mma16816(c, a[s], bb0, bb1);
+        const int i = (lane >> 3) + 4 * s, q = lane & 7;
+        const int64_t v = g * 16 + i;
+        uint4 val = make_uint4(0u, 0u, 0u, 0u);
+        if (v < p.nvec) {
+          const int64_t h = v % p.heads, t = (v / p.heads) % p.tokens, b = v / (p.heads * p.tokens);
+          val = __ldg(reinterpret_cast<const uint4*>(p.x + b * p.sb + t * p.st + h * p.sh) + q);
         }
-        const int code = nt * 8 + 2 * qd;
-        const float2 cc = *reinterpret_cast<const float2*>(s_rcc + code);
-        take_min(__fadd_rn(__fmaf_rn(-2.f, c[0], rr0), cc.x), code, b00, i00);
-        take_min(__fadd_rn(__fmaf_rn(-2.f, c[1], rr0), cc.y), code + 1, b01, i01);
-        take_min(__fadd_rn(__fmaf_rn(-2.f, c[2], rr1), cc.x), code, b10, i10);
-        take_min(__fadd_rn(__fmaf_rn(-2.f, c[3], rr1), cc.y), code + 1, b11, i11);
+        xt[swz(i, q)] = val;
       }
-      merge_min(b00, i00, b01, i01);
-      merge_min(b10, i10, b11, i11);
-      quad_min(b00, i00);
-      quad_min(b10, i10);
-      if (qd == 0) {
-        s_rcode[r0] = s_act[r0] ? (uint8_t)i00 : 0;
-        s_rcode[r0 + 8] = s_act[r0 + 8] ? (uint8_t)i10 : 0;
+      __syncwarp();
+      // |x_m|^2 per (vector, subspace), sequential fp32 (quantization.py:94)
+      for (int idx = lane; idx < 16 * M; idx += 32) {
+        const int i = idx / M, m = idx - i * M;
+        const uint16_t* xr = reinterpret_cast<const uint16_t*>(&xt[swz(i, (m * DS) >> 3)]) + ((m * DS) & 7);
+        float s = 0.f;
+#pragma unroll
+        for (int k = 0; k < DS; ++k) {
+          const float v = h2f(xr[k]);
+          s = __fmaf_rn(v, v, s);
+        }
+        s_xsq[idx] = s;
       }
       __syncwarp();
     }
+    if (split > 1) __syncthreads();
 
-    // ---- sparse top-S of the fp16 decode error, and the code stores: one lane per vector ----
-    if (lane < 16) {
-      const int i = lane;
-      const int64_t v = g * 16 + i;
-      if (v < p.nvec) {
-        const int64_t h = v % p.heads, t = (v / p.heads) % p.tokens, b = v / (p.heads * p.tokens);
-        const int64_t row = b * p.heads + h, tok = p.first + t;
-        const int fk = p.kv * 5;
-        uint8_t* f_pq = p.data + field_byte(p.lay, p.rows, p.cap, p.slot, row, tok, fk + 0);
-        for (int m = 0; m < M; ++m) f_pq[m] = s_code[i * M + m];
-        if (p.L > 0) {
-          p.data[field_byte(p.lay, p.rows, p.cap, p.slot, row, tok, fk + 1)] = s_rcode[i];
-          p.data[field_byte(p.lay, p.rows, p.cap, p.slot, row, tok, fk + 2)] = s_act[i];
+    // ---- PQ: per-subspace argmin over K centroids (subspaces part, part + split, ...) ----
+    if (live) {
+      for (int m = part; m < M; m += split) {
+        const int chunk = (m * DS) >> 3;
+        const uint32_t* x0 = reinterpret_cast<const uint32_t*>(&xt[swz(r0, chunk)]);
+        const uint32_t* x1 = reinterpret_cast<const uint32_t*>(&xt[swz(r0 + 8, chunk)]);
+        const uint32_t a0 = x0[qd], a1 = x1[qd];
+        const float xx0 = s_xsq[r0 * M + m], xx1 = s_xsq[(r0 + 8) * M + m];
+        // B lanes that carry this subspace's dims (4-dim subspaces fill half of k)
+        const bool bl = DS == 8 || ((qd >> 1) == (m & 1));
+        const uint32_t* cbm = reinterpret_cast<const uint32_t*>(s_pq + (size_t)m * K * DS);
+        const float* ccm = s_pqcc + m * K;
+        float b00 = INF, b01 = INF, b10 = INF, b11 = INF;  // rows r0 / r0+8, column parity 0 / 1
+        int i00 = 0, i01 = 0, i10 = 0, i11 = 0;
+#pragma unroll 4
+        for (int nt = 0; nt < K / 8; ++nt) {
+          const int cb = nt * 8 + r0;  // centroid of this lane's B column
+          const uint32_t b = bl ? cbm[(cb * DS >> 1) + (DS == 8 ? qd : (qd & 1))] : 0u;
+          float c[4] = {0.f, 0.f, 0.f, 0.f};
+          mma1688(c, a0, a1, b);
+          const int code = nt * 8 + 2 * qd;
+          const float2 cc = *reinterpret_cast<const float2*>(ccm + code);
+          take_min(__fadd_rn(__fmaf_rn(-2.f, c[0], xx0), cc.x), code, b00, i00);
+          take_min(__fadd_rn(__fmaf_rn(-2.f, c[1], xx0), cc.y), code + 1, b01, i01);
+          take_min(__fadd_rn(__fmaf_rn(-2.f, c[2], xx1), cc.x), code, b10, i10);
+          take_min(__fadd_rn(__fmaf_rn(-2.f, c[3], xx1), cc.y), code + 1, b11, i11);
         }
-        if (p.S > 0) {
-          uint8_t* f_spi = p.data + field_byte(p.lay, p.rows, p.cap, p.slot, row, tok, fk + 3);
-          uint16_t* f_spv =
-              reinterpret_cast<uint16_t*>(p.data + field_byte(p.lay, p.rows, p.cap, p.slot, row, tok, fk + 4));
-          // err = x - fp16(pq + rvq) in fp32 (quantization.py:310-319 decode, then the error)
-          float err[kTcD];
-          const bool act = p.L > 0 && s_act[i];
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const uint4 xv = xt[swz(i, q)];
-            uint4 cv;  // the decode: PQ centroid, plus the RVQ row in fp16 when active
-            if constexpr (DS == 8) {
-              cv = *reinterpret_cast<const uint4*>(s_pq + ((size_t)q * K + s_code[i * M + q]) * 8);
-            } else {
-              const uint2 lo =
-                  *reinterpret_cast<const uint2*>(s_pq + ((size_t)(2 * q) * K + s_code[i * M + 2 * q]) * 4);
-              const uint2 hi =
-                  *reinterpret_cast<const uint2*>(s_pq + ((size_t)(2 * q + 1) * K + s_code[i * M + 2 * q + 1]) * 4);
-              cv = make_uint4(lo.x, lo.y, hi.x, hi.y);
-            }
-            if (act) {
-              const uint4 rr = s_rvq[swz(s_rcode[i], q)];
-              cv.x = hadd2_u32(cv.x, rr.x); cv.y = hadd2_u32(cv.y, rr.y);
-              cv.z = hadd2_u32(cv.z, rr.z); cv.w = hadd2_u32(cv.w, rr.w);
-            }
-            const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
-            const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w};
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const float2 xf = __half22float2(*reinterpret_cast<const __half2*>(&xw[k]));
-              const float2 cf = __half22float2(*reinterpret_cast<const __half2*>(&cw[k]));
-              err[8 * q + 2 * k] = __fsub_rn(xf.x, cf.x);
-              err[8 * q + 2 * k + 1] = __fsub_rn(xf.y, cf.y);
-            }
-          }
-          unsigned long long taken = 0ull;
-          for (int s = 0; s < p.S; ++s) {  // largest |err| not yet taken, ties to the lower index
-            float bm = -1.f;
-            int bi = 0;
-#pragma unroll
-            for (int d = 0; d < kTcD; ++d) {
-              const float mg = ((taken >> d) & 1ull) ? -2.f : fabsf(err[d]);
-              if (mg > bm) {
-                bm = mg;
-                bi = d;
-              }
-            }
-            float ev = 0.f;
-#pragma unroll
-            for (int d = 0; d < kTcD; ++d) ev = d == bi ? err[d] : ev;
-            taken |= 1ull << bi;
-            f_spi[s] = (uint8_t)bi;
-            f_spv[s] = f2h(ev);
-          }
+        merge_min(b00, i00, b01, i01);
+        merge_min(b10, i10, b11, i11);
+        quad_min(b00, i00);
+        quad_min(b10, i10);
+        if (qd == 0) {
+          s_code[r0 * M + m] = (uint8_t)i00;
+          s_code[(r0 + 8) * M + m] = (uint8_t)i10;
         }
       }
     }
-    __syncwarp();
+    if (split > 1) __syncthreads(); else __syncwarp();
+    // ---- the leader finishes the group; every warp meets the same barriers ----
+    if (live && lead) {
+
+      // ---- residual r = fp16(x - c): one rounding of the exact difference ----
+      for (int idx = lane; idx < 16 * 8; idx += 32) {
+        const int i = idx >> 3, q = idx & 7;
+        const uint4 xv = xt[swz(i, q)];
+        uint4 cv;
+        if constexpr (DS == 8) {
+          cv = *reinterpret_cast<const uint4*>(s_pq + ((size_t)q * K + s_code[i * M + q]) * 8);
+        } else {
+          const uint2 lo = *reinterpret_cast<const uint2*>(s_pq + ((size_t)(2 * q) * K + s_code[i * M + 2 * q]) * 4);
+          const uint2 hi =
+              *reinterpret_cast<const uint2*>(s_pq + ((size_t)(2 * q + 1) * K + s_code[i * M + 2 * q + 1]) * 4);
+          cv = make_uint4(lo.x, lo.y, hi.x, hi.y);
+        }
+        uint4 rv;
+        rv.x = hsub2_u32(xv.x, cv.x); rv.y = hsub2_u32(xv.y, cv.y);
+        rv.z = hsub2_u32(xv.z, cv.z); rv.w = hsub2_u32(xv.w, cv.w);
+        rt[swz(i, q)] = rv;
+        const int64_t v = g * 16 + i;
+        if (p.residual_out && v < p.nvec) {
+          const int64_t h = v % p.heads, t = (v / p.heads) % p.tokens, b = v / (p.heads * p.tokens);
+          reinterpret_cast<uint4*>(p.residual_out + b * p.sb + t * p.st + h * p.sh)[q] = rv;
+        }
+      }
+      __syncwarp();
+
+      // ---- RVQ, one layer (quantization.py:216-250) ----
+      if (p.L > 0) {
+        if (lane < 16) {  // norm gate, sequential fp32
+          float nn = 0.f;
+          for (int q = 0; q < 8; ++q) {
+            const uint4 rv = rt[swz(lane, q)];
+            const uint32_t w4[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[k]));
+              nn = __fmaf_rn(f.x, f.x, nn);
+              nn = __fmaf_rn(f.y, f.y, nn);
+            }
+          }
+          s_rr[lane] = nn;
+          s_act[lane] = __fsqrt_rn(nn) > p.thr ? 1 : 0;
+        }
+        __syncwarp();
+        uint32_t a[4][4];
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+          a[s][0] = reinterpret_cast<const uint32_t*>(&rt[swz(r0, 2 * s)])[qd];
+          a[s][1] = reinterpret_cast<const uint32_t*>(&rt[swz(r0 + 8, 2 * s)])[qd];
+          a[s][2] = reinterpret_cast<const uint32_t*>(&rt[swz(r0, 2 * s + 1)])[qd];
+          a[s][3] = reinterpret_cast<const uint32_t*>(&rt[swz(r0 + 8, 2 * s + 1)])[qd];
+        }
+        const float rr0 = s_rr[r0], rr1 = s_rr[r0 + 8];
+        float b00 = INF, b01 = INF, b10 = INF, b11 = INF;
+        int i00 = 0, i01 = 0, i10 = 0, i11 = 0;
+#pragma unroll 2
+        for (int nt = 0; nt < Kr / 8; ++nt) {
+          const int cb = nt * 8 + r0;
+          float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int s = 0; s < 4; ++s) {
+            const uint32_t bb0 = reinterpret_cast<const uint32_t*>(&s_rvq[swz(cb, 2 * s)])[qd];
+            const uint32_t bb1 = reinterpret_cast<const uint32_t*>(&s_rvq[swz(cb, 2 * s + 1)])[qd];
+            mma16816(c, a[s], bb0, bb1);
+          }
+          const int code = nt * 8 + 2 * qd;
+          const float2 cc = *reinterpret_cast<const float2*>(s_rcc + code);
+          take_min(__fadd_rn(__fmaf_rn(-2.f, c[0], rr0), cc.x), code, b00, i00);
+          take_min(__fadd_rn(__fmaf_rn(-2.f, c[1], rr0), cc.y), code + 1, b01, i01);
+          take_min(__fadd_rn(__fmaf_rn(-2.f, c[2], rr1), cc.x), code, b10, i10);
+          take_min(__fadd_rn(__fmaf_rn(-2.f, c[3], rr1), cc.y), code + 1, b11, i11);
+        }
+        merge_min(b00, i00, b01, i01);
+        merge_min(b10, i10, b11, i11);
+        quad_min(b00, i00);
+        quad_min(b10, i10);
+        if (qd == 0) {
+          s_rcode[r0] = s_act[r0] ? (uint8_t)i00 : 0;
+          s_rcode[r0 + 8] = s_act[r0 + 8] ? (uint8_t)i10 : 0;
+        }
+        __syncwarp();
+      }
+
+      // ---- sparse top-S of the fp16 decode error, and the code stores: one lane per vector ----
+      if (lane < 16) {
+        const int i = lane;
+        const int64_t v = g * 16 + i;
+        if (v < p.nvec) {
+          const int64_t h = v % p.heads, t = (v / p.heads) % p.tokens, b = v / (p.heads * p.tokens);
+          const int64_t row = b * p.heads + h, tok = p.first + t;
+          const int fk = p.kv * 5;
+          uint8_t* f_pq = p.data + field_byte(p.lay, p.rows, p.cap, p.slot, row, tok, fk + 0);
+          for (int m = 0; m < M; ++m) f_pq[m] = s_code[i * M + m];
+          if (p.L > 0) {
+            p.data[field_byte(p.lay, p.rows, p.cap, p.slot, row, tok, fk + 1)] = s_rcode[i];
+            p.data[field_byte(p.lay, p.rows, p.cap, p.slot, row, tok, fk + 2)] = s_act[i];
+          }
+          if (p.S > 0) {
+            uint8_t* f_spi = p.data + field_byte(p.lay, p.rows, p.cap, p.slot, row, tok, fk + 3);
+            uint16_t* f_spv =
+                reinterpret_cast<uint16_t*>(p.data + field_byte(p.lay, p.rows, p.cap, p.slot, row, tok, fk + 4));
+            // err = x - fp16(pq + rvq) in fp32 (quantization.py:310-319 decode, then the error)
+            float err[kTcD];
+            const bool act = p.L > 0 && s_act[i];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const uint4 xv = xt[swz(i, q)];
+              uint4 cv;  // the decode: PQ centroid, plus the RVQ row in fp16 when active
+              if constexpr (DS == 8) {
+                cv = *reinterpret_cast<const uint4*>(s_pq + ((size_t)q * K + s_code[i * M + q]) * 8);
+              } else {
+                const uint2 lo =
+                    *reinterpret_cast<const uint2*>(s_pq + ((size_t)(2 * q) * K + s_code[i * M + 2 * q]) * 4);
+                const uint2 hi =
+                    *reinterpret_cast<const uint2*>(s_pq + ((size_t)(2 * q + 1) * K + s_code[i * M + 2 * q + 1]) * 4);
+                cv = make_uint4(lo.x, lo.y, hi.x, hi.y);
+              }
+              if (act) {
+                const uint4 rr = s_rvq[swz(s_rcode[i], q)];
+                cv.x = hadd2_u32(cv.x, rr.x); cv.y = hadd2_u32(cv.y, rr.y);
+                cv.z = hadd2_u32(cv.z, rr.z); cv.w = hadd2_u32(cv.w, rr.w);
+              }
+              const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+              const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w};
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const float2 xf = __half22float2(*reinterpret_cast<const __half2*>(&xw[k]));
+                const float2 cf = __half22float2(*reinterpret_cast<const __half2*>(&cw[k]));
+                err[8 * q + 2 * k] = __fsub_rn(xf.x, cf.x);
+                err[8 * q + 2 * k + 1] = __fsub_rn(xf.y, cf.y);
+              }
+            }
+            unsigned long long taken = 0ull;
+            for (int s = 0; s < p.S; ++s) {  // largest |err| not yet taken, ties to the lower index
+              float bm = -1.f;
+              int bi = 0;
+#pragma unroll
+              for (int d = 0; d < kTcD; ++d) {
+                const float mg = ((taken >> d) & 1ull) ? -2.f : fabsf(err[d]);
+                if (mg > bm) {
+                  bm = mg;
+                  bi = d;
+                }
+              }
+              float ev = 0.f;
+#pragma unroll
+              for (int d = 0; d < kTcD; ++d) ev = d == bi ? err[d] : ev;
+              taken |= 1ull << bi;
+              f_spi[s] = (uint8_t)bi;
+              f_spv[s] = f2h(ev);
+            }
+          }
+        }
+      }
+    }  // leader
+    if (split > 1) __syncthreads(); else __syncwarp();
   }
 }
 
@@ -396,7 +426,12 @@ int encode_tc_launch(const rfsn_quantizer* qz, const uint16_t* x, int64_t batch,
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t groups = (p.nvec + 15) / 16;
-  const int64_t want = (groups + kTcWarps - 1) / kTcWarps;
+  // split mode (one warp per subspace) when its grid fits in one wave of CTAs: a
+  // decode step's append is a handful of groups, and a warp walking all M subspaces
+  // alone would set the kernel's duration
+  const int64_t split_ctas = (groups * p.M + kTcWarps - 1) / kTcWarps;
+  p.split = (kTcWarps % p.M == 0 && split_ctas <= sms) ? p.M : 1;
+  const int64_t want = p.split > 1 ? split_ctas : (groups + kTcWarps - 1) / kTcWarps;
   const int grid = (int)(want < sms ? want : sms);
   cudaError_t e;
   if (qz->subspace_dim == 8) {

@@ -336,5 +336,30 @@ def decode_attention(qz: QuantizerBuffers, q: torch.Tensor, out: torch.Tensor, s
     return out
 
 
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    """fp16 RMSNorm over the last dim in one launch (fp32 math, fp32 weight)."""
+    _need_cuda(x, "x")
+    if x.dtype != torch.float16 or weight.dtype != torch.float32 or weight.numel() != x.shape[-1]:
+        raise ValueError("rms_norm expects fp16 x [..., dim] and an fp32 weight of dim")
+    x = x.contiguous()
+    w = weight.contiguous()
+    y = torch.empty_like(x)
+    dim = int(x.shape[-1])
+    call("rfsn_rmsnorm_f16", _ptr(x), _ptr(w), _ptr(y), x.numel() // dim if dim else 0, dim, float(eps),
+         _stream(x.device.index))
+    return y
+
+
+def gelu_tanh(x: torch.Tensor) -> torch.Tensor:
+    """Tanh-approximate GELU of fp16 x in one launch, rounded to fp16 after every operation."""
+    _need_cuda(x, "x")
+    if x.dtype != torch.float16:
+        raise ValueError("gelu_tanh expects fp16 input")
+    x = x.contiguous()
+    y = torch.empty_like(x)
+    call("rfsn_gelu_tanh_f16", _ptr(x), _ptr(y), x.numel(), _stream(x.device.index))
+    return y
+
+
 def version() -> int:
     return lib().rfsn_version()

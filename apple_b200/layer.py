@@ -4,7 +4,8 @@
 q/k/v projections -> cache update -> cache-backed fused decode attention (or
 dense causal attention without a cache) -> o_proj + residual -> RMSNorm ->
 GELU FFN (2x) + residual.  Projections are plain torch GEMMs (cuBLAS); the
-attention and every quantizer operation run in librfsn_b200.so.  Extensions:
+attention, every quantizer operation, the RMSNorms and the GELU run in
+librfsn_b200.so (one launch each).  Extensions:
 ``num_kv_heads`` (GQA) and ``batch_size`` > 1 sequences per cache.
 """
 from __future__ import annotations
@@ -17,6 +18,7 @@ from typing import Dict, List, Optional
 
 import torch
 
+from . import kernels as K
 from .attention import _dense_exact_attention, _gelu
 from .cache import RFSNv10KVCacheMLX
 from .quantization import HybridQuantizerMLX
@@ -46,11 +48,16 @@ class _Linear:
 
 
 class _RMSNorm:
+    """RMSNorm with an fp32 weight (mlx.nn.RMSNorm).  fp16 inputs, which are what the layer
+    passes, run as one kernel (rfsn_rmsnorm_f16) with the same operation order."""
+
     def __init__(self, dims: int, device, eps: float = 1e-5):
         self.weight = torch.ones(dims, device=device)
         self.eps = eps
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        if x.dtype == torch.float16 and x.is_cuda:
+            return K.rms_norm(x, self.weight, self.eps)
         xf = x.float()
         return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps) * self.weight).to(x.dtype)
 
@@ -149,7 +156,9 @@ class RFSNDecoderLayerMLX:
         attn_out = self.o_proj(attended.reshape(B, -1, self.num_heads * self.head_dim)).to(residual.dtype)
         hidden = residual + attn_out
         ffn_input = self.ffn_norm(hidden).to(torch.float16)
-        ffn_out = self.ffn_down(_gelu(self.ffn_up(ffn_input))).to(hidden.dtype)
+        up = self.ffn_up(ffn_input)
+        act = K.gelu_tanh(up) if up.dtype == torch.float16 else _gelu(up)  # one launch for the fp16 chain
+        ffn_out = self.ffn_down(act).to(hidden.dtype)
         return hidden + ffn_out
 
 

@@ -199,6 +199,21 @@ int rfsn_cold_prefetch(void* dst_device, const void* src_pinned_host, size_t byt
  * (save_compressed_chunk, storage.py:117-135). */
 int rfsn_cold_evict(void* dst_pinned_host, const void* src_device, size_t bytes, void* stream);
 
+/* Decoder-layer element-wise steps, one launch each (RFSNDecoderLayerMLX,
+ * rfsn_v10_mlx_ane_complete.py:114-172, which evaluates them as chains of
+ * tensor operations).
+ *
+ * rfsn_rmsnorm_f16: y[r] = fp16((x[r] * rsqrt(mean(x[r]^2) + eps)) * weight) in
+ * fp32, for `rows` contiguous fp16 rows of `dim` features and an fp32 weight of
+ * `dim` (the layer's RMSNorm / mlx.nn.RMSNorm).
+ *
+ * rfsn_gelu_tanh_f16: y = 0.5 x (1 + tanh(0.7978845608 (x + 0.044715 x^3))) over
+ * n fp16 values, rounded to fp16 after every operation as the layer's fp16
+ * expression is (attention.py:137-138).  x and y may alias. */
+int rfsn_rmsnorm_f16(const uint16_t* x, const float* weight, uint16_t* y, int64_t rows, int dim, float eps,
+                     void* stream);
+int rfsn_gelu_tanh_f16(const uint16_t* x, uint16_t* y, int64_t n, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

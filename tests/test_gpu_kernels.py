@@ -276,10 +276,14 @@ def test_abi_rejects_out_of_range_segment():
         K.decode_attention(qz, q, out, [(K.STORE_WARM, 0, 20, 20, 0)], kv_heads=4, causal=False, warm=st)
 
 
-@pytest.mark.parametrize("ds,L,thr,S", [(8, 1, 0.5, 0), (4, 1, -1.0, 8), (8, 0, 0.0, 0), (4, 1, 0.5, 0), (8, 1, -1.0, 4)])
-def test_tensor_core_encoder_vs_oracle(ds, L, thr, S):
+@pytest.mark.parametrize("ds,L,thr,S,T", [(8, 1, 0.5, 0, 1249), (4, 1, -1.0, 8, 1249), (8, 0, 0.0, 0, 1249),
+                                          (4, 1, 0.5, 0, 1249), (8, 1, -1.0, 4, 1249),
+                                          (8, 0, 0.0, 0, 37), (4, 1, -1.0, 8, 37)])
+def test_tensor_core_encoder_vs_oracle(ds, L, thr, S, T):
     """Spill encoder on tensor cores (D = 64 presets) vs the oracle on strided, ragged input:
-    B=2 sequences x 1249 tokens x 2 heads (not a multiple of the 16-vector tile)."""
+    B=2 sequences x T tokens x 2 heads (not a multiple of the 16-vector tile).  T = 1249 runs
+    one warp per 16-vector group; T = 37 (a decode-sized append) runs split mode, one warp
+    per PQ subspace."""
     rng = np.random.default_rng(100 * ds + 10 * L + S)
     D, M = 64, 64 // ds
     pq_cb = (rng.standard_normal((M, 256, ds)) * 0.8).astype(np.float16)
@@ -288,7 +292,7 @@ def test_tensor_core_encoder_vs_oracle(ds, L, thr, S):
     big = rng.standard_normal((2, 1300, 2, D)).astype(np.float32)
     big[..., rng.choice(D, 4, replace=False)] *= 6.0
     big = big.astype(np.float16)
-    T0, T = 30, 1249
+    T0 = 30
     x = big[:, T0:T0 + T]
     oq = R.Quantizer(pq_cb, rvq_cb if L else np.zeros((0, 256, D), np.float16), thr, sparse_topk=S)
     qz = K.QuantizerBuffers(to_dev(pq_cb), to_dev(rvq_cb) if L else None, thr, S)
@@ -305,7 +309,7 @@ def test_tensor_core_encoder_vs_oracle(ds, L, thr, S):
             pq = store.read(0, "pq", 0, row, 7, T).cpu().numpy()
             pq_tie_ok(x[b, :, h], pq_cb, pq, ref.pq[:, h])
             agree = (pq == ref.pq[:, h]).all(axis=1)
-            assert agree.mean() > 0.99
+            assert (~agree).sum() <= max(1, T // 100)  # fp32 distance ties only (checked above)
             got_res = res[b, :, h].cpu().numpy()
             np.testing.assert_array_equal(got_res[agree].view(np.uint16),
                                           residual.reshape(T, 2, D)[agree, h].view(np.uint16))
@@ -314,7 +318,7 @@ def test_tensor_core_encoder_vs_oracle(ds, L, thr, S):
                 np.testing.assert_array_equal(act[agree], ref.mask[agree, h])
                 rv = store.read(0, "rvq", 0, row, 7, T).cpu().numpy()[:, 0].astype(np.int64)
                 sel = agree & ref.mask[:, h]
-                assert (rv[sel] == ref.rvq[sel, h, 0]).mean() > 0.99
+                assert (rv[sel] != ref.rvq[sel, h, 0]).sum() <= max(1, T // 100)
                 sel = sel & (rv == ref.rvq[:, h, 0])
             else:
                 sel = agree
@@ -324,3 +328,65 @@ def test_tensor_core_encoder_vs_oracle(ds, L, thr, S):
                 np.testing.assert_array_equal(
                     store.read(0, "sp_val", 0, row, 7, T).cpu().numpy()[sel].view(np.uint16),
                     ref.sp_val[sel, h].view(np.uint16))
+
+
+def _ulp_diff(a, b):
+    ai = a.view(torch.int16).int()
+    bi = b.view(torch.int16).int()
+    # map sign-magnitude fp16 bit patterns to a monotonic integer line
+    ai = torch.where(ai < 0, -32768 - ai, ai)
+    bi = torch.where(bi < 0, -32768 - bi, bi)
+    return (ai - bi).abs()
+
+
+@pytest.mark.parametrize("rows,dim,offset", [(32, 2048, 0), (3, 1000, 0), (5, 512, 1)])
+def test_fused_rmsnorm_vs_torch_chain(rows, dim, offset):
+    """rfsn_rmsnorm_f16 vs the layer's tensor-op RMSNorm (fp32 math): at most one fp16 step
+    apart (the sum of squares is reduced in another order), and almost all bit-exact.
+    dim 1000 and a 2-byte offset view take the scalar path."""
+    from apple_b200.layer import _RMSNorm
+    g = torch.Generator(device="cuda").manual_seed(rows * dim)
+    base = (torch.randn(rows * dim + offset, generator=g, device="cuda") * 3).half()
+    x = base[offset:].view(rows, dim)
+    w = torch.rand(dim, generator=g, device="cuda") + 0.5
+    xf = x.float()
+    ref = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5) * w).half()
+    got = K.rms_norm(x, w, 1e-5)
+    d = _ulp_diff(got, ref)
+    assert int(d.max()) <= 1
+    assert float((d == 0).float().mean()) > 0.99
+    norm = _RMSNorm(dim, "cuda")
+    norm.weight = w
+    assert torch.equal(norm(x), got)
+
+
+def _gelu_chain64(x16: np.ndarray) -> np.ndarray:
+    """attention.py:137-138 operation by operation: float64 math, fp16 rounding after each step."""
+    r = lambda a: a.astype(np.float16).astype(np.float64)  # noqa: E731
+    x = x16.astype(np.float64)
+    x3 = r(x * x * x)
+    inner = r(x + r(0.044715 * x3))
+    t = r(np.tanh(r(0.7978845608 * inner)))
+    return (r(0.5 * x) * r(1.0 + t)).astype(np.float16)
+
+
+@pytest.mark.parametrize("n", [32 * 4096, 1001])
+def test_fused_gelu_vs_fp16_chain(n):
+    """rfsn_gelu_tanh_f16 vs the layer's fp16 expression evaluated with accurate math
+    (float64, fp16 rounding after every operation): bit-exact except where tanhf's last
+    fp32 bit crosses an fp16 rounding boundary, which moves the result by one fp16 step
+    of itself or, near tanh = -1, by one step of tanh (2^-11) times 0.5 x.  Also close to
+    the torch tensor chain the layer used before (its fp16 tanh differs in rounding)."""
+    from apple_b200.attention import _gelu
+    g = torch.Generator(device="cuda").manual_seed(n)
+    x = (torch.randn(n, generator=g, device="cuda") * 2.5).half()
+    x[:8] = torch.tensor([0.0, -0.0, 1e-4, -1e-4, 6.0, -6.0, 30.0, -30.0], device="cuda").half()
+    got = K.gelu_tanh(x).cpu()
+    ref = torch.from_numpy(_gelu_chain64(x.cpu().numpy()))
+    err = (got.float() - ref.float()).abs()
+    ulp_ref = torch.exp2(torch.floor(torch.log2(ref.float().abs().clamp_min(2.0 ** -14))) - 10)
+    bound = torch.maximum(ulp_ref, 0.5 * x.cpu().float().abs() * 2.0 ** -11)
+    assert bool((err <= bound * 1.0001).all()), f"max err {float(err.max())}"
+    assert float((err == 0).float().mean()) > 0.999
+    torch_chain = _gelu(x).cpu()
+    assert float((torch_chain == got).float().mean()) > 0.99
