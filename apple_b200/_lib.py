@@ -70,6 +70,9 @@ SIGNATURES = {
     "rfsn_encode": (C.c_int, [C.POINTER(Quantizer), C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_int64,
                               C.c_int64, C.c_int64, C.POINTER(CodeStore), C.c_int32, C.c_int64, C.c_int64,
                               C.c_void_p, C.c_void_p]),
+    "rfsn_encode_kv": (C.c_int, [C.POINTER(Quantizer), C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int64,
+                                 C.c_int64, C.c_int64, C.c_int64, C.POINTER(CodeStore), C.c_int64, C.c_int64,
+                                 C.c_void_p]),
     "rfsn_decode_codes": (C.c_int, [C.POINTER(Quantizer), C.POINTER(CodeStore), C.c_int32, C.c_int64, C.c_int64,
                                     C.c_int64, C.c_int64, C.c_int64, C.c_void_p, C.c_int64, C.c_int64,
                                     C.c_int64, C.c_void_p]),

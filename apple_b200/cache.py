@@ -84,7 +84,6 @@ class RFSNv10KVCacheMLX:
         self._warm_ring = 0
         self._cold: Optional[ColdTier] = None
         self._cold_root: Optional[Path] = None
-        self._qpos_cache: Dict[Tuple, torch.Tensor] = {}
         self._plan_cache: Dict[Tuple, Tuple[List, Dict[str, int]]] = {}
 
     # ------------------------------------------------------------------ stats
@@ -275,9 +274,13 @@ class RFSNv10KVCacheMLX:
             self._hot_v[:, idx:idx + cnt] = v[:, off:off + cnt].permute(0, 2, 1, 3).reshape(self.rows, cnt, -1)
 
     def _encode_kv(self, k: torch.Tensor, v: torch.Tensor, store: K.CodeStoreBuffers, slot: int, first: int) -> None:
-        """Spill encoder: K and V tokens [B, T, H, D] into tokens [first, first+T) of a store."""
-        K.encode(self._qz, k, store, slot, first, kv=0)
-        K.encode(self._qz, v, store, slot, first, kv=1)
+        """Spill encoder: K and V tokens [B, T, H, D] into tokens [first, first+T) of a store
+        (one launch when their layouts match, as projections of one input give)."""
+        if k.stride() == v.stride():
+            K.encode_kv(self._qz, k, v, store, slot, first)
+        else:
+            K.encode(self._qz, k, store, slot, first, kv=0)
+            K.encode(self._qz, v, store, slot, first, kv=1)
 
     def _update_prefix(self, k, v, disk_dir) -> None:
         n = k.shape[1]
@@ -526,17 +529,13 @@ class RFSNv10KVCacheMLX:
             return q.contiguous(), False
         raise ValueError(f"q must be [Q, H, D] (batch 1), [B, H, D] or [B, Q, H, D]; got {tuple(q.shape)}")
 
-    def _qpos(self, query_positions, start, end, qb: torch.Tensor) -> torch.Tensor:
+    def _qpos(self, query_positions, start, end, qb: torch.Tensor) -> Optional[torch.Tensor]:
+        """Per-query last visible positions [B, Q, Hq] int32, or None when every query sits at
+        the window's last position end - 1: then causal masking hides no key of the window
+        [start, end), and the kernel runs unmasked with no position tensor."""
         B, Qn, Hq, _ = qb.shape
         if query_positions is None:
-            key = (B, Qn, Hq, end)
-            t = self._qpos_cache.get(key)
-            if t is None:
-                if len(self._qpos_cache) > 64:
-                    self._qpos_cache.clear()
-                t = torch.full((B, Qn, Hq), end - 1, dtype=torch.int32, device=self.device)
-                self._qpos_cache[key] = t
-            return t
+            return None
         pos = _host_ints(query_positions)
         pos = np.maximum(pos - start, -1) + start
         if self.batch == 1:
@@ -554,10 +553,8 @@ class RFSNv10KVCacheMLX:
                 pos = np.broadcast_to(pos[:, None, :], (B, Qn, Hq))
             elif pos.shape != (B, Qn, Hq):
                 raise ValueError("query_positions must be [B], [B, H] or [B, Q, H]")
-        if pos.size and bool((pos == end - 1).all()):
-            # the decode case (every query at the newest token): reuse the cached device tensor
-            # instead of uploading positions each step
-            return self._qpos(None, start, end, qb)
+        if pos.size and bool((pos >= end - 1).all()):
+            return None  # the decode case: every query sees the whole window
         return torch.as_tensor(np.ascontiguousarray(pos, dtype=np.int32)).to(self.device, non_blocking=True)
 
     def attention_forward(self, q: torch.Tensor, pq_codebook=None, rvq_codebook=None, causal: bool = True,
@@ -591,7 +588,7 @@ class RFSNv10KVCacheMLX:
         if out is None:
             out = torch.empty_like(qb)
         qpos = self._qpos(query_positions, start, end, qb) if causal else None
-        K.decode_attention(self._qz, qb, out, segs, kv_heads=self.heads, qpos=qpos, causal=causal,
+        K.decode_attention(self._qz, qb, out, segs, kv_heads=self.heads, qpos=qpos, causal=qpos is not None,
                            scale=self.head_dim ** -0.5,
                            hot=(self._hot_k, self._hot_v) if self._hot_k is not None else None,
                            warm=self._warm, cold=self._cold.pool if self._cold is not None else None)

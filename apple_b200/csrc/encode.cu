@@ -321,8 +321,8 @@ extern "C" int rfsn_encode(const rfsn_quantizer* qz, const uint16_t* x, int64_t 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   // tensor-core encoder for the configurations it covers (bit-identical codes up to fp32 ties)
   if (encode_tc_supported(qz) && !((uintptr_t)residual_out & 15))
-    return encode_tc_launch(qz, x, batch, tokens, heads, stride_b, stride_t, stride_h, dst, kv, dst_slot, dst_first,
-                            residual_out, s);
+    return encode_tc_launch(qz, x, nullptr, batch, tokens, heads, stride_b, stride_t, stride_h, dst, kv, dst_slot,
+                            dst_first, residual_out, s);
 
   EncodeParams p{};
   p.x = x; p.batch = batch; p.tokens = tokens; p.heads = heads;
@@ -351,6 +351,33 @@ extern "C" int rfsn_encode(const rfsn_quantizer* qz, const uint16_t* x, int64_t 
     if (e == cudaSuccess) encode_kernel<128><<<blocks, kEncThreads, smem, s>>>(p);
   }
   return check_cuda(e == cudaSuccess ? cudaGetLastError() : e);
+}
+
+extern "C" int rfsn_encode_kv(const rfsn_quantizer* qz, const uint16_t* k, const uint16_t* v, int64_t batch,
+                              int64_t tokens, int64_t heads, int64_t stride_b, int64_t stride_t, int64_t stride_h,
+                              const rfsn_code_store* dst, int64_t dst_slot, int64_t dst_first, void* stream) {
+  int st = validate_quantizer(qz);
+  if (st != RFSN_OK) return st;
+  if (!k || !v) return RFSN_ERR_INVALID_ARGUMENT;
+  if (((uintptr_t)v & 15)) return RFSN_ERR_ALIGNMENT;
+  if (!encode_tc_supported(qz)) {  // two launches of the general encoder
+    st = rfsn_encode(qz, k, batch, tokens, heads, stride_b, stride_t, stride_h, dst, 0, dst_slot, dst_first, nullptr,
+                     stream);
+    if (st != RFSN_OK) return st;
+    return rfsn_encode(qz, v, batch, tokens, heads, stride_b, stride_t, stride_h, dst, 1, dst_slot, dst_first,
+                       nullptr, stream);
+  }
+  // the K call's checks cover the shared shape, strides and destination
+  if (!dst || batch < 0 || tokens < 0 || heads <= 0) return RFSN_ERR_INVALID_ARGUMENT;
+  st = validate_store(dst, qz);
+  if (st != RFSN_OK) return st;
+  if (batch * heads > dst->rows || dst_slot < 0 || dst_slot >= dst->slots || dst_first < 0 ||
+      dst_first + tokens > dst->cap)
+    return RFSN_ERR_INVALID_ARGUMENT;
+  if (((uintptr_t)k & 15) || (stride_b & 7) || (stride_t & 7) || (stride_h & 7)) return RFSN_ERR_ALIGNMENT;
+  if (batch * tokens * heads == 0) return RFSN_OK;
+  return encode_tc_launch(qz, k, v, batch, tokens, heads, stride_b, stride_t, stride_h, dst, 0, dst_slot, dst_first,
+                          nullptr, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int rfsn_decode_codes(const rfsn_quantizer* qz, const rfsn_code_store* src, int32_t kv, int64_t slot,

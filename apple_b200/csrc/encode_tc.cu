@@ -40,6 +40,8 @@ constexpr int kTcD = 64;
 
 struct EncTcParams {
   const uint16_t* x;
+  const uint16_t* x_v;  // K and V in one launch: groups [ngk, 2 ngk) encode x_v into the V fields
+  int64_t ngk;          // 16-vector groups of x
   int64_t batch, tokens, heads, sb, st, sh, nvec;
   uint8_t* data;
   BlockLayout lay;
@@ -154,12 +156,16 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1) encode_tc_kernel(const __gri
 
   const int r0 = lane >> 2, qd = lane & 3;
   const float INF = __int_as_float(0x7f800000);
-  const int64_t ngroups = (p.nvec + 15) / 16;
+  const int64_t ngroups = p.x_v ? 2 * p.ngk : p.ngk;
 
   // the round count is the same for every warp of the CTA (split mode syncs the CTA)
   for (int64_t base = (int64_t)blockIdx.x * gpc; base < ngroups; base += (int64_t)gridDim.x * gpc) {
-    const int64_t g = base + gslot;
-    const bool live = g < ngroups;
+    const int64_t gg = base + gslot;
+    const bool live = gg < ngroups;
+    const bool isv = p.x_v != nullptr && gg >= p.ngk;  // a V group of a K+V launch
+    const int64_t g = isv ? gg - p.ngk : gg;           // group index within its tensor
+    const uint16_t* xs = isv ? p.x_v : p.x;
+    const int kvf = isv ? 1 : p.kv;
     // ---- x tile (leader) ----
     if (live && lead) {
 #pragma unroll
@@ -169,7 +175,7 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1) encode_tc_kernel(const __gri
         uint4 val = make_uint4(0u, 0u, 0u, 0u);
         if (v < p.nvec) {
           const int64_t h = v % p.heads, t = (v / p.heads) % p.tokens, b = v / (p.heads * p.tokens);
-          val = __ldg(reinterpret_cast<const uint4*>(p.x + b * p.sb + t * p.st + h * p.sh) + q);
+          val = __ldg(reinterpret_cast<const uint4*>(xs + b * p.sb + t * p.st + h * p.sh) + q);
         }
         xt[swz(i, q)] = val;
       }
@@ -320,7 +326,7 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1) encode_tc_kernel(const __gri
         if (v < p.nvec) {
           const int64_t h = v % p.heads, t = (v / p.heads) % p.tokens, b = v / (p.heads * p.tokens);
           const int64_t row = b * p.heads + h, tok = p.first + t;
-          const int fk = p.kv * 5;
+          const int fk = kvf * 5;
           uint8_t* f_pq = p.data + field_byte(p.lay, p.rows, p.cap, p.slot, row, tok, fk + 0);
           for (int m = 0; m < M; ++m) f_pq[m] = s_code[i * M + m];
           if (p.L > 0) {
@@ -396,11 +402,13 @@ bool encode_tc_supported(const rfsn_quantizer* qz) {
          qz->sparse_topk <= kTcD;
 }
 
-int encode_tc_launch(const rfsn_quantizer* qz, const uint16_t* x, int64_t batch, int64_t tokens, int64_t heads,
-                     int64_t sb, int64_t st, int64_t sh, const rfsn_code_store* dst, int kv, int64_t slot,
-                     int64_t first, uint16_t* residual_out, cudaStream_t stream) {
+int encode_tc_launch(const rfsn_quantizer* qz, const uint16_t* x, const uint16_t* x_v, int64_t batch,
+                     int64_t tokens, int64_t heads, int64_t sb, int64_t st, int64_t sh, const rfsn_code_store* dst,
+                     int kv, int64_t slot, int64_t first, uint16_t* residual_out, cudaStream_t stream) {
+  if (x_v && (kv != 0 || residual_out)) return RFSN_ERR_INVALID_ARGUMENT;
   EncTcParams p{};
   p.x = x;
+  p.x_v = x_v;
   p.batch = batch; p.tokens = tokens; p.heads = heads; p.sb = sb; p.st = st; p.sh = sh;
   p.nvec = batch * tokens * heads;
   p.data = dst->data;
@@ -425,7 +433,8 @@ int encode_tc_launch(const rfsn_quantizer* qz, const uint16_t* x, int64_t batch,
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t groups = (p.nvec + 15) / 16;
+  p.ngk = (p.nvec + 15) / 16;
+  const int64_t groups = x_v ? 2 * p.ngk : p.ngk;
   // split mode (one warp per subspace) when its grid fits in one wave of CTAs: a
   // decode step's append is a handful of groups, and a warp walking all M subspaces
   // alone would set the kernel's duration

@@ -223,6 +223,23 @@ def encode(qz: QuantizerBuffers, x: torch.Tensor, store: CodeStoreBuffers, slot:
          kv, slot, first, _ptr(residual_out), _stream())
 
 
+def encode_kv(qz: QuantizerBuffers, k: torch.Tensor, v: torch.Tensor, store: CodeStoreBuffers, slot: int,
+              first: int) -> None:
+    """Encode K and V [B, T, H, D] (same shape and strides) into tokens first..first+T of a
+    store in one launch (rfsn_encode_kv)."""
+    _need_cuda(k, "k")
+    _need_cuda(v, "v")
+    if k.shape != v.shape or k.stride() != v.stride():
+        raise ValueError("k and v must have the same shape and strides")
+    if k.dtype != torch.float16 or v.dtype != torch.float16 or k.dim() != 4 or k.shape[-1] != qz.D or k.stride(-1) != 1:
+        raise ValueError("k and v must be fp16 [B, T, H, D] with a contiguous last dim")
+    B, T, H, _ = k.shape
+    q = qz.struct()
+    s = store.struct()
+    call("rfsn_encode_kv", C.byref(q), _ptr(k), _ptr(v), B, T, H, k.stride(0), k.stride(1), k.stride(2), C.byref(s),
+         slot, first, _stream())
+
+
 def decode_codes(qz: QuantizerBuffers, store: CodeStoreBuffers, slot: int, first: int, count: int,
                  out: torch.Tensor, kv: int = 0) -> torch.Tensor:
     """Exact fp16 decode of K (kv=0) or V (kv=1) tokens [first, first+count) into

@@ -1093,6 +1093,12 @@ def run_stack(args) -> None:
         e1.record(stream)
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
+    # one more (untimed) replay inside an NVTX range, so a profiler can select exactly one step:
+    # ncu --nvtx --nvtx-include "rfsn_stack_step/" ...
+    torch.cuda.nvtx.range_push("rfsn_stack_step")
+    graph.replay()
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
     if world > 1:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -1122,11 +1128,12 @@ def run_stack(args) -> None:
     achieved = nbytes / (ms * 1e-3) / 1e9
     if rank == 0:
         line = {
-            "metric": "22-layer decode tokens/s (16K ctx, batch 32, PQ 8x8)", "value": c["batch"] * 1e3 / ms,
+            "metric": f"{c['layers']}-layer decode tokens/s (16K ctx, batch 32, PQ 8x8)", "value": c["batch"] * 1e3 / ms,
             "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": warm_steps, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "f16 operands, f32 accumulate", "data": "synthetic",
-            "config": {"workload": "BASELINE configs[2]: TinyLlama-1.1B-shaped 22-layer stack, random init",
+            "config": {"workload": "BASELINE configs[2]: TinyLlama-1.1B-shaped 22-layer stack, random init"
+                       + ("" if c["layers"] == 22 else f" (reduced to {c['layers']} layers)"),
                        "global_batch": c["batch"], "batch_per_gpu": b_local, "seq_len": ctx,
                        "hot": "first 512 tokens fp16", "warm": "PQ 8x8 K256", "parallelism": f"batch-shard dp{world}",
                        "step": "one decode token for the batch through 22 RFSNDecoderLayerMLX layers, replayed "
@@ -1159,6 +1166,9 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--layers", type=int, default=0,
+                    help="stack workload only: number of layers (default: the 22 of configs[2]); fewer layers "
+                         "make a small case for profiling captures")
     ap.add_argument("--workload", default="decode", choices=["decode", "encode", "layer", "longctx", "stack"],
                     help="decode: fused decode attention (configs[1], the headline); encode: spill encoder "
                          "(configs[4]); layer: single decoder layer decode (configs[0]); longctx: 131K three-tier "
@@ -1176,6 +1186,8 @@ def main() -> None:
                                   "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                                           "d2h_bytes_per_step": 0}}))
         else:
+            if args.layers:
+                STACK["layers"] = args.layers
             run_stack(args)
     elif args.workload == "longctx":
         if args.impl == "reference":

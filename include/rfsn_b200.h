@@ -121,6 +121,15 @@ int rfsn_encode(const rfsn_quantizer* qz, const uint16_t* x, int64_t batch, int6
                 int64_t stride_b, int64_t stride_t, int64_t stride_h, const rfsn_code_store* dst, int32_t kv,
                 int64_t dst_slot, int64_t dst_first, uint16_t* residual_out, void* stream);
 
+/* K and V of the same tokens in one launch: rfsn_encode(k, kv = 0) and rfsn_encode(v, kv = 1)
+ * with the same shape, strides and destination, no residual output.  The reference encodes
+ * them with two _compress_tensor_sequence calls (_add_to_warm, cache.py:122-132); at decode a
+ * step appends one token per row, and one launch instead of two halves the encoder's fixed
+ * cost.  Same codes as the two calls. */
+int rfsn_encode_kv(const rfsn_quantizer* qz, const uint16_t* k, const uint16_t* v, int64_t batch, int64_t tokens,
+                   int64_t heads, int64_t stride_b, int64_t stride_t, int64_t stride_h, const rfsn_code_store* dst,
+                   int64_t dst_slot, int64_t dst_first, void* stream);
+
 /* Decode compressed tokens to dense fp16 — _decode_compressed_tensor (quantization.py:394-402),
  * i.e. fp16(pq_decode + rvq_correction) (:319) plus the sparse residual added in fp32 and
  * rounded once.  K (kv = 0) or V (kv = 1) tokens [first, first+count) of every row of slot `slot`; token i of row

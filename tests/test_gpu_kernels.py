@@ -390,3 +390,25 @@ def test_fused_gelu_vs_fp16_chain(n):
     assert float((err == 0).float().mean()) > 0.999
     torch_chain = _gelu(x).cpu()
     assert float((torch_chain == got).float().mean()) > 0.99
+
+
+@pytest.mark.parametrize("D,ds,L,S,T", [(64, 8, 0, 0, 1), (64, 4, 1, 8, 3), (64, 8, 1, 4, 700), (128, 16, 1, 0, 5)])
+def test_encode_kv_matches_two_calls(D, ds, L, S, T):
+    """rfsn_encode_kv (K and V in one launch) writes the same store bytes as rfsn_encode with
+    kv = 0 and kv = 1: decode-sized appends (split mode), a large batch (one warp per group)
+    and a configuration outside the tensor-core encoder (D = 128, 16-dim subspaces)."""
+    rng = np.random.default_rng(D + ds + T)
+    M = D // ds
+    pq_cb = rng.standard_normal((M, 256, ds)).astype(np.float16)
+    rvq_cb = (rng.standard_normal((1, 256, D)) * 0.3).astype(np.float16)
+    rvq_cb[:, 0] = 0
+    qz = K.QuantizerBuffers(to_dev(pq_cb), to_dev(rvq_cb) if L else None, 0.2, S)
+    kv = torch.from_numpy(rng.standard_normal((2, 3, T, 4, D)).astype(np.float16)).cuda()
+    k, v = kv[0], kv[1]
+    one = K.CodeStoreBuffers(qz, rows=12, cap=K.align16(T + 5))
+    two = K.CodeStoreBuffers(qz, rows=12, cap=K.align16(T + 5))
+    K.encode_kv(qz, k, v, one, 0, 5)
+    K.encode(qz, k, two, 0, 5, kv=0)
+    K.encode(qz, v, two, 0, 5, kv=1)
+    torch.cuda.synchronize()
+    assert torch.equal(one.data, two.data)
