@@ -52,10 +52,14 @@ constexpr int kNoLimit = 1 << 30;         // position limit of a row that sees e
 // the per-warp scratch that goes with it: two sets of sparse scatter rows
 // [tokens per round][4 slots][D] fp16, reused as the warp's fp32 [RMAX][D]
 // partial output when a piece ends.
-// (Four tokens per round, measured on B200, ran 1.9x slower than two: the
-// extra live registers cost more than the added load overlap.)
-__host__ __device__ constexpr int tokens_per_round(int) { return 2; }
-__host__ __device__ constexpr int scratch_bytes(int D) { return 2 * tokens_per_round(D) * 4 * D * 2; }
+// Layouts with a sparse residual or RVQ rows rebuild two tokens per round (four,
+// measured on B200, ran 1.9x slower: the extra live registers cost more than the
+// added load overlap).  PQ-only blocks rebuild a token with one gather, so they take
+// four tokens per round for more independent loads and MMAs in flight; they have no
+// sparse scatter rows, so the scratch size below (two tokens per round) still holds
+// their fp32 partial output.
+__host__ __device__ constexpr int tokens_per_round(int, int lp) { return lp == kDs8PqOnly ? 4 : 2; }
+__host__ __device__ constexpr int scratch_bytes(int D) { return 2 * 2 * 4 * D * 2; }
 constexpr int64_t kMaxSmem = 227 * 1024;  // opt-in shared memory per CTA on sm_100
 
 struct SegDev {
@@ -365,7 +369,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
   float* s_ml = reinterpret_cast<float*>(smem + p.smem_ml);  // [NW][RMAX][2]
   const float NEG_INF = __int_as_float(0xff800000);
   constexpr int NMMA = DPL / 4;  // K mma k-steps per row-step
-  constexpr int kTpr = tokens_per_round(D);
+  constexpr int kTpr = tokens_per_round(D, LP);
   constexpr int kBlock = LP != kGeneric ? Preset<LP>::BLOCK : 0;
   const int block_bytes = LP != kGeneric ? kBlock : p.lay.block_bytes;
 
@@ -450,13 +454,24 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
       const int t_lo = ch == 0 ? lead : 0;
       const int t_hi = min(kBlockTokens, span - ch * kBlockTokens);
       const int pos_base = pos0 - lead + ch * kBlockTokens;
+      // a full block: all 16 tokens in range and visible to every live query row
+      const bool full = t_lo == 0 && t_hi == kBlockTokens &&
+                        __all_sync(0xffffffffu, srow >= p.R || c.qp_lim >= pos_base + kBlockTokens - 1);
       if (kind == 0) {
-        const size_t r0 = (size_t)ch * kBlockTokens * D;
-        process_block<D, RMAX, LP, true, kTpr>(c, nullptr, hot_k + r0, hot_v + r0, t_lo, t_hi, pos_base, aq, acc, m_run,
-                                         l_run);
+        const uint16_t* hk = hot_k + (size_t)ch * kBlockTokens * D;
+        const uint16_t* hv = hot_v + (size_t)ch * kBlockTokens * D;
+        if (full)
+          process_block<D, RMAX, LP, true, kTpr, true>(c, nullptr, hk, hv, t_lo, t_hi, pos_base, aq, acc, m_run, l_run);
+        else
+          process_block<D, RMAX, LP, true, kTpr, false>(c, nullptr, hk, hv, t_lo, t_hi, pos_base, aq, acc, m_run, l_run);
       } else {
-        process_block<D, RMAX, LP, false, kTpr>(c, sb + ch * block_bytes, nullptr, nullptr, t_lo, t_hi, pos_base, aq,
-                                          acc, m_run, l_run);
+        const unsigned char* blk = sb + ch * block_bytes;
+        if (full)
+          process_block<D, RMAX, LP, false, kTpr, true>(c, blk, nullptr, nullptr, t_lo, t_hi, pos_base, aq, acc, m_run,
+                                                        l_run);
+        else
+          process_block<D, RMAX, LP, false, kTpr, false>(c, blk, nullptr, nullptr, t_lo, t_hi, pos_base, aq, acc, m_run,
+                                                         l_run);
       }
     }
     // release the stage

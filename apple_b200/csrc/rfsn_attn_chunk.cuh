@@ -227,7 +227,7 @@ __device__ __forceinline__ void load_round(const ChunkCtx& c, const unsigned cha
       recon_generic<D>(c, blk, kv, tb[i], dim0, w[i]);
     }
   }
-  if constexpr (!DENSE) {
+  if constexpr (!DENSE && (LP == kGeneric || Preset<LP>::S > 0)) {
     if (c.S > 0) sparse_round<D, LP, TPR>(c, blk, kv, tb, valid, round, slot, j, dim0, w);
   }
 }
@@ -242,7 +242,12 @@ __device__ __forceinline__ void load_round(const ChunkCtx& c, const unsigned cha
 // holds acc[u] = {O[2q][DPL*g+2u], O[2q+1][DPL*g+2u], O[2q][DPL*g+2u+1],
 // O[2q+1][DPL*g+2u+1]} for query rows 2q, 2q+1 (unnormalised, online-softmax
 // scaled) -- the D fragment of O^T = V^T P^T.
-template <int D, int RMAX, int LP, bool DENSE, int TPR>
+//
+// FULL: every token of the block is valid and visible to every live query row
+// (the common case; the caller decides it warp-uniformly), so the per-token
+// range checks and score masks compile away.  Rows past the KV head's query
+// count then score 0 instead of being masked; their state is never read.
+template <int D, int RMAX, int LP, bool DENSE, int TPR, bool FULL>
 __device__ __forceinline__ void process_block(const ChunkCtx& c, const unsigned char* blk, const uint16_t* dense_k,
                                               const uint16_t* dense_v, int t_lo, int t_hi, int pos_base,
                                               const uint32_t (*aq)[4], float (*acc)[4], float& m_run,
@@ -251,7 +256,7 @@ __device__ __forceinline__ void process_block(const ChunkCtx& c, const unsigned 
   constexpr int NT = D / 16;   // P.V tiles of 16 dims
   constexpr int NMMA = DPL / 4;
   constexpr int NR = 4 / TPR;  // rounds per phase
-  static_assert(TPR == 2, "P.V pairs the two tokens of a round");
+  static_assert(TPR == 2 || TPR == 4, "P.V takes the tokens of a round as one k8 (2) or k16 (4) step");
   static_assert(RMAX <= 8, "P.V covers at most 8 query rows");
   const float NEG_INF = __int_as_float(0xff800000);
   const int lane = threadIdx.x & 31;
@@ -270,7 +275,7 @@ __device__ __forceinline__ void process_block(const ChunkCtx& c, const unsigned 
 #pragma unroll
     for (int i = 0; i < TPR; ++i) {
       tb[i] = 4 * (rr * TPR + i) + slot;
-      valid[i] = tb[i] >= t_lo && tb[i] < t_hi;
+      valid[i] = FULL || (tb[i] >= t_lo && tb[i] < t_hi);
     }
     uint32_t w[TPR][DPL / 2];
     load_round<D, LP, DENSE, TPR>(c, blk, dense_k, 0, tb, valid, t_lo, rr, slot, j, dim0, odd, w);
@@ -284,7 +289,8 @@ __device__ __forceinline__ void process_block(const ChunkCtx& c, const unsigned 
 #pragma unroll
     for (int i = 0; i < TPR; ++i) {
       const int stb = 4 * (rr * TPR + i) + sslot;
-      sc[rr * TPR + i] = (stb >= t_lo && stb < s_hi) ? (cfr[i][0] + cfr[i][3]) * c.sl2 : NEG_INF;
+      const float v = (cfr[i][0] + cfr[i][3]) * c.sl2;
+      sc[rr * TPR + i] = (FULL || (stb >= t_lo && stb < s_hi)) ? v : NEG_INF;
     }
   }
 
@@ -299,7 +305,7 @@ __device__ __forceinline__ void process_block(const ChunkCtx& c, const unsigned 
   float lsum = 0.f;
 #pragma unroll
   for (int rs = 0; rs < 4; ++rs) {
-    pr[rs] = (sc[rs] == NEG_INF) ? 0.f : ex2_approx(sc[rs] - m_new);
+    pr[rs] = (!FULL && sc[rs] == NEG_INF) ? 0.f : ex2_approx(sc[rs] - m_new);
     lsum += pr[rs];
   }
   lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
@@ -317,13 +323,14 @@ __device__ __forceinline__ void process_block(const ChunkCtx& c, const unsigned 
     }
   }
 
-  // ---------------- values: O^T += V^T P^T, one mma.m16n8k8 per tile and round ----------------
-  // Round rr rebuilds tokens 8rr + slot and 8rr + 4 + slot in lane (slot, j).  In the mma, k index
-  // 2q + e (q = lane%4) is token 8rr + q + 4e, A rows g and g+8 (g = lane/4) of tile u are dims
-  // DPL*g + 2u and DPL*g + 2u + 1, and B column g is query row g.  Lane (g, q) therefore takes the
-  // values rebuilt by lane (slot q, j g) = 8q + g, pairs them by token with byte permutes, and
-  // supplies its own probabilities P[row g][tokens 8rr + q, 8rr + q + 4] (left here by the score
-  // phase) split into fp16 hi + lo halves.
+  // ---------------- values: O^T += V^T P^T on tensor cores ----------------
+  // Round rr rebuilds tokens 4(rr*TPR + i) + slot (i < TPR) in lane (slot, j).  In the mma, A rows g
+  // and g+8 (g = lane/4) of tile u are dims DPL*g + 2u and DPL*g + 2u + 1, B column g is query row
+  // g, and k index 2q + e (q = lane%4; e < 2, then 8 + e for the k16 step) is the round's token
+  // i = e (then 2 + e).  Lane (g, q) therefore takes the values rebuilt by lane (slot q, j g) =
+  // 8q + g, pairs them by token with byte permutes, and supplies its own probabilities of those
+  // tokens for row g (left in this lane by the score phase) split into fp16 hi + lo halves.
+  // Two tokens per round: one m16n8k8 per tile; four: one m16n8k16.
   const int src = (sslot << 3) | (lane >> 2);
 #pragma unroll
   for (int rr = 0; rr < NR; ++rr) {
@@ -332,20 +339,30 @@ __device__ __forceinline__ void process_block(const ChunkCtx& c, const unsigned 
 #pragma unroll
     for (int i = 0; i < TPR; ++i) {
       tb[i] = 4 * (rr * TPR + i) + slot;
-      valid[i] = tb[i] >= t_lo && tb[i] < t_hi;
+      valid[i] = FULL || (tb[i] >= t_lo && tb[i] < t_hi);
     }
     uint32_t w[TPR][DPL / 2];
     load_round<D, LP, DENSE, TPR>(c, blk, dense_v, 1, tb, valid, t_lo, NR + rr, slot, j, dim0, odd, w);
-    uint32_t bhi, blo;
-    split_h2(pr[2 * rr], pr[2 * rr + 1], bhi, blo);
+    uint32_t bhi[TPR / 2], blo[TPR / 2];
+#pragma unroll
+    for (int h = 0; h < TPR / 2; ++h) split_h2(pr[rr * TPR + 2 * h], pr[rr * TPR + 2 * h + 1], bhi[h], blo[h]);
 #pragma unroll
     for (int u = 0; u < NT; ++u) {
-      const uint32_t x0 = __shfl_sync(0xffffffffu, w[0][u], src);
-      const uint32_t x1 = __shfl_sync(0xffffffffu, w[1][u], src);
-      const uint32_t a0 = prmt(x0, x1, 0x5410u);  // dim DPL*g + 2u of the round's two tokens
-      const uint32_t a1 = prmt(x0, x1, 0x7632u);  // dim DPL*g + 2u + 1
-      mma16808(acc[u], a0, a1, bhi);
-      mma16808(acc[u], a0, a1, blo);
+      uint32_t a[TPR];
+#pragma unroll
+      for (int h = 0; h < TPR / 2; ++h) {
+        const uint32_t x0 = __shfl_sync(0xffffffffu, w[2 * h][u], src);
+        const uint32_t x1 = __shfl_sync(0xffffffffu, w[2 * h + 1][u], src);
+        a[2 * h] = prmt(x0, x1, 0x5410u);      // dim DPL*g + 2u of the pair's two tokens
+        a[2 * h + 1] = prmt(x0, x1, 0x7632u);  // dim DPL*g + 2u + 1
+      }
+      if constexpr (TPR == 2) {
+        mma16808(acc[u], a[0], a[1], bhi[0]);
+        mma16808(acc[u], a[0], a[1], blo[0]);
+      } else {
+        mma16816(acc[u], a, bhi[0], bhi[1]);
+        mma16816(acc[u], a, blo[0], blo[1]);
+      }
     }
   }
 }

@@ -86,6 +86,8 @@ class RFSNDecoderLayerMLX:
         self.o_proj = mk(config.num_heads * config.head_dim, config.hidden_dim)
         self.ffn_up = mk(config.hidden_dim, self.ffn_hidden_dim)
         self.ffn_down = mk(self.ffn_hidden_dim, config.hidden_dim)
+        self._qkv_w: Optional[torch.Tensor] = None  # q/k/v weights concatenated in the activations' dtype
+        self._qkv_src: tuple = ()
         self.quantizer = HybridQuantizerMLX(config)
         self.disk_cache_dir = Path(config.disk_cache_dir) / f"decoder_layer_{layer_idx}"
         self.cache = RFSNv10KVCacheMLX(config, layer_idx=layer_idx)
@@ -100,6 +102,19 @@ class RFSNDecoderLayerMLX:
             shutil.rmtree(self.disk_cache_dir)
         self.cache.close()
         self.cache = RFSNv10KVCacheMLX(self.config, layer_idx=self.layer_idx)
+
+    def _qkv(self, a: torch.Tensor):
+        """q, k and v projections of the same input as one GEMM over the concatenated weights
+        (rebuilt when a projection's weight is replaced); returns views of the one product."""
+        ws = (self.q_proj.weight, self.k_proj.weight, self.v_proj.weight)
+        if (self._qkv_w is None or self._qkv_w.dtype != a.dtype or len(self._qkv_src) != 3
+                or any(x is not y for x, y in zip(self._qkv_src, ws))):
+            self._qkv_w = torch.cat([w.to(a.dtype) for w in ws], 0)
+            self._qkv_src = ws
+        y = torch.matmul(a, self._qkv_w.t())
+        nq = self.num_heads * self.head_dim
+        nk = self.num_kv_heads * self.head_dim
+        return y[..., :nq], y[..., nq:nq + nk], y[..., nq + nk:]
 
     def _project_heads(self, projected: torch.Tensor, heads: int) -> torch.Tensor:
         b, s, _ = projected.shape
@@ -131,9 +146,10 @@ class RFSNDecoderLayerMLX:
         x = x.to(device=torch.device(self.config.device))
         residual = x.to(torch.float16)
         attn_input = self.attn_norm(residual).to(torch.float16)
-        q_heads = self._project_heads(self.q_proj(attn_input), self.num_heads)
-        k_heads = self._project_heads(self.k_proj(attn_input), self.num_kv_heads)
-        v_heads = self._project_heads(self.v_proj(attn_input), self.num_kv_heads)
+        q_p, k_p, v_p = self._qkv(attn_input)
+        q_heads = self._project_heads(q_p, self.num_heads)
+        k_heads = self._project_heads(k_p, self.num_kv_heads)
+        v_heads = self._project_heads(v_p, self.num_kv_heads)
         B = int(x.shape[0])
         if use_cache:
             if tuple(x.shape[:2]) != (self.config.batch_size, 1):

@@ -853,6 +853,44 @@ def longctx_setup(dev):
     return cfg, cache, q
 
 
+def longctx_cpu_baseline(steps: int = 2) -> dict:
+    """The numpy cache (oracle/restate.py OracleCache, the reference's tiering with the
+    recent-hot extension) on ONE (sequence, KV head) row of the configs[3] workload at the
+    full 131072-token context: hot 2048, warm 32768, 188 cold chunks.  The step time of the
+    32-row batch is extrapolated from it (rows are independent)."""
+    from oracle import restate as R
+    c = LONG
+    rng = np.random.default_rng(c["seed"])
+    T, ch, D = c["context"], c["chunk"], c["head_dim"]
+    G = c["q_heads"] // c["kv_heads"]
+    walk = np.cumsum(rng.standard_normal((T // ch, D), dtype=np.float32) * 0.05, axis=0)
+    k = (np.repeat(walk, ch, axis=0) + rng.standard_normal((T, D), dtype=np.float32)).astype(np.float16)[None, :, None]
+    v = rng.standard_normal((1, T, 1, D), dtype=np.float32).astype(np.float16)
+    flat = np.concatenate([k[0, ::97, 0], v[0, ::97, 0]], 0)
+    idx = rng.integers(0, flat.shape[0], (c["M"], c["K"]))
+    pq = np.stack([flat[idx[m], c["ds"] * m:c["ds"] * (m + 1)] for m in range(c["M"])]).astype(np.float16)
+    _, res = R.pq_quantize(flat[rng.integers(0, flat.shape[0], c["Kr"])], pq)
+    rvq = res.reshape(1, c["Kr"], D).astype(np.float16).copy()
+    rvq[:, 0] = 0
+    cfg = R.OracleConfig(hidden_dim=G * D, num_heads=G, num_kv_heads=1, head_dim=D, num_subspaces=c["M"],
+                         subspace_dim=c["ds"], num_rvq_layers=1, rvq_codebook_size=c["Kr"],
+                         rvq_sparsity_threshold=-1.0, hot_capacity=c["hot"], warm_capacity=c["warm"],
+                         block_size_seq=128, sparse_topk=c["sparse"], hot_policy="recent", cold_chunk_tokens=ch)
+    cache = R.OracleCache(cfg, R.Quantizer(pq, rvq, -1.0, sparse_topk=c["sparse"]), batch=1)
+    for a in range(0, T, 8192):
+        cache.update(k[:, a:a + 8192], v[:, a:a + 8192])
+    q = rng.standard_normal((1, 1, G, D), dtype=np.float32).astype(np.float16)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        cache.attention_forward(q, causal=True, context_window=T, current_position=T - 1)
+    dt = (time.perf_counter() - t0) / steps
+    rows = c["batch"] * c["kv_heads"]
+    return {"value": 1.0 / (dt * rows), "unit": "steps/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"numpy cache (oracle/restate.py), one (sequence, KV head) row at 131072 tokens (hot 2048, "
+                      f"warm 32768, 188 cold chunks), mean of {steps} steps = {dt * 1e3:.0f} ms; step time "
+                      f"extrapolated x{rows} rows"}
+
+
 def run_longctx(args) -> None:
     import torch
     from apple_b200 import kernels as K
@@ -932,7 +970,8 @@ def run_longctx(args) -> None:
                                                           "cold_chunk_cache_misses", "cold_tokens_materialized")}},
         "e2e": {"value": 1.0 / e2e_s, "unit": "steps/s", "h2d_bytes_per_step": hqh.numel() * 2,
                 "d2h_bytes_per_step": hqh.numel() * 2, "api": "RFSNv10KVCacheMLX.attention_forward with router"},
-        "max_abs_diff_api_vs_graph": err, "gpu_launches": steps, "clocks": clocks.summary()}))
+        "max_abs_diff_api_vs_graph": err, "gpu_launches": steps, "clocks": clocks.summary(),
+        "cpu_baseline": longctx_cpu_baseline()}))
     cache.close()
 
 
@@ -1192,8 +1231,11 @@ def main() -> None:
     elif args.workload == "longctx":
         if args.impl == "reference":
             if int(os.environ.get("RANK", "0")) == 0:
-                print(json.dumps({"impl": "reference", "unavailable": "no CPU arm for the 131K three-tier workload: "
-                                  "the numpy port needs minutes per step at this size"}))
+                cb = longctx_cpu_baseline()
+                print(json.dumps({"metric": "long-context decode attn steps/s (131K ctx, three tiers)",
+                                  "value": cb["value"], "unit": "steps/s", "n_gpus": args.gpus, "impl": "reference",
+                                  "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": "steps/s",
+                                                               "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
         else:
             run_longctx(args)
     elif args.workload == "layer":
