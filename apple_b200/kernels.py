@@ -378,28 +378,5 @@ def gelu_tanh(x: torch.Tensor) -> torch.Tensor:
     return y
 
 
-def linear_supported(x: torch.Tensor, weight: torch.Tensor) -> bool:
-    """Whether rfsn_linear_f16 serves y = x @ weight^T (decode rows; see the header)."""
-    if not (x.is_cuda and x.dtype == torch.float16 and weight.dtype == torch.float16 and weight.dim() == 2):
-        return False
-    n, k = weight.shape
-    m = x.numel() // k if k else 0
-    return (x.shape[-1] == k and 0 < m <= 32 and n % 32 == 0 and k % 256 == 0 and weight.is_contiguous()
-            and weight.data_ptr() % 16 == 0)
-
-
-def linear(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
-    """y = x @ weight^T for decode-shaped x [..., K] (at most 32 rows) in one launch of
-    rfsn_linear_f16; weight [N, K] fp16 contiguous.  Check linear_supported first."""
-    k = weight.shape[1]
-    x2 = x.reshape(-1, k)
-    if x2.stride(1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
-        x2 = x2.contiguous()
-    m, n = x2.shape[0], weight.shape[0]
-    y = torch.empty((m, n), dtype=torch.float16, device=x.device)
-    call("rfsn_linear_f16", _ptr(x2), _ptr(weight), _ptr(y), m, n, k, x2.stride(0), n, _stream(x.device.index))
-    return y.reshape(*x.shape[:-1], n)
-
-
 def version() -> int:
     return lib().rfsn_version()

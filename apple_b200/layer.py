@@ -43,9 +43,7 @@ class _Linear:
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         # like mlx.nn.Linear: the weight is cast to the activations' dtype (fp16 in the layer)
         if self._cast is None or self._cast.dtype != x.dtype or self._src is not self.weight:
-            self._cast, self._src = self.weight.to(x.dtype).contiguous(), self.weight
-        if K.linear_supported(x, self._cast):  # decode rows: one weight-streaming launch
-            return K.linear(x, self._cast)
+            self._cast, self._src = self.weight.to(x.dtype), self.weight
         return torch.matmul(x, self._cast.t())
 
 
@@ -113,7 +111,7 @@ class RFSNDecoderLayerMLX:
                 or any(x is not y for x, y in zip(self._qkv_src, ws))):
             self._qkv_w = torch.cat([w.to(a.dtype) for w in ws], 0)
             self._qkv_src = ws
-        y = K.linear(a, self._qkv_w) if K.linear_supported(a, self._qkv_w) else torch.matmul(a, self._qkv_w.t())
+        y = torch.matmul(a, self._qkv_w.t())
         nq = self.num_heads * self.head_dim
         nk = self.num_kv_heads * self.head_dim
         return y[..., :nq], y[..., nq:nq + nk], y[..., nq + nk:]

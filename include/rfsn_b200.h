@@ -223,14 +223,6 @@ int rfsn_rmsnorm_f16(const uint16_t* x, const float* weight, uint16_t* y, int64_
                      void* stream);
 int rfsn_gelu_tanh_f16(const uint16_t* x, uint16_t* y, int64_t n, void* stream);
 
-/* Decode-shaped projection y[M x N] = x[M x K] . w[N x K]^T (the layer's q/k/v, o_proj and
- * FFN projections at one token per sequence), fp16 in and out, fp32 accumulation.  x rows
- * are ldx elements apart, y rows ldy.  Serves M <= 32, N % 32 == 0, K % 256 == 0 with x and
- * w 16-byte aligned and ldx % 8 == 0; returns RFSN_ERR_UNSUPPORTED for other shapes (the
- * caller uses a library GEMM). */
-int rfsn_linear_f16(const uint16_t* x, const uint16_t* w, uint16_t* y, int64_t M, int64_t N, int64_t K, int64_t ldx,
-                    int64_t ldy, void* stream);
-
 #ifdef __cplusplus
 }
 #endif
