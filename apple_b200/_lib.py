@@ -58,7 +58,8 @@ class AttnArgs(C.Structure):
                 ("causal", C.c_int32), ("scale", C.c_float), ("hot", DenseStore), ("warm", CodeStore),
                 ("cold", CodeStore),
                 ("segments", C.POINTER(Segment)), ("num_segments", C.c_int32), ("num_ctas", C.c_int32),
-                ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t), ("device_status", C.c_void_p)]
+                ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t), ("device_status", C.c_void_p),
+                ("q_batch_stride", C.c_int64)]
 
 
 # exported symbol -> (restype, argtypes); must match include/rfsn_b200.h

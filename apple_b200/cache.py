@@ -521,12 +521,15 @@ class RFSNv10KVCacheMLX:
         # a pinned host query is uploaded asynchronously on the current stream (ordered
         # before the attention kernel); keep it unchanged until the call's result is read
         q = q.to(device=self.device, dtype=torch.float16, non_blocking=bool(not q.is_cuda and q.is_pinned()))
+        # a view whose sequences are each packed (e.g. the query heads of a wider projection
+        # output) is read in place through the kernel's batch stride
+        pack = lambda t: t if K._queries_packed(t) else t.contiguous()  # noqa: E731
         if self.batch == 1 and q.dim() == 3:
-            return q.unsqueeze(0).contiguous(), True          # [1, Q, Hq, D]
+            return pack(q.unsqueeze(0)), True                 # [1, Q, Hq, D]
         if q.dim() == 3 and q.shape[0] == self.batch:
-            return q.unsqueeze(1).contiguous(), False         # [B, 1, Hq, D]
+            return pack(q.unsqueeze(1)), False                # [B, 1, Hq, D]
         if q.dim() == 4 and q.shape[0] == self.batch:
-            return q.contiguous(), False
+            return pack(q), False
         raise ValueError(f"q must be [Q, H, D] (batch 1), [B, H, D] or [B, Q, H, D]; got {tuple(q.shape)}")
 
     def _qpos(self, query_positions, start, end, qb: torch.Tensor) -> Optional[torch.Tensor]:
@@ -586,7 +589,7 @@ class RFSNv10KVCacheMLX:
         stats["query_tokens"] = int(q.shape[0])
         self.last_access_stats = stats
         if out is None:
-            out = torch.empty_like(qb)
+            out = torch.empty(qb.shape, dtype=torch.float16, device=qb.device)
         qpos = self._qpos(query_positions, start, end, qb) if causal else None
         K.decode_attention(self._qz, qb, out, segs, kv_heads=self.heads, qpos=qpos, causal=qpos is not None,
                            scale=self.head_dim ** -0.5,

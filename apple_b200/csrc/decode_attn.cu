@@ -27,7 +27,7 @@
 // [j*D/8, (j+1)*D/8).  A lane rebuilds its dims exactly from codebooks staged
 // in shared memory (rfsn_attn_chunk.cuh), K scores for all query rows of the
 // KV head (GQA group x queries) come from one tensor-core MMA per 8 dims, and
-// V is accumulated in fp32 with paired FMAs.  Softmax state is fp32 and
+// P.V runs on tensor cores too (O^T = V^T P^T, fp32 accumulators).  Softmax state is fp32 and
 // rescaled only when a row's running max grows.  All waits are bounded
 // (rfsn_common.cuh).
 #include <cuda_runtime.h>
@@ -73,6 +73,7 @@ struct StoreDev {
 
 struct AttnParams {
   const uint16_t* q;
+  int64_t q_bstride;  // elements between consecutive sequences' queries
   const int32_t* qpos;
   uint16_t* out;
   float* ws_o;
@@ -422,7 +423,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
         const uint16_t* qrow = nullptr;
         if (gA < p.R) {
           const int qi = gA / p.G, g = gA - qi * p.G;
-          qrow = p.q + ((size_t)(b * p.Q + qi) * p.Hq + kvh * p.G + g) * D;
+          qrow = p.q + (size_t)b * p.q_bstride + ((size_t)qi * p.Hq + kvh * p.G + g) * D;
         }
 #pragma unroll
         for (int s = 0; s < NMMA; ++s) {
@@ -633,7 +634,11 @@ static int make_plan(const rfsn_attn_args* a, const rfsn_quantizer* qz, Plan& pl
   const int G = a->q_heads / a->kv_heads;
   const int R = G * a->queries;
   if (R > RFSN_MAX_ROWS_PER_KV) return RFSN_ERR_UNSUPPORTED;
+  const int64_t q_packed = (int64_t)a->queries * a->q_heads * a->head_dim;
+  if (a->q_batch_stride != 0 && (a->q_batch_stride < q_packed || (a->q_batch_stride & 7)))
+    return RFSN_ERR_INVALID_ARGUMENT;
   p.q = a->q; p.qpos = a->qpos; p.dev_status = a->device_status;
+  p.q_bstride = a->q_batch_stride ? a->q_batch_stride : q_packed;
   p.B = a->batch; p.Q = a->queries; p.Hq = a->q_heads; p.Hkv = a->kv_heads; p.D = a->head_dim; p.G = G; p.R = R;
   p.causal = a->causal; p.scale = a->scale;
   p.hot_k = a->hot.k; p.hot_v = a->hot.v; p.hot_cap = a->hot.cap;

@@ -282,6 +282,13 @@ class _AttnCall:
 _ATTN_CALLS: "dict" = {}
 
 
+def _queries_packed(q: torch.Tensor) -> bool:
+    """[B, Q, Hq, D] with each sequence's queries packed and any batch stride the kernel takes."""
+    B, Qn, Hq, D = q.shape
+    inner = q.stride(3) == 1 and (Hq == 1 or q.stride(2) == D) and (Qn == 1 or q.stride(1) == Hq * D)
+    return inner and (B == 1 or (q.stride(0) % 8 == 0 and q.stride(0) >= Qn * Hq * D)) and q.data_ptr() % 16 == 0
+
+
 def _qz_key(qz: QuantizerBuffers) -> tuple:
     return (_ptr(qz.pq_codebooks), _ptr(qz.rvq_codebooks), qz.M, qz.K, qz.ds, qz.L, qz.Kr, float(qz.threshold),
             int(qz.sparse_topk))
@@ -303,8 +310,8 @@ def decode_attention(qz: QuantizerBuffers, q: torch.Tensor, out: torch.Tensor, s
     segments: (store, slot, first, count, pos0) tuples in window order.
     """
     _need_cuda(q, "q")
-    if q.dtype != torch.float16 or q.dim() != 4 or not q.is_contiguous():
-        raise ValueError("q must be contiguous fp16 [B, Q, Hq, D]")
+    if q.dtype != torch.float16 or q.dim() != 4 or not _queries_packed(q):
+        raise ValueError("q must be fp16 [B, Q, Hq, D], packed within a sequence (batch stride a multiple of 8)")
     if out.shape != q.shape or out.dtype != torch.float16 or not out.is_contiguous():
         raise ValueError("out must be contiguous fp16 like q")
     B, Qn, Hq, D = q.shape
@@ -316,7 +323,7 @@ def decode_attention(qz: QuantizerBuffers, q: torch.Tensor, out: torch.Tensor, s
     scale = float(D ** -0.5 if scale is None else scale)
     hot_key = None if hot is None else (_ptr(hot[0]), _ptr(hot[1]), hot[0].shape[1], hot[0].shape[0])
     key = (q.device.index, B, Qn, Hq, D, kv_heads, bool(causal), scale, num_ctas, tuple(map(tuple, segments)),
-           hot_key, _store_key(warm), _store_key(cold), _qz_key(qz))
+           hot_key, _store_key(warm), _store_key(cold), _qz_key(qz), q.stride(0) if B > 1 else 0)
     entry = _ATTN_CALLS.get(key)
     if entry is None:
         a = AttnArgs()
@@ -336,6 +343,7 @@ def decode_attention(qz: QuantizerBuffers, q: torch.Tensor, out: torch.Tensor, s
         a.segments = segs
         a.num_segments = len(segments)
         a.num_ctas = num_ctas
+        a.q_batch_stride = q.stride(0) if B > 1 else 0  # one sequence: no stride to follow
         qs = qz.struct()
         a.q, a.out, a.qpos = _ptr(q), _ptr(out), _ptr(qpos) if causal else None
         nbytes = C.c_size_t(0)

@@ -163,7 +163,7 @@ class RFSNDecoderLayerMLX:
             if window is None:
                 window = max(self.config.block_size_seq, min(total, self.config.warm_capacity))
             qpos = [total - 1] if self.config.batch_size == 1 else [total - 1] * B
-            attended = self.cache.attention_forward(q_heads[:, 0].contiguous(), causal=True, query_positions=qpos,
+            attended = self.cache.attention_forward(q_heads[:, 0], causal=True, query_positions=qpos,
                                                     router=router, current_position=total - 1,
                                                     context_window=window)
             attended = attended.reshape(B, 1, self.num_heads, self.head_dim)

@@ -177,6 +177,9 @@ typedef struct rfsn_attn_args {
   size_t workspace_bytes;
   int32_t* device_status;          /* optional device int32, set non-zero on a device-side failure: 1/2 a bounded
                                       wait timed out, 4 a row ticket could not be taken */
+  int64_t q_batch_stride;          /* elements from one sequence's queries to the next (a multiple of 8, at least
+                                      queries*q_heads*head_dim); 0 = packed.  Lets q be a view of a wider
+                                      projection output. */
 } rfsn_attn_args;
 
 /* Bytes of device workspace rfsn_decode_attention needs for these arguments. */

@@ -412,3 +412,38 @@ def test_encode_kv_matches_two_calls(D, ds, L, S, T):
     K.encode(qz, v, two, 0, 5, kv=1)
     torch.cuda.synchronize()
     assert torch.equal(one.data, two.data)
+
+
+@pytest.mark.parametrize("Qn", [1, 2])
+def test_fused_attention_strided_queries(Qn):
+    """q as a view with a batch stride (the query heads of a wider projection output) gives
+    bit-identical outputs to the packed copy; a batch stride that is not a multiple of 8
+    elements is refused."""
+    rng = np.random.default_rng(7 + Qn)
+    B, Hkv, G, D, T_hot, T_warm = 3, 2, 4, 64, 48, 160
+    pq_cb, rvq_cb, k, v = _make_cfg2_like(rng, B, Hkv, G, D, T_hot, T_warm, S=8, ds=4, L=1, thr=-1.0)
+    oq = R.Quantizer(pq_cb, rvq_cb, -1.0, sparse_topk=8)
+    qz = K.QuantizerBuffers(to_dev(pq_cb), to_dev(rvq_cb), -1.0, 8)
+    kc = [oq.compress(k[b, :T_warm]) for b in range(B)]
+    vc = [oq.compress(v[b, :T_warm]) for b in range(B)]
+
+    def rows(cs):
+        return [R.Codes(c.pq[:, h], c.rvq[:, h], c.mask[:, h], c.sp_idx[:, h], c.sp_val[:, h])
+                for c in cs for h in range(Hkv)]
+
+    ws = kv_to_store(qz, rows(kc), rows(vc), cap=T_warm)
+    hot_k = to_dev(np.ascontiguousarray(k[:, T_warm:].transpose(0, 2, 1, 3).reshape(B * Hkv, T_hot, D)))
+    hot_v = to_dev(np.ascontiguousarray(v[:, T_warm:].transpose(0, 2, 1, 3).reshape(B * Hkv, T_hot, D)))
+    Hq = Hkv * G
+    wide = torch.from_numpy(rng.standard_normal((B, Qn * Hq * D + 320)).astype(np.float16)).cuda()
+    qv = wide[:, :Qn * Hq * D].view(B, Qn, Hq, D)  # batch stride Qn*Hq*D + 320
+    segs = [(K.STORE_WARM, 0, 0, T_warm, 0), (K.STORE_HOT, 0, 0, T_hot, T_warm)]
+    out_v = torch.empty((B, Qn, Hq, D), dtype=torch.float16, device="cuda")
+    out_c = torch.empty_like(out_v)
+    K.decode_attention(qz, qv, out_v, segs, kv_heads=Hkv, causal=False, hot=(hot_k, hot_v), warm=ws)
+    K.decode_attention(qz, qv.contiguous(), out_c, segs, kv_heads=Hkv, causal=False, hot=(hot_k, hot_v), warm=ws)
+    torch.cuda.synchronize()
+    assert torch.equal(out_v, out_c)
+    odd = torch.zeros((B, Qn * Hq * D + 4), dtype=torch.float16, device="cuda")[:, :Qn * Hq * D].view(B, Qn, Hq, D)
+    with pytest.raises(ValueError):
+        K.decode_attention(qz, odd, out_v, segs, kv_heads=Hkv, causal=False, hot=(hot_k, hot_v), warm=ws)
