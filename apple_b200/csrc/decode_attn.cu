@@ -571,8 +571,12 @@ struct Plan {
 };
 
 // Consumer warps per CTA, chosen so the per-thread register budget of one
-// CTA per SM covers q and the output accumulator without spilling.
-static constexpr int consumer_warps(int D, int rmax) {
+// CTA per SM covers q and the output accumulator without spilling.  PQ-only
+// blocks (one gather per token, no RVQ or sparse state) fit 96 registers, so they
+// run 19 consumer warps: the kernel is latency-bound there, and more warps hide
+// more of it.  The other presets spill at 96 and keep 15.
+static constexpr int consumer_warps(int D, int rmax, int lp) {
+  if (D == 64 && lp == kDs8PqOnly) return 19;
   // total warps (NW + producer) a multiple of 4 so each SM sub-partition gets the same count
   // (the output state no longer depends on rmax; D = 128 keeps 16 dims per lane in flight)
   return D == 64 ? 15 : (rmax <= 2 ? 15 : 11);
@@ -680,7 +684,6 @@ static int make_plan(const rfsn_attn_args* a, const rfsn_quantizer* qz, Plan& pl
   // (tile sizes are chosen after the shared-memory layout fixes the stage size)
   // kernel variant
   pl.rmax = R <= 1 ? 1 : R <= 2 ? 2 : R <= 4 ? 4 : 8;
-  pl.nw = consumer_warps(p.D, pl.rmax);
   const int64_t pq_bytes = (int64_t)p.M * p.K * p.ds * 2;
   const int64_t rvq_bytes = (int64_t)p.L * p.Kr * p.D * 2;
   // Shared-memory layout: codebooks and per-warp scratch first, the TMA ring
@@ -693,6 +696,7 @@ static int make_plan(const rfsn_attn_args* a, const rfsn_quantizer* qz, Plan& pl
   for (int attempt = 0; attempt < 2; ++attempt) {
     pl.rvq_smem = attempt == 0 && p.L > 0 && rvq_bytes <= 64 * 1024;
     pl.lp = pick_preset(p, pl.rvq_smem);
+    pl.nw = consumer_warps(p.D, pl.rmax, pl.lp);
     const bool pq_swap = pl.lp == kDs4Rvq1DenseS8 || pl.lp == kDs4Rvq1Mask;
     int64_t off = 0;
     p.smem_pq = (int)off; off = align_up(off + pq_bytes, 128);
@@ -779,7 +783,7 @@ static cudaError_t launch_ds(const Plan& pl, cudaStream_t s) {
     switch (pl.lp) {
       case kDs4Rvq1DenseS8: return launch_variant<D, RMAX, NW, kDs4Rvq1DenseS8>(pl, s);
       case kDs4Rvq1Mask: return launch_variant<D, RMAX, NW, kDs4Rvq1Mask>(pl, s);
-      case kDs8PqOnly: return launch_variant<D, RMAX, NW, kDs8PqOnly>(pl, s);
+      case kDs8PqOnly: return launch_variant<D, RMAX, consumer_warps(D, RMAX, kDs8PqOnly), kDs8PqOnly>(pl, s);
       case kDs8Rvq1Mask: return launch_variant<D, RMAX, NW, kDs8Rvq1Mask>(pl, s);
       default: break;
     }
@@ -791,17 +795,17 @@ static cudaError_t launch(const Plan& pl, cudaStream_t s) {
   const int D = pl.p.D;
   if (D == 64) {
     switch (pl.rmax) {
-      case 1: return launch_ds<64, 1, consumer_warps(64, 1)>(pl, s);
-      case 2: return launch_ds<64, 2, consumer_warps(64, 2)>(pl, s);
-      case 4: return launch_ds<64, 4, consumer_warps(64, 4)>(pl, s);
-      default: return launch_ds<64, 8, consumer_warps(64, 8)>(pl, s);
+      case 1: return launch_ds<64, 1, consumer_warps(64, 1, kGeneric)>(pl, s);
+      case 2: return launch_ds<64, 2, consumer_warps(64, 2, kGeneric)>(pl, s);
+      case 4: return launch_ds<64, 4, consumer_warps(64, 4, kGeneric)>(pl, s);
+      default: return launch_ds<64, 8, consumer_warps(64, 8, kGeneric)>(pl, s);
     }
   }
   switch (pl.rmax) {
-    case 1: return launch_ds<128, 1, consumer_warps(128, 1)>(pl, s);
-    case 2: return launch_ds<128, 2, consumer_warps(128, 2)>(pl, s);
-    case 4: return launch_ds<128, 4, consumer_warps(128, 4)>(pl, s);
-    default: return launch_ds<128, 8, consumer_warps(128, 8)>(pl, s);
+    case 1: return launch_ds<128, 1, consumer_warps(128, 1, kGeneric)>(pl, s);
+    case 2: return launch_ds<128, 2, consumer_warps(128, 2, kGeneric)>(pl, s);
+    case 4: return launch_ds<128, 4, consumer_warps(128, 4, kGeneric)>(pl, s);
+    default: return launch_ds<128, 8, consumer_warps(128, 8, kGeneric)>(pl, s);
   }
 }
 
