@@ -26,9 +26,23 @@ namespace rfsn {
 
 constexpr int kNormThreads = 256;
 
+// fp16 a + b as the layer's fp16 tensor add rounds it (fp32 sum, one rounding)
+__device__ __forceinline__ uint32_t hadd2_round(uint32_t a, uint32_t b) {
+  const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&a));
+  const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&b));
+  const __half2 h = __floats2half2_rn(__fadd_rn(fa.x, fb.x), __fadd_rn(fa.y, fb.y));
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 // One CTA per row.  Rows with dim % 8 == 0 and 16-byte aligned rows use 16-byte
-// loads; any other row shape takes the scalar loop.
-__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const uint16_t* __restrict__ x,
+// loads; any other row shape takes the scalar loop.  With `b` set, the row is
+// first x + b (fp16), written to `sum` and normalised (the layer's residual add
+// followed by its FFN RMSNorm); the row is re-read from `sum` by the thread
+// that wrote it.
+// (x and sum are not __restrict__: with b set the row is read back from sum, which
+// this kernel writes, so those loads must not take the read-only path)
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const uint16_t* x, const uint16_t* __restrict__ b,
+                                                               uint16_t* sum,
                                                                const float* __restrict__ w,
                                                                uint16_t* __restrict__ y, int dim, float eps,
                                                                int vec) {
@@ -36,6 +50,21 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const uint16_t* _
   const int64_t row = blockIdx.x;
   const uint16_t* xr = x + row * dim;
   uint16_t* yr = y + row * dim;
+  if (b) {  // residual add; the rest of the kernel reads the sum back
+    const uint16_t* br = b + row * dim;
+    uint16_t* sr = sum + row * dim;
+    if (vec) {
+      for (int i = threadIdx.x; i < dim / 8; i += blockDim.x) {
+        const uint4 u = reinterpret_cast<const uint4*>(xr)[i];
+        const uint4 v = reinterpret_cast<const uint4*>(br)[i];
+        reinterpret_cast<uint4*>(sr)[i] =
+            make_uint4(hadd2_round(u.x, v.x), hadd2_round(u.y, v.y), hadd2_round(u.z, v.z), hadd2_round(u.w, v.w));
+      }
+    } else {
+      for (int i = threadIdx.x; i < dim; i += blockDim.x) sr[i] = f2h(__fadd_rn(h2f(xr[i]), h2f(br[i])));
+    }
+    xr = sr;  // each thread re-reads only the elements it wrote (same loop order)
+  }
   float ss = 0.f;
   if (vec) {
     for (int i = threadIdx.x; i < dim / 8; i += blockDim.x) {
@@ -123,8 +152,22 @@ extern "C" int rfsn_rmsnorm_f16(const uint16_t* x, const float* weight, uint16_t
   if (rows == 0) return RFSN_OK;
   const int vec = dim % 8 == 0 && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0 &&
                   (reinterpret_cast<uintptr_t>(weight) & 15) == 0;
-  rmsnorm_kernel<<<(unsigned)rows, kNormThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(x, weight, y, dim, eps,
-                                                                                            vec);
+  rmsnorm_kernel<<<(unsigned)rows, kNormThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      x, nullptr, nullptr, weight, y, dim, eps, vec);
+  return check_cuda(cudaGetLastError());
+}
+
+extern "C" int rfsn_add_rmsnorm_f16(const uint16_t* x, const uint16_t* b, uint16_t* sum, const float* weight,
+                                    uint16_t* y, int64_t rows, int dim, float eps, void* stream) {
+  if (rows < 0 || dim <= 0 || (rows > 0 && (!x || !b || !sum || !weight || !y))) return RFSN_ERR_INVALID_ARGUMENT;
+  if (rows > 0x7fffffff) return RFSN_ERR_UNSUPPORTED;
+  if (rows == 0) return RFSN_OK;
+  const uintptr_t ptrs = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(b) |
+                         reinterpret_cast<uintptr_t>(sum) | reinterpret_cast<uintptr_t>(y) |
+                         reinterpret_cast<uintptr_t>(weight);
+  const int vec = dim % 8 == 0 && (ptrs & 15) == 0;
+  rmsnorm_kernel<<<(unsigned)rows, kNormThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(x, b, sum, weight, y,
+                                                                                            dim, eps, vec);
   return check_cuda(cudaGetLastError());
 }
 

@@ -375,6 +375,24 @@ def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
     return y
 
 
+def add_rms_norm(x: torch.Tensor, b: torch.Tensor, weight: torch.Tensor,
+                 eps: float) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(x + b, rms_norm(x + b)) for fp16 x, b of the same shape, in one launch."""
+    _need_cuda(x, "x")
+    if x.dtype != torch.float16 or b.dtype != torch.float16 or b.shape != x.shape or weight.dtype != torch.float32 \
+            or weight.numel() != x.shape[-1]:
+        raise ValueError("add_rms_norm expects fp16 x and b of one shape [..., dim] and an fp32 weight of dim")
+    x = x.contiguous()
+    b = b.contiguous()
+    w = weight.contiguous()
+    s = torch.empty_like(x)
+    y = torch.empty_like(x)
+    dim = int(x.shape[-1])
+    call("rfsn_add_rmsnorm_f16", _ptr(x), _ptr(b), _ptr(s), _ptr(w), _ptr(y), x.numel() // dim if dim else 0, dim,
+         float(eps), _stream(x.device.index))
+    return s, y
+
+
 def gelu_tanh(x: torch.Tensor) -> torch.Tensor:
     """Tanh-approximate GELU of fp16 x in one launch, rounded to fp16 after every operation."""
     _need_cuda(x, "x")

@@ -170,8 +170,12 @@ class RFSNDecoderLayerMLX:
         else:
             attended = _dense_exact_attention(q_heads, k_heads, v_heads, self.scale, causal=True)
         attn_out = self.o_proj(attended.reshape(B, -1, self.num_heads * self.head_dim)).to(residual.dtype)
-        hidden = residual + attn_out
-        ffn_input = self.ffn_norm(hidden).to(torch.float16)
+        if residual.is_cuda and residual.dtype == torch.float16 and attn_out.dtype == torch.float16:
+            # residual add and FFN RMSNorm in one launch (same roundings)
+            hidden, ffn_input = K.add_rms_norm(residual, attn_out, self.ffn_norm.weight, self.ffn_norm.eps)
+        else:
+            hidden = residual + attn_out
+            ffn_input = self.ffn_norm(hidden).to(torch.float16)
         up = self.ffn_up(ffn_input)
         act = K.gelu_tanh(up) if up.dtype == torch.float16 else _gelu(up)  # one launch for the fp16 chain
         ffn_out = self.ffn_down(act).to(hidden.dtype)

@@ -226,6 +226,12 @@ int rfsn_rmsnorm_f16(const uint16_t* x, const float* weight, uint16_t* y, int64_
                      void* stream);
 int rfsn_gelu_tanh_f16(const uint16_t* x, uint16_t* y, int64_t n, void* stream);
 
+/* sum = fp16(x + b) (one rounding of the fp32 sum, as the layer's fp16 residual add) and
+ * y = rfsn_rmsnorm_f16(sum) in one launch: the layer's `hidden = residual + attn_out`
+ * followed by its FFN RMSNorm (RFSNDecoderLayerMLX.__call__, rfsn_v10_mlx_ane_complete.py:114-172). */
+int rfsn_add_rmsnorm_f16(const uint16_t* x, const uint16_t* b, uint16_t* sum, const float* weight, uint16_t* y,
+                         int64_t rows, int dim, float eps, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

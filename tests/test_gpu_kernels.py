@@ -447,3 +447,16 @@ def test_fused_attention_strided_queries(Qn):
     odd = torch.zeros((B, Qn * Hq * D + 4), dtype=torch.float16, device="cuda")[:, :Qn * Hq * D].view(B, Qn, Hq, D)
     with pytest.raises(ValueError):
         K.decode_attention(qz, odd, out_v, segs, kv_heads=Hkv, causal=False, hot=(hot_k, hot_v), warm=ws)
+
+
+@pytest.mark.parametrize("rows,dim,offset", [(32, 2048, 0), (3, 1000, 0)])
+def test_fused_add_rmsnorm(rows, dim, offset):
+    """rfsn_add_rmsnorm_f16: the sum is the fp16 tensor add bit for bit, and the normalised
+    output equals rfsn_rmsnorm_f16 of that sum bit for bit (dim 1000 takes the scalar path)."""
+    g = torch.Generator(device="cuda").manual_seed(rows + dim)
+    x = (torch.randn((rows, dim), generator=g, device="cuda") * 2).half()
+    b = (torch.randn((rows, dim), generator=g, device="cuda") * 2).half()
+    w = torch.rand(dim, generator=g, device="cuda") + 0.5
+    s, y = K.add_rms_norm(x, b, w, 1e-5)
+    assert torch.equal(s, x + b)
+    assert torch.equal(y, K.rms_norm(x + b, w, 1e-5))
