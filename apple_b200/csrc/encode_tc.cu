@@ -65,6 +65,23 @@ __device__ __forceinline__ void mma1688(float c[4], uint32_t a0, uint32_t a1, ui
 // 16-byte chunk q of row i of a swizzled [rows][64] fp16 tile (128 B rows).
 __device__ __forceinline__ int swz(int i, int q) { return i * 8 + (q ^ (i & 7)); }
 
+// Two candidates' distances (x_sq - 2 dot) + c_sq with one paired fma.rn.f32x2 and
+// add.rn.f32x2: each element is rounded exactly as __fadd_rn(__fmaf_rn(-2, dot,
+// x_sq), c_sq) rounds it, in half the instructions.
+__device__ __forceinline__ void dist2(float& d0, float& d1, float dot0, float dot1, float xsq, float csq0,
+                                     float csq1) {
+  asm("{\n\t.reg .b64 C, M, X, D, E;\n\t"
+      "mov.b64 C, {%2, %3};\n\t"
+      "mov.b64 M, {%4, %4};\n\t"
+      "mov.b64 X, {%5, %5};\n\t"
+      "fma.rn.f32x2 D, M, C, X;\n\t"
+      "mov.b64 E, {%6, %7};\n\t"
+      "add.rn.f32x2 D, D, E;\n\t"
+      "mov.b64 {%0, %1}, D;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(dot0), "f"(dot1), "f"(-2.f), "f"(xsq), "f"(csq0), "f"(csq1));
+}
+
 // Running first-minimum: take (d, idx) if strictly smaller.
 __device__ __forceinline__ void take_min(float d, int idx, float& best, int& bi) {
   const bool p = d < best;
@@ -218,10 +235,13 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1) encode_tc_kernel(const __gri
           mma1688(c, a0, a1, b);
           const int code = nt * 8 + 2 * qd;
           const float2 cc = *reinterpret_cast<const float2*>(ccm + code);
-          take_min(__fadd_rn(__fmaf_rn(-2.f, c[0], xx0), cc.x), code, b00, i00);
-          take_min(__fadd_rn(__fmaf_rn(-2.f, c[1], xx0), cc.y), code + 1, b01, i01);
-          take_min(__fadd_rn(__fmaf_rn(-2.f, c[2], xx1), cc.x), code, b10, i10);
-          take_min(__fadd_rn(__fmaf_rn(-2.f, c[3], xx1), cc.y), code + 1, b11, i11);
+          float d0, d1, d2, d3;
+          dist2(d0, d1, c[0], c[1], xx0, cc.x, cc.y);
+          dist2(d2, d3, c[2], c[3], xx1, cc.x, cc.y);
+          take_min(d0, code, b00, i00);
+          take_min(d1, code + 1, b01, i01);
+          take_min(d2, code, b10, i10);
+          take_min(d3, code + 1, b11, i11);
         }
         merge_min(b00, i00, b01, i01);
         merge_min(b10, i10, b11, i11);
@@ -303,10 +323,13 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1) encode_tc_kernel(const __gri
           }
           const int code = nt * 8 + 2 * qd;
           const float2 cc = *reinterpret_cast<const float2*>(s_rcc + code);
-          take_min(__fadd_rn(__fmaf_rn(-2.f, c[0], rr0), cc.x), code, b00, i00);
-          take_min(__fadd_rn(__fmaf_rn(-2.f, c[1], rr0), cc.y), code + 1, b01, i01);
-          take_min(__fadd_rn(__fmaf_rn(-2.f, c[2], rr1), cc.x), code, b10, i10);
-          take_min(__fadd_rn(__fmaf_rn(-2.f, c[3], rr1), cc.y), code + 1, b11, i11);
+          float d0, d1, d2, d3;
+          dist2(d0, d1, c[0], c[1], rr0, cc.x, cc.y);
+          dist2(d2, d3, c[2], c[3], rr1, cc.x, cc.y);
+          take_min(d0, code, b00, i00);
+          take_min(d1, code + 1, b01, i01);
+          take_min(d2, code, b10, i10);
+          take_min(d3, code + 1, b11, i11);
         }
         merge_min(b00, i00, b01, i01);
         merge_min(b10, i10, b11, i11);
