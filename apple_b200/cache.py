@@ -523,7 +523,7 @@ class RFSNv10KVCacheMLX:
         q = q.to(device=self.device, dtype=torch.float16, non_blocking=bool(not q.is_cuda and q.is_pinned()))
         # a view whose sequences are each packed (e.g. the query heads of a wider projection
         # output) is read in place through the kernel's batch stride
-        pack = lambda t: t if K._queries_packed(t) else t.contiguous()  # noqa: E731
+        pack = lambda t: t if K.queries_packed(t) else t.contiguous()  # noqa: E731
         if self.batch == 1 and q.dim() == 3:
             return pack(q.unsqueeze(0)), True                 # [1, Q, Hq, D]
         if q.dim() == 3 and q.shape[0] == self.batch:

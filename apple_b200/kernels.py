@@ -282,7 +282,7 @@ class _AttnCall:
 _ATTN_CALLS: "dict" = {}
 
 
-def _queries_packed(q: torch.Tensor) -> bool:
+def queries_packed(q: torch.Tensor) -> bool:
     """[B, Q, Hq, D] with each sequence's queries packed and any batch stride the kernel takes."""
     B, Qn, Hq, D = q.shape
     inner = q.stride(3) == 1 and (Hq == 1 or q.stride(2) == D) and (Qn == 1 or q.stride(1) == Hq * D)
@@ -310,7 +310,7 @@ def decode_attention(qz: QuantizerBuffers, q: torch.Tensor, out: torch.Tensor, s
     segments: (store, slot, first, count, pos0) tuples in window order.
     """
     _need_cuda(q, "q")
-    if q.dtype != torch.float16 or q.dim() != 4 or not _queries_packed(q):
+    if q.dtype != torch.float16 or q.dim() != 4 or not queries_packed(q):
         raise ValueError("q must be fp16 [B, Q, Hq, D], packed within a sequence (batch stride a multiple of 8)")
     if out.shape != q.shape or out.dtype != torch.float16 or not out.is_contiguous():
         raise ValueError("out must be contiguous fp16 like q")

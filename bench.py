@@ -770,7 +770,9 @@ def run_layer(args) -> None:
                      "note": "latency-bound: about 10 kernel launches per step on a 4.4 MB working set"},
         "e2e": {"value": 1.0 / e2e_s, "unit": "steps/s", "h2d_bytes_per_step": c["hidden"] * 2,
                 "d2h_bytes_per_step": c["hidden"] * 2, "api": "RFSNDecoderLayerMLX.__call__(use_cache=True)"},
-        "clocks": clocks.summary(), "cpu_baseline": cpu}))
+        # ours per step: attention, RMSNorm, add + RMSNorm, GELU; plus a spill encode whenever the
+        # hot ring overflows (not counted)
+        "gpu_launches": 4 * steps, "clocks": clocks.summary(), "cpu_baseline": cpu}))
     layer.cache.close()
 
 
@@ -1184,7 +1186,8 @@ def run_stack(args) -> None:
             "e2e": {"value": c["batch"] / e2e_s, "unit": "tokens/s",
                     "h2d_bytes_per_step": hx.numel() * 2, "d2h_bytes_per_step": hx.numel() * 2,
                     "api": "RFSNDecoderLayerMLX.__call__(use_cache=True) x 22, eager, caches advancing"},
-            "gpu_launches": args.steps * c["layers"] * 3, "clocks": clocks.summary()}
+            # ours per layer: K+V encode, attention, RMSNorm, add + RMSNorm, GELU (projections are cuBLAS)
+            "gpu_launches": args.steps * c["layers"] * 5, "clocks": clocks.summary()}
         if world == 1:
             line["cpu_baseline"] = stack_cpu_baseline()
             line["cpu_baseline"]["value"] *= c["batch"]
