@@ -60,6 +60,9 @@ constexpr int kNoLimit = 1 << 30;         // position limit of a row that sees e
 // their fp32 partial output.
 __host__ __device__ constexpr int tokens_per_round(int, int lp) { return lp == kDs8PqOnly ? 4 : 2; }
 __host__ __device__ constexpr int scratch_bytes(int D) { return 2 * 2 * 4 * D * 2; }
+// PQ-only blocks also take two blocks (32 tokens) per softmax update, halving the
+// per-block cost of the max/sum shuffle chain; tiles then hold whole pairs.
+__host__ __device__ constexpr int blocks_per_chunk(int lp) { return lp == kDs8PqOnly ? 2 : 1; }
 constexpr int64_t kMaxSmem = 227 * 1024;  // opt-in shared memory per CTA on sm_100
 
 struct SegDev {
@@ -371,6 +374,8 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
   const float NEG_INF = __int_as_float(0xff800000);
   constexpr int NMMA = DPL / 4;  // K mma k-steps per row-step
   constexpr int kTpr = tokens_per_round(D, LP);
+  constexpr int kNB = blocks_per_chunk(LP);     // 16-token blocks per softmax update
+  constexpr int kChunk = kBlockTokens * kNB;
   constexpr int kBlock = LP != kGeneric ? Preset<LP>::BLOCK : 0;
   const int block_bytes = LP != kGeneric ? kBlock : p.lay.block_bytes;
 
@@ -448,31 +453,33 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
     // chunks (16-token blocks) are dealt round-robin over the CTA's whole tile
     // stream, so no warp carries an extra chunk of every tile
     const int span = lead + n;
-    const int nchunks = (span + kBlockTokens - 1) / kBlockTokens;
+    const int nchunks = (span + kChunk - 1) / kChunk;
     const int c_first = (warp - chunk_base % NW + NW) % NW;
     chunk_base += nchunks;
     for (int ch = c_first; ch < nchunks; ch += NW) {
       const int t_lo = ch == 0 ? lead : 0;
-      const int t_hi = min(kBlockTokens, span - ch * kBlockTokens);
-      const int pos_base = pos0 - lead + ch * kBlockTokens;
-      // a full block: all 16 tokens in range and visible to every live query row
-      const bool full = t_lo == 0 && t_hi == kBlockTokens &&
-                        __all_sync(0xffffffffu, srow >= p.R || c.qp_lim >= pos_base + kBlockTokens - 1);
+      const int t_hi = min(kChunk, span - ch * kChunk);
+      const int pos_base = pos0 - lead + ch * kChunk;
+      // a full chunk: all its tokens in range and visible to every live query row
+      const bool full = t_lo == 0 && t_hi == kChunk &&
+                        __all_sync(0xffffffffu, srow >= p.R || c.qp_lim >= pos_base + kChunk - 1);
       if (kind == 0) {
-        const uint16_t* hk = hot_k + (size_t)ch * kBlockTokens * D;
-        const uint16_t* hv = hot_v + (size_t)ch * kBlockTokens * D;
+        const uint16_t* hk = hot_k + (size_t)ch * kChunk * D;
+        const uint16_t* hv = hot_v + (size_t)ch * kChunk * D;
         if (full)
-          process_block<D, RMAX, LP, true, kTpr, true>(c, nullptr, hk, hv, t_lo, t_hi, pos_base, aq, acc, m_run, l_run);
+          process_block<D, RMAX, LP, true, kTpr, true, kNB>(c, nullptr, hk, hv, t_lo, t_hi, pos_base, aq, acc, m_run,
+                                                            l_run);
         else
-          process_block<D, RMAX, LP, true, kTpr, false>(c, nullptr, hk, hv, t_lo, t_hi, pos_base, aq, acc, m_run, l_run);
+          process_block<D, RMAX, LP, true, kTpr, false, kNB>(c, nullptr, hk, hv, t_lo, t_hi, pos_base, aq, acc, m_run,
+                                                             l_run);
       } else {
-        const unsigned char* blk = sb + ch * block_bytes;
+        const unsigned char* blk = sb + ch * kNB * block_bytes;
         if (full)
-          process_block<D, RMAX, LP, false, kTpr, true>(c, blk, nullptr, nullptr, t_lo, t_hi, pos_base, aq, acc, m_run,
-                                                        l_run);
+          process_block<D, RMAX, LP, false, kTpr, true, kNB>(c, blk, nullptr, nullptr, t_lo, t_hi, pos_base, aq, acc,
+                                                             m_run, l_run);
         else
-          process_block<D, RMAX, LP, false, kTpr, false>(c, blk, nullptr, nullptr, t_lo, t_hi, pos_base, aq, acc, m_run,
-                                                         l_run);
+          process_block<D, RMAX, LP, false, kTpr, false, kNB>(c, blk, nullptr, nullptr, t_lo, t_hi, pos_base, aq, acc,
+                                                              m_run, l_run);
       }
     }
     // release the stage
@@ -571,12 +578,12 @@ struct Plan {
 };
 
 // Consumer warps per CTA, chosen so the per-thread register budget of one
-// CTA per SM covers q and the output accumulator without spilling.  PQ-only
-// blocks (one gather per token, no RVQ or sparse state) fit 96 registers, so they
-// run 19 consumer warps: the kernel is latency-bound there, and more warps hide
-// more of it.  The other presets spill at 96 and keep 15.
+// CTA per SM covers q and the output accumulator without spilling.  (Measured
+// for PQ-only blocks on B200: one-block chunks at 19 warps / 96 registers ran
+// 58.7 us per config-3 launch, two-block chunks at 15 warps / 128 registers
+// 58.0 us; two-block chunks spill at 96 registers.)
 static constexpr int consumer_warps(int D, int rmax, int lp) {
-  if (D == 64 && lp == kDs8PqOnly) return 19;
+  if (D == 64 && lp == kDs8PqOnly) return 15;
   // total warps (NW + producer) a multiple of 4 so each SM sub-partition gets the same count
   // (the output state no longer depends on rmax; D = 128 keeps 16 dims per lane in flight)
   return D == 64 ? 15 : (rmax <= 2 ? 15 : 11);
@@ -720,9 +727,10 @@ static int make_plan(const rfsn_attn_args* a, const rfsn_quantizer* qz, Plan& pl
   // costs a ring round trip, so tiles are as large as the stage allows)
   p.tile_blocks = p.stage_bytes / p.lay.block_bytes;
   if (p.tile_blocks > 1024) p.tile_blocks = 1024;
+  p.tile_blocks -= p.tile_blocks % blocks_per_chunk(pl.lp);  // a chunk never reads past its stage
   if (p.tile_blocks < 2) return RFSN_ERR_UNSUPPORTED;
-  p.tile_dense = (p.stage_bytes / (4 * p.D)) / 16 * 16;  // K and V rows of fp16
-  if (p.tile_dense < 16) return RFSN_ERR_UNSUPPORTED;
+  p.tile_dense = (p.stage_bytes / (4 * p.D)) / 32 * 32;  // K and V rows of fp16, whole 32-token chunks
+  if (p.tile_dense < 32) return RFSN_ERR_UNSUPPORTED;
   p.rvq_smem = pl.rvq_smem ? 1 : 0;
   if (pl.smem > kMaxSmem) return RFSN_ERR_UNSUPPORTED;
 

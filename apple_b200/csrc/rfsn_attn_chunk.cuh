@@ -212,15 +212,20 @@ __device__ __forceinline__ void sparse_round(const ChunkCtx& c, const unsigned c
 
 // Rebuild this lane's dims of its TPR tokens tb[i] (K or V fields), all loads
 // of the round issued before any is used.
-template <int D, int LP, bool DENSE, int TPR>
+// NB: 16-token blocks per chunk; token tb of the chunk lives in block tb / 16
+// (consecutive blocks of a tile are adjacent in shared memory).
+template <int D, int LP, bool DENSE, int TPR, int NB = 1>
 __device__ __forceinline__ void load_round(const ChunkCtx& c, const unsigned char* blk, const uint16_t* dense,
                                            int kv, const int* tb, const bool* valid, int t_lo, int round, int slot,
                                            int j, int dim0, bool odd, uint32_t (*w)[D / 16]) {
   constexpr int DPL = D / 8;
+  static_assert(NB == 1 || (LP != kGeneric && Preset<LP>::S == 0), "multi-block chunks: fixed layouts without sparse");
 #pragma unroll
   for (int i = 0; i < TPR; ++i) {
     if constexpr (DENSE) {
       load_dense<DPL>(dense + (valid[i] ? tb[i] : t_lo) * D + dim0, w[i]);
+    } else if constexpr (LP != kGeneric && NB > 1) {
+      recon_fast<LP>(c, blk + (tb[i] >> 4) * Preset<LP>::BLOCK, kv, tb[i] & 15, j, odd, w[i]);
     } else if constexpr (LP != kGeneric) {
       recon_fast<LP>(c, blk, kv, tb[i], j, odd, w[i]);
     } else {
@@ -232,10 +237,10 @@ __device__ __forceinline__ void load_round(const ChunkCtx& c, const unsigned cha
   }
 }
 
-// One 16-token chunk: K scores on tensor cores, online softmax, then P.V on
-// tensor cores.  blk: the block's bytes (code tiles); dense_k/dense_v: the
-// chunk's 16 hot rows (dense tiles).  Valid tokens are [t_lo, t_hi); token tb is
-// at position pos_base + tb.  TPR tokens per lane are loaded per round (4 / TPR
+// One chunk of NB 16-token blocks: K scores on tensor cores, online softmax,
+// then P.V on tensor cores.  blk: the first block's bytes (code tiles; the next
+// block follows it); dense_k/dense_v: the chunk's hot rows (dense tiles).  Valid
+// tokens are [t_lo, t_hi); token tb is at position pos_base + tb.  TPR tokens per lane are loaded per round (4 / TPR
 // rounds per phase); a round's loads are all in flight before its arithmetic.
 //
 // Output accumulators (D/16 tiles x 4 per lane): lane (g = lane/4, q = lane%4)
@@ -247,15 +252,16 @@ __device__ __forceinline__ void load_round(const ChunkCtx& c, const unsigned cha
 // (the common case; the caller decides it warp-uniformly), so the per-token
 // range checks and score masks compile away.  Rows past the KV head's query
 // count then score 0 instead of being masked; their state is never read.
-template <int D, int RMAX, int LP, bool DENSE, int TPR, bool FULL>
+template <int D, int RMAX, int LP, bool DENSE, int TPR, bool FULL, int NB = 1>
 __device__ __forceinline__ void process_block(const ChunkCtx& c, const unsigned char* blk, const uint16_t* dense_k,
                                               const uint16_t* dense_v, int t_lo, int t_hi, int pos_base,
                                               const uint32_t (*aq)[4], float (*acc)[4], float& m_run,
                                               float& l_run) {
   constexpr int DPL = D / 8;
-  constexpr int NT = D / 16;   // P.V tiles of 16 dims
+  constexpr int NT = D / 16;        // P.V tiles of 16 dims
   constexpr int NMMA = DPL / 4;
-  constexpr int NR = 4 / TPR;  // rounds per phase
+  constexpr int NR = 4 * NB / TPR;  // rounds per phase
+  constexpr int NS = 4 * NB;        // scores per lane (tokens 4 rs + lane%4)
   static_assert(TPR == 2 || TPR == 4, "P.V takes the tokens of a round as one k8 (2) or k16 (4) step");
   static_assert(RMAX <= 8, "P.V covers at most 8 query rows");
   const float NEG_INF = __int_as_float(0xff800000);
@@ -267,7 +273,7 @@ __device__ __forceinline__ void process_block(const ChunkCtx& c, const unsigned 
   const int s_hi = min(t_hi, c.qp_lim - pos_base + 1);
 
   // ---------------- scores ----------------
-  float sc[4];
+  float sc[NS];
 #pragma unroll
   for (int rr = 0; rr < NR; ++rr) {
     int tb[TPR];
@@ -278,7 +284,7 @@ __device__ __forceinline__ void process_block(const ChunkCtx& c, const unsigned 
       valid[i] = FULL || (tb[i] >= t_lo && tb[i] < t_hi);
     }
     uint32_t w[TPR][DPL / 2];
-    load_round<D, LP, DENSE, TPR>(c, blk, dense_k, 0, tb, valid, t_lo, rr, slot, j, dim0, odd, w);
+    load_round<D, LP, DENSE, TPR, NB>(c, blk, dense_k, 0, tb, valid, t_lo, rr, slot, j, dim0, odd, w);
     float cfr[TPR][4];
 #pragma unroll
     for (int i = 0; i < TPR; ++i) {
@@ -294,17 +300,19 @@ __device__ __forceinline__ void process_block(const ChunkCtx& c, const unsigned 
     }
   }
 
-  // ---------------- online softmax of row lane/4 over the 16 tokens ----------------
+  // ---------------- online softmax of row lane/4 over the chunk's tokens ----------------
   float cmax = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+#pragma unroll
+  for (int rs = 4; rs < NS; rs += 2) cmax = fmaxf(cmax, fmaxf(sc[rs], sc[rs + 1]));
   cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 1));
   cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 2));
   const float m_new = fmaxf(m_run, cmax);
   float alpha = 1.f;
   if (m_new > m_run) alpha = (m_run == NEG_INF) ? 0.f : ex2_approx(m_run - m_new);
-  float pr[4];
+  float pr[NS];
   float lsum = 0.f;
 #pragma unroll
-  for (int rs = 0; rs < 4; ++rs) {
+  for (int rs = 0; rs < NS; ++rs) {
     pr[rs] = (!FULL && sc[rs] == NEG_INF) ? 0.f : ex2_approx(sc[rs] - m_new);
     lsum += pr[rs];
   }
@@ -342,7 +350,7 @@ __device__ __forceinline__ void process_block(const ChunkCtx& c, const unsigned 
       valid[i] = FULL || (tb[i] >= t_lo && tb[i] < t_hi);
     }
     uint32_t w[TPR][DPL / 2];
-    load_round<D, LP, DENSE, TPR>(c, blk, dense_v, 1, tb, valid, t_lo, NR + rr, slot, j, dim0, odd, w);
+    load_round<D, LP, DENSE, TPR, NB>(c, blk, dense_v, 1, tb, valid, t_lo, NR + rr, slot, j, dim0, odd, w);
     uint32_t bhi[TPR / 2], blo[TPR / 2];
 #pragma unroll
     for (int h = 0; h < TPR / 2; ++h) split_h2(pr[rr * TPR + 2 * h], pr[rr * TPR + 2 * h + 1], bhi[h], blo[h]);
