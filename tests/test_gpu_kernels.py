@@ -218,6 +218,7 @@ def _make_cfg2_like(rng, B, Hkv, G, D, T_hot, T_warm, S=8, ds=4, L=1, thr=-1.0, 
     (1, 2, 4, 1, 64, 4, 1, 12, -1.0, 40, 300, 0),      # top-12 sparse: two entries per lane
     (1, 2, 4, 2, 64, 4, 1, 8, -1.0, 64, 600, 0),       # config-2 preset with R = 8 query rows
     (2, 2, 1, 1, 64, 4, 1, 8, -1.0, 32, 500, 3),       # config-2 preset with R = 1
+    (2, 4, 8, 1, 64, 8, 0, 0, 0.0, 48, 1013, 5),       # config-3 preset (PQ 8x8, GQA 8): partial 32-token chunks
 ])
 def test_fused_attention_vs_oracle(B, Hkv, G, Qn, D, ds, L, S, thr, T_hot, T_warm, num_ctas):
     rng = np.random.default_rng(B * 1000 + Hkv * 10 + D + L)
