@@ -118,50 +118,96 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1) encode_tc_kernel(const __gri
   const int nthr = blockDim.x;
   const int K = p.K, Kr = p.Kr;
 
-  // ---- stage codebooks and their squared norms (sequential fp32 sums) ----
-  for (int i = threadIdx.x; i < M * K * DS / 8; i += nthr)
-    reinterpret_cast<uint4*>(s_pq)[i] = __ldg(reinterpret_cast<const uint4*>(p.pq_cb) + i);
-  if (p.L > 0) {
-    for (int i = threadIdx.x; i < Kr * 8; i += nthr) {
-      const int c = i >> 3, q = i & 7;
-      s_rvq[swz(c, q)] = __ldg(reinterpret_cast<const uint4*>(p.rvq_cb) + i);
-    }
-  }
-  __syncthreads();  // norms are summed from the staged copies
-  for (int i = threadIdx.x; i < M * K; i += nthr) {
-    const uint16_t* c = s_pq + (size_t)i * DS;
-    float s = 0.f;
-#pragma unroll
-    for (int k = 0; k < DS; ++k) {
-      const float v = h2f(c[k]);
-      s = __fmaf_rn(v, v, s);
-    }
-    s_pqcc[i] = s;
-  }
-  if (p.L > 0) {
-    for (int i = threadIdx.x; i < Kr; i += nthr) {
-      float s = 0.f;
-      for (int q = 0; q < 8; ++q) {
-        const uint4 r = s_rvq[swz(i, q)];
-        const uint32_t w4[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[k]));
-          s = __fmaf_rn(f.x, f.x, s);
-          s = __fmaf_rn(f.y, f.y, s);
-        }
-      }
-      s_rcc[i] = s;
-    }
-  }
-  __syncthreads();
-
-  // tiles: each group's leader warp (part 0) owns them; in split mode the group's
-  // other warps write their subspaces' codes into the leader's s_code
   const int split = p.split;
   const int gpc = kTcWarps / split;  // groups per CTA and round
   const int gslot = warp / split, part = warp - gslot * split;
   const bool lead = part == 0;
+
+  // ---- stage codebooks and their squared norms (sequential fp32 sums) ----
+  if (split > 1) {
+    // Split mode: warp `part` of the first group stages PQ subspace `part` and sums its
+    // norms itself, while the leaders load their x tiles; the barrier before the search
+    // publishes every slice to every warp (the leader's residual step reads them after
+    // the barrier that follows the search).
+    if (gslot == 0) {
+      const int n = K * DS / 8;
+      const uint4* src = reinterpret_cast<const uint4*>(p.pq_cb) + (size_t)part * n;
+      uint4* dst = reinterpret_cast<uint4*>(s_pq) + (size_t)part * n;
+      for (int i = lane; i < n; i += 32) dst[i] = __ldg(src + i);
+      __syncwarp();
+      for (int i = lane; i < K; i += 32) {
+        const uint16_t* c = s_pq + ((size_t)part * K + i) * DS;
+        float s = 0.f;
+#pragma unroll
+        for (int k = 0; k < DS; ++k) {
+          const float v = h2f(c[k]);
+          s = __fmaf_rn(v, v, s);
+        }
+        s_pqcc[part * K + i] = s;
+      }
+    }
+    if (p.L > 0) {
+      for (int i = threadIdx.x; i < Kr * 8; i += nthr) {
+        const int c = i >> 3, q = i & 7;
+        s_rvq[swz(c, q)] = __ldg(reinterpret_cast<const uint4*>(p.rvq_cb) + i);
+      }
+      __syncthreads();
+      for (int i = threadIdx.x; i < Kr; i += nthr) {
+        float s = 0.f;
+        for (int q = 0; q < 8; ++q) {
+          const uint4 r = s_rvq[swz(i, q)];
+          const uint32_t w4[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[k]));
+            s = __fmaf_rn(f.x, f.x, s);
+            s = __fmaf_rn(f.y, f.y, s);
+          }
+        }
+        s_rcc[i] = s;
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < M * K * DS / 8; i += nthr)
+      reinterpret_cast<uint4*>(s_pq)[i] = __ldg(reinterpret_cast<const uint4*>(p.pq_cb) + i);
+    if (p.L > 0) {
+      for (int i = threadIdx.x; i < Kr * 8; i += nthr) {
+        const int c = i >> 3, q = i & 7;
+        s_rvq[swz(c, q)] = __ldg(reinterpret_cast<const uint4*>(p.rvq_cb) + i);
+      }
+    }
+    __syncthreads();  // norms are summed from the staged copies
+    for (int i = threadIdx.x; i < M * K; i += nthr) {
+      const uint16_t* c = s_pq + (size_t)i * DS;
+      float s = 0.f;
+#pragma unroll
+      for (int k = 0; k < DS; ++k) {
+        const float v = h2f(c[k]);
+        s = __fmaf_rn(v, v, s);
+      }
+      s_pqcc[i] = s;
+    }
+    if (p.L > 0) {
+      for (int i = threadIdx.x; i < Kr; i += nthr) {
+        float s = 0.f;
+        for (int q = 0; q < 8; ++q) {
+          const uint4 r = s_rvq[swz(i, q)];
+          const uint32_t w4[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[k]));
+            s = __fmaf_rn(f.x, f.x, s);
+            s = __fmaf_rn(f.y, f.y, s);
+          }
+        }
+        s_rcc[i] = s;
+      }
+    }
+    __syncthreads();
+  }
+
+  // tiles: each group's leader warp (part 0) owns them; in split mode the group's
+  // other warps write their subspaces' codes into the leader's s_code
   unsigned char* wb = smem + p.smem_warp + (size_t)(gslot * split) * p.warp_bytes;
   uint4* xt = reinterpret_cast<uint4*>(wb);                    // [16][8 chunks] swizzled x
   uint4* rt = xt + 16 * 8;                                     // [16][8 chunks] swizzled residual
