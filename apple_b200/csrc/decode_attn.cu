@@ -186,7 +186,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
   TileDesc* descs = reinterpret_cast<TileDesc*>(smem + p.smem_desc);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + p.smem_flag);
   uint16_t* s_pq = reinterpret_cast<uint16_t*>(smem + p.smem_pq);
-  uint16_t* s_pqsw = reinterpret_cast<uint16_t*>(smem + p.smem_pqsw);  // 4-dim presets only
+  uint16_t* s_pqsw = reinterpret_cast<uint16_t*>(smem + p.smem_pqsw);  // 4-dim presets; PQ-only: 3 V copies
   uint16_t* s_rvq = reinterpret_cast<uint16_t*>(smem + p.smem_rvq);
 
   const int warp = threadIdx.x >> 5;
@@ -213,7 +213,14 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
       for (int i = threadIdx.x; i < nc * per; i += nthr) {
         const int cen = i / per, part = i - cen * per;
         const int c = cen / p.M, m = cen - c * p.M;
-        reinterpret_cast<uint4*>(s_pq)[i] = __ldg(reinterpret_cast<const uint4*>(p.pq_cb) + (m * p.K + c) * per + part);
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(p.pq_cb) + (m * p.K + c) * per + part);
+        reinterpret_cast<uint4*>(s_pq)[i] = v;
+        if constexpr (LP == kDs8PqOnly) {
+          // copies q = 1..3 for the V gathers of lanes with lane % 4 == q: subspace m at
+          // position m ^ 2q, so a quarter-warp's 8 lanes hit 8 distinct bank groups
+#pragma unroll
+          for (int q = 1; q < 4; ++q) reinterpret_cast<uint4*>(s_pqsw)[(q - 1) * nc + c * 8 + (m ^ (2 * q))] = v;
+        }
       }
     } else if (p.ds == 4) {
       // 4-dim presets also stage a copy with subspace pairs swapped (position m holds m^1)
@@ -382,6 +389,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
   ChunkCtx c;
   c.pq_cm = s_pq;
   c.pq_sel = (Preset<LP>::DS == 4 && LP != kGeneric && (slot & 1)) ? s_pqsw : s_pq;
+  c.pq_vsel = (LP == kDs8PqOnly && (lane & 3)) ? s_pqsw + (size_t)((lane & 3) - 1) * p.M * p.K * p.ds : s_pq;
   c.rvq_s = s_rvq;
   c.rvq_g = p.rvq_cb;
   c.scratch = reinterpret_cast<uint16_t*>(scr);
@@ -707,7 +715,9 @@ static int make_plan(const rfsn_attn_args* a, const rfsn_quantizer* qz, Plan& pl
     const bool pq_swap = pl.lp == kDs4Rvq1DenseS8 || pl.lp == kDs4Rvq1Mask;
     int64_t off = 0;
     p.smem_pq = (int)off; off = align_up(off + pq_bytes, 128);
-    p.smem_pqsw = (int)off; if (pq_swap) off = align_up(off + pq_bytes, 128);
+    p.smem_pqsw = (int)off;
+    if (pq_swap) off = align_up(off + pq_bytes, 128);
+    if (pl.lp == kDs8PqOnly) off = align_up(off + 3 * pq_bytes, 128);  // V-gather copies
     p.smem_rvq = (int)off; if (pl.rvq_smem) off = align_up(off + rvq_bytes, 128);
     p.smem_scr = (int)off; off = align_up(off + (int64_t)pl.nw * p.scr_bytes, 128);
     p.smem_ml = (int)off; off = align_up(off + (int64_t)pl.nw * pl.rmax * 2 * 4, 128);

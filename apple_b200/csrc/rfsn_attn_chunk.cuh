@@ -74,6 +74,7 @@ __host__ inline bool preset_layout_matches(const BlockLayout& b) {
 struct ChunkCtx {
   const uint16_t* pq_cm;   // code-major PQ codebook [K][M][ds] (shared)
   const uint16_t* pq_sel;  // this lane's copy: pq_cm, or the pair-swapped copy for odd slots (4-dim presets)
+  const uint16_t* pq_vsel; // PQ-only preset: this lane's copy for V gathers (subspace m at m ^ 2(lane%4))
   const uint16_t* rvq_s;   // RVQ codebook [L][Kr][D] (shared, when staged)
   const uint16_t* rvq_g;   // RVQ codebook (global)
   uint16_t* scratch;       // this warp's sparse scatter rows [2 sets][tokens per round][4 slots][D] fp16
@@ -339,6 +340,46 @@ __device__ __forceinline__ void process_block(const ChunkCtx& c, const unsigned 
   // 8q + g, pairs them by token with byte permutes, and supplies its own probabilities of those
   // tokens for row g (left in this lane by the score phase) split into fp16 hi + lo halves.
   // Two tokens per round: one m16n8k8 per tile; four: one m16n8k16.
+  if constexpr (!DENSE && LP == kDs8PqOnly) {
+    // PQ-only code tiles: lane (g, q) gathers V of its own k-pair tokens (4(rr*TPR + i) + q) at
+    // subspace g (dims [8g, 8g+8)) straight from its codebook copy, so no shuffles are needed
+    using P = Preset<LP>;
+    const int g = lane >> 2;
+    const uint16_t* cb = c.pq_vsel;
+    const int pos = g ^ (2 * sslot);
+#pragma unroll
+    for (int rr = 0; rr < NR; ++rr) {
+      uint32_t w[TPR][4];
+#pragma unroll
+      for (int i = 0; i < TPR; ++i) {
+        const int tb = 4 * (rr * TPR + i) + sslot;
+        const unsigned char* f = blk + (tb >> 4) * P::BLOCK + P::FB;
+        const uint32_t code = f[P::OPQ + (tb & 15) * P::M + g];
+        const uint4 v = *reinterpret_cast<const uint4*>(cb + ((code * P::M + pos) << 3));
+        w[i][0] = v.x; w[i][1] = v.y; w[i][2] = v.z; w[i][3] = v.w;
+      }
+      uint32_t bhi[TPR / 2], blo[TPR / 2];
+#pragma unroll
+      for (int h = 0; h < TPR / 2; ++h) split_h2(pr[rr * TPR + 2 * h], pr[rr * TPR + 2 * h + 1], bhi[h], blo[h]);
+#pragma unroll
+      for (int u = 0; u < NT; ++u) {
+        uint32_t a[TPR];
+#pragma unroll
+        for (int h = 0; h < TPR / 2; ++h) {
+          a[2 * h] = prmt(w[2 * h][u], w[2 * h + 1][u], 0x5410u);
+          a[2 * h + 1] = prmt(w[2 * h][u], w[2 * h + 1][u], 0x7632u);
+        }
+        if constexpr (TPR == 2) {
+          mma16808(acc[u], a[0], a[1], bhi[0]);
+          mma16808(acc[u], a[0], a[1], blo[0]);
+        } else {
+          mma16816(acc[u], a, bhi[0], bhi[1]);
+          mma16816(acc[u], a, blo[0], blo[1]);
+        }
+      }
+    }
+    return;
+  }
   const int src = (sslot << 3) | (lane >> 2);
 #pragma unroll
   for (int rr = 0; rr < NR; ++rr) {
