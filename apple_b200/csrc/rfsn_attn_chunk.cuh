@@ -85,9 +85,11 @@ struct ChunkCtx {
 };
 
 // Fast path: this lane's 8 dims of token tb of a block, K (kv = 0) or V (kv = 1) fields.
+// rvq_in / act_in: the token's RVQ code and activity byte when the caller has them
+// already (one 16-byte load per field and phase), else -1 to read them here.
 template <int LP>
 __device__ __forceinline__ void recon_fast(const ChunkCtx& c, const unsigned char* blk, int kv, int tb, int j,
-                                           bool odd, uint32_t* w) {
+                                           bool odd, uint32_t* w, int rvq_in = -1, int act_in = -1) {
   using P = Preset<LP>;
   const unsigned char* f = blk + kv * P::FB;
   if constexpr (P::DS == 4) {
@@ -105,9 +107,9 @@ __device__ __forceinline__ void recon_fast(const ChunkCtx& c, const unsigned cha
     w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
   }
   if constexpr (P::L == 1) {
-    const uint32_t code = f[P::ORVQ + tb];
+    const uint32_t code = rvq_in >= 0 ? (uint32_t)rvq_in : f[P::ORVQ + tb];
     if constexpr (P::MASK) {
-      const bool act = f[P::OACT + tb] != 0;
+      const bool act = (act_in >= 0 ? act_in : f[P::OACT + tb]) != 0;
       const uint4 r = *reinterpret_cast<const uint4*>(c.rvq_s + (act ? code : 0u) * 64 + 8 * j);
       w[0] = hadd2_u32(w[0], act ? r.x : 0u); w[1] = hadd2_u32(w[1], act ? r.y : 0u);
       w[2] = hadd2_u32(w[2], act ? r.z : 0u); w[3] = hadd2_u32(w[3], act ? r.w : 0u);
@@ -215,10 +217,15 @@ __device__ __forceinline__ void sparse_round(const ChunkCtx& c, const unsigned c
 // of the round issued before any is used.
 // NB: 16-token blocks per chunk; token tb of the chunk lives in block tb / 16
 // (consecutive blocks of a tile are adjacent in shared memory).
+// rq / ra (fixed layouts with one RVQ layer, one-block chunks): the phase's 16 RVQ
+// codes / activity bytes as 4 words; token 4 rs + slot of round-token rs = rsbase + i is
+// byte `slot` of word rs.
 template <int D, int LP, bool DENSE, int TPR, int NB = 1>
 __device__ __forceinline__ void load_round(const ChunkCtx& c, const unsigned char* blk, const uint16_t* dense,
                                            int kv, const int* tb, const bool* valid, int t_lo, int round, int slot,
-                                           int j, int dim0, bool odd, uint32_t (*w)[D / 16]) {
+                                           int j, int dim0, bool odd, uint32_t (*w)[D / 16],
+                                           const uint32_t* rq = nullptr, const uint32_t* ra = nullptr,
+                                           int rsbase = 0) {
   constexpr int DPL = D / 8;
   static_assert(NB == 1 || (LP != kGeneric && Preset<LP>::S == 0), "multi-block chunks: fixed layouts without sparse");
 #pragma unroll
@@ -227,6 +234,10 @@ __device__ __forceinline__ void load_round(const ChunkCtx& c, const unsigned cha
       load_dense<DPL>(dense + (valid[i] ? tb[i] : t_lo) * D + dim0, w[i]);
     } else if constexpr (LP != kGeneric && NB > 1) {
       recon_fast<LP>(c, blk + (tb[i] >> 4) * Preset<LP>::BLOCK, kv, tb[i] & 15, j, odd, w[i]);
+    } else if constexpr (LP != kGeneric && Preset<LP>::L == 1) {
+      const int code = (int)((rq[rsbase + i] >> (8 * slot)) & 0xffu);
+      const int act = Preset<LP>::MASK ? (int)((ra[rsbase + i] >> (8 * slot)) & 0xffu) : -1;
+      recon_fast<LP>(c, blk, kv, tb[i], j, odd, w[i], code, act);
     } else if constexpr (LP != kGeneric) {
       recon_fast<LP>(c, blk, kv, tb[i], j, odd, w[i]);
     } else {
@@ -273,6 +284,19 @@ __device__ __forceinline__ void process_block(const ChunkCtx& c, const unsigned 
   // score lane (row lane/4, token slot sslot): visible tokens are [t_lo, s_hi)
   const int s_hi = min(t_hi, c.qp_lim - pos_base + 1);
 
+  // one broadcast 16-byte load per field and phase for the RVQ codes / activity bytes
+  constexpr bool kCodeWords = !DENSE && LP != kGeneric && NB == 1 && Preset<LP>::L == 1;
+  uint32_t rq[4] = {0u, 0u, 0u, 0u}, ra[4] = {0u, 0u, 0u, 0u};
+  if constexpr (kCodeWords) {
+    using P = Preset<LP>;
+    const uint4 r4 = *reinterpret_cast<const uint4*>(blk + P::ORVQ);
+    rq[0] = r4.x; rq[1] = r4.y; rq[2] = r4.z; rq[3] = r4.w;
+    if constexpr (P::MASK) {
+      const uint4 a4 = *reinterpret_cast<const uint4*>(blk + P::OACT);
+      ra[0] = a4.x; ra[1] = a4.y; ra[2] = a4.z; ra[3] = a4.w;
+    }
+  }
+
   // ---------------- scores ----------------
   float sc[NS];
 #pragma unroll
@@ -285,7 +309,8 @@ __device__ __forceinline__ void process_block(const ChunkCtx& c, const unsigned 
       valid[i] = FULL || (tb[i] >= t_lo && tb[i] < t_hi);
     }
     uint32_t w[TPR][DPL / 2];
-    load_round<D, LP, DENSE, TPR, NB>(c, blk, dense_k, 0, tb, valid, t_lo, rr, slot, j, dim0, odd, w);
+    load_round<D, LP, DENSE, TPR, NB>(c, blk, dense_k, 0, tb, valid, t_lo, rr, slot, j, dim0, odd, w, rq, ra,
+                                      rr * TPR);
     float cfr[TPR][4];
 #pragma unroll
     for (int i = 0; i < TPR; ++i) {
@@ -329,6 +354,16 @@ __device__ __forceinline__ void process_block(const ChunkCtx& c, const unsigned 
     for (int u = 0; u < NT; ++u) {
       acc[u][0] *= a0; acc[u][2] *= a0;
       acc[u][1] *= a1; acc[u][3] *= a1;
+    }
+  }
+
+  if constexpr (kCodeWords) {  // the V fields' codes
+    using P = Preset<LP>;
+    const uint4 r4 = *reinterpret_cast<const uint4*>(blk + P::FB + P::ORVQ);
+    rq[0] = r4.x; rq[1] = r4.y; rq[2] = r4.z; rq[3] = r4.w;
+    if constexpr (P::MASK) {
+      const uint4 a4 = *reinterpret_cast<const uint4*>(blk + P::FB + P::OACT);
+      ra[0] = a4.x; ra[1] = a4.y; ra[2] = a4.z; ra[3] = a4.w;
     }
   }
 
@@ -391,7 +426,8 @@ __device__ __forceinline__ void process_block(const ChunkCtx& c, const unsigned 
       valid[i] = FULL || (tb[i] >= t_lo && tb[i] < t_hi);
     }
     uint32_t w[TPR][DPL / 2];
-    load_round<D, LP, DENSE, TPR, NB>(c, blk, dense_v, 1, tb, valid, t_lo, NR + rr, slot, j, dim0, odd, w);
+    load_round<D, LP, DENSE, TPR, NB>(c, blk, dense_v, 1, tb, valid, t_lo, NR + rr, slot, j, dim0, odd, w, rq, ra,
+                                      rr * TPR);
     uint32_t bhi[TPR / 2], blo[TPR / 2];
 #pragma unroll
     for (int h = 0; h < TPR / 2; ++h) split_h2(pr[rr * TPR + 2 * h], pr[rr * TPR + 2 * h + 1], bhi[h], blo[h]);
