@@ -85,6 +85,10 @@ class RFSNv10KVCacheMLX:
         self._cold: Optional[ColdTier] = None
         self._cold_root: Optional[Path] = None
         self._plan_cache: Dict[Tuple, Tuple[List, Dict[str, int]]] = {}
+        # prepared attention calls for cached plans; _store_epoch changes whenever a store
+        # buffer or the quantizer is replaced, which retires the calls that point at them
+        self._attn_calls: Dict[Tuple, Any] = {}
+        self._store_epoch = 0
 
     # ------------------------------------------------------------------ stats
     def _empty_access_stats(self) -> Dict[str, int]:
@@ -191,6 +195,8 @@ class RFSNv10KVCacheMLX:
             if (qz.M, qz.K, qz.ds, qz.L, qz.Kr, qz.sparse_topk) != (self._qz.M, self._qz.K, self._qz.ds, self._qz.L,
                                                                      self._qz.Kr, self._qz.sparse_topk):
                 raise ValueError("quantizer layout changed after tokens were cached")
+        if qz is not self._qz:
+            self._store_epoch += 1
         self._qz = qz
 
     def _ensure_hot(self, need: int) -> None:
@@ -212,6 +218,7 @@ class RFSNv10KVCacheMLX:
             new_k[:, :n] = self._hot_k
             new_v[:, :n] = self._hot_v
         self._hot_k, self._hot_v = new_k, new_v
+        self._store_epoch += 1
 
     def _ensure_warm(self, need: int) -> None:
         qz = self._qz
@@ -219,6 +226,7 @@ class RFSNv10KVCacheMLX:
             if self._warm is None:
                 self._warm_ring = _ceil_to(max(self.warm_capacity, 1), self.chunk_tokens) + self.chunk_tokens
                 self._warm = K.CodeStoreBuffers(qz, self.rows, self._warm_ring, device=self.device)
+                self._store_epoch += 1
             return
         if self._warm is not None and self._warm.cap >= need:
             return
@@ -228,6 +236,7 @@ class RFSNv10KVCacheMLX:
             self._warm = K.CodeStoreBuffers(qz, self.rows, cap, device=self.device)
         else:
             self._warm = self._warm.grow(qz, cap)
+        self._store_epoch += 1
 
     def _ensure_cold(self, disk_dir: Optional[Path]) -> ColdTier:
         root = Path(self.config.disk_cache_dir) if disk_dir is None else Path(disk_dir)
@@ -591,10 +600,23 @@ class RFSNv10KVCacheMLX:
         if out is None:
             out = torch.empty(qb.shape, dtype=torch.float16, device=qb.device)
         qpos = self._qpos(query_positions, start, end, qb) if causal else None
-        K.decode_attention(self._qz, qb, out, segs, kv_heads=self.heads, qpos=qpos, causal=qpos is not None,
-                           scale=self.head_dim ** -0.5,
-                           hot=(self._hot_k, self._hot_v) if self._hot_k is not None else None,
-                           warm=self._warm, cold=self._cold.pool if self._cold is not None else None)
+        ck = None
+        if key is not None:  # a cached plan: reuse its prepared call (same stores, shapes and masking)
+            ck = (key, qb.shape, qb.stride(0), qpos is not None, self._store_epoch)
+            entry = self._attn_calls.get(ck)
+            if entry is not None:
+                K.run_attention(entry, qb, out, qpos)
+                ck = None
+        if ck is not None or key is None:
+            entry = K.attention_call(self._qz, qb, out, segs, kv_heads=self.heads, qpos=qpos,
+                                     causal=qpos is not None, scale=self.head_dim ** -0.5,
+                                     hot=(self._hot_k, self._hot_v) if self._hot_k is not None else None,
+                                     warm=self._warm, cold=self._cold.pool if self._cold is not None else None)
+            K.run_attention(entry, qb, out, qpos)
+            if ck is not None:
+                if len(self._attn_calls) > 32:
+                    self._attn_calls.clear()
+                self._attn_calls[ck] = entry
         if squeeze:
             return out[0]
         return out.reshape(q.shape) if q.dim() == 3 else out

@@ -309,6 +309,29 @@ def decode_attention(qz: QuantizerBuffers, q: torch.Tensor, out: torch.Tensor, s
     hot: (k, v) fp16 [rows, cap, D]; warm/cold: code stores (K and V fields).
     segments: (store, slot, first, count, pos0) tuples in window order.
     """
+    entry = attention_call(qz, q, out, segments, kv_heads, qpos=qpos, causal=causal, scale=scale, hot=hot, warm=warm,
+                           cold=cold, num_ctas=num_ctas)
+    run_attention(entry, q, out, qpos if causal else None, device_status)
+    return out
+
+
+def run_attention(entry: "_AttnCall", q: torch.Tensor, out: torch.Tensor, qpos: Optional[torch.Tensor] = None,
+                  device_status: Optional[torch.Tensor] = None) -> None:
+    """Launch a prepared call (attention_call) with this step's q / out / qpos.  The caller
+    guarantees they have the shapes, strides and causal setting the call was prepared for."""
+    a = entry.args
+    a.q, a.out = q.data_ptr(), out.data_ptr()
+    a.qpos = qpos.data_ptr() if qpos is not None else None
+    a.device_status = _ptr(device_status)
+    call("rfsn_decode_attention", C.byref(a), C.byref(entry.qs), _stream(q.device.index))
+
+
+def attention_call(qz: QuantizerBuffers, q: torch.Tensor, out: torch.Tensor, segments: Sequence[Tuple],
+                   kv_heads: int, qpos: Optional[torch.Tensor] = None, causal: bool = True,
+                   scale: Optional[float] = None, hot: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
+                   warm: Optional[CodeStoreBuffers] = None, cold: Optional[CodeStoreBuffers] = None,
+                   num_ctas: int = 0) -> "_AttnCall":
+    """Validate the arguments and return the (memoised) prepared call for them."""
     _need_cuda(q, "q")
     if q.dtype != torch.float16 or q.dim() != 4 or not queries_packed(q):
         raise ValueError("q must be fp16 [B, Q, Hq, D], packed within a sequence (batch stride a multiple of 8)")
@@ -353,12 +376,7 @@ def decode_attention(qz: QuantizerBuffers, q: torch.Tensor, out: torch.Tensor, s
         if len(_ATTN_CALLS) >= 256:
             _ATTN_CALLS.clear()
         entry = _ATTN_CALLS[key] = _AttnCall(a, segs, qs, ws)
-    a = entry.args
-    a.q, a.out = q.data_ptr(), out.data_ptr()
-    a.qpos = qpos.data_ptr() if causal else None
-    a.device_status = _ptr(device_status)
-    call("rfsn_decode_attention", C.byref(a), C.byref(entry.qs), _stream(q.device.index))
-    return out
+    return entry
 
 
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
