@@ -106,6 +106,29 @@ __device__ __forceinline__ void quad_min(float& best, int& bi) {
   }
 }
 
+// Token v = (b, t, h) of the [batch, tokens, heads] vectors; nvec < 2^31 (checked at
+// launch), so 32-bit division suffices.
+__device__ __forceinline__ int64_t vec_offset(const EncTcParams& p, uint32_t v) {
+  const uint32_t heads = (uint32_t)p.heads, tokens = (uint32_t)p.tokens;
+  const uint32_t bt = v / heads, h = v - bt * heads;
+  const uint32_t b = bt / tokens, t = bt - b * tokens;
+  return (int64_t)b * p.sb + (int64_t)t * p.st + (int64_t)h * p.sh;
+}
+
+// The four 16-byte chunks lane `lane` holds of group gg's x tile: rows (lane >> 3) + 4 s,
+// chunk lane & 7; zero rows past the end.
+__device__ __forceinline__ void fetch_x(const EncTcParams& p, int64_t gg, int lane, uint4 out[4]) {
+  const bool isv = p.x_v != nullptr && gg >= p.ngk;
+  const int64_t g = isv ? gg - p.ngk : gg;
+  const uint16_t* xs = isv ? p.x_v : p.x;
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    const int64_t v = g * 16 + (lane >> 3) + 4 * s;
+    out[s] = make_uint4(0u, 0u, 0u, 0u);
+    if (v < p.nvec) out[s] = __ldg(reinterpret_cast<const uint4*>(xs + vec_offset(p, (uint32_t)v)) + (lane & 7));
+  }
+}
+
 template <int DS>
 __global__ void __launch_bounds__(kTcWarps * 32, 1) encode_tc_kernel(const __grid_constant__ EncTcParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -119,31 +142,56 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1) encode_tc_kernel(const __gri
   const int K = p.K, Kr = p.Kr;
 
   const int split = p.split;
-  const int gpc = kTcWarps / split;  // groups per CTA and round
+  const int gpc = (nthr >> 5) / split;  // groups per CTA and round
   const int gslot = warp / split, part = warp - gslot * split;
   const bool lead = part == 0;
 
+  const int64_t ngroups = p.x_v ? 2 * p.ngk : p.ngk;
   // ---- stage codebooks and their squared norms (sequential fp32 sums) ----
+  uint4 xpre[4];  // split mode: the leader's x rows, requested before the codebook staging
   if (split > 1) {
-    // Split mode: warp `part` of the first group stages PQ subspace `part` and sums its
-    // norms itself, while the leaders load their x tiles; the barrier before the search
-    // publishes every slice to every warp (the leader's residual step reads them after
-    // the barrier that follows the search).
+    // Split mode runs one round per CTA.  The leaders request their x rows first, so
+    // that load's latency overlaps the staging.  Warp `part` of the first group then
+    // stages PQ subspace `part` and sums its norms from the registers it loaded; the
+    // barrier before the search publishes every slice to every warp (the leader's
+    // residual step reads them after the barrier that follows the search).
+    const int64_t gg0 = (int64_t)blockIdx.x * gpc + gslot;
+    if (lead && gg0 < ngroups) fetch_x(p, gg0, lane, xpre);
     if (gslot == 0) {
+      // 16-byte chunks of the slice: one 8-dim or two 4-dim centroids each; K <= 256
+      // gives at most 8 per lane, all requested before the first is used
       const int n = K * DS / 8;
       const uint4* src = reinterpret_cast<const uint4*>(p.pq_cb) + (size_t)part * n;
       uint4* dst = reinterpret_cast<uint4*>(s_pq) + (size_t)part * n;
-      for (int i = lane; i < n; i += 32) dst[i] = __ldg(src + i);
-      __syncwarp();
-      for (int i = lane; i < K; i += 32) {
-        const uint16_t* c = s_pq + ((size_t)part * K + i) * DS;
-        float s = 0.f;
+      uint4 cl[8];
 #pragma unroll
-        for (int k = 0; k < DS; ++k) {
-          const float v = h2f(c[k]);
-          s = __fmaf_rn(v, v, s);
+      for (int j = 0; j < 8; ++j)
+        if (lane + 32 * j < n) cl[j] = __ldg(src + lane + 32 * j);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = lane + 32 * j;
+        if (i >= n) break;
+        const uint4 c = cl[j];
+        dst[i] = c;
+        const uint32_t w4[4] = {c.x, c.y, c.z, c.w};
+        float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[k]));
+          if (DS == 8 || k < 2) {
+            s0 = __fmaf_rn(f.x, f.x, s0);
+            s0 = __fmaf_rn(f.y, f.y, s0);
+          } else {
+            s1 = __fmaf_rn(f.x, f.x, s1);
+            s1 = __fmaf_rn(f.y, f.y, s1);
+          }
         }
-        s_pqcc[part * K + i] = s;
+        if (DS == 8) {
+          s_pqcc[part * K + i] = s0;
+        } else {
+          s_pqcc[part * K + 2 * i] = s0;
+          s_pqcc[part * K + 2 * i + 1] = s1;
+        }
       }
     }
     if (p.L > 0) {
@@ -219,7 +267,6 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1) encode_tc_kernel(const __gri
 
   const int r0 = lane >> 2, qd = lane & 3;
   const float INF = __int_as_float(0x7f800000);
-  const int64_t ngroups = p.x_v ? 2 * p.ngk : p.ngk;
 
   // the round count is the same for every warp of the CTA (split mode syncs the CTA)
   for (int64_t base = (int64_t)blockIdx.x * gpc; base < ngroups; base += (int64_t)gridDim.x * gpc) {
@@ -227,21 +274,18 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1) encode_tc_kernel(const __gri
     const bool live = gg < ngroups;
     const bool isv = p.x_v != nullptr && gg >= p.ngk;  // a V group of a K+V launch
     const int64_t g = isv ? gg - p.ngk : gg;           // group index within its tensor
-    const uint16_t* xs = isv ? p.x_v : p.x;
     const int kvf = isv ? 1 : p.kv;
     // ---- x tile (leader) ----
     if (live && lead) {
+      uint4 xr[4];
+      if (split > 1 && base == (int64_t)blockIdx.x * gpc) {
 #pragma unroll
-      for (int s = 0; s < 4; ++s) {
-        const int i = (lane >> 3) + 4 * s, q = lane & 7;
-        const int64_t v = g * 16 + i;
-        uint4 val = make_uint4(0u, 0u, 0u, 0u);
-        if (v < p.nvec) {
-          const int64_t h = v % p.heads, t = (v / p.heads) % p.tokens, b = v / (p.heads * p.tokens);
-          val = __ldg(reinterpret_cast<const uint4*>(xs + b * p.sb + t * p.st + h * p.sh) + q);
-        }
-        xt[swz(i, q)] = val;
+        for (int s = 0; s < 4; ++s) xr[s] = xpre[s];
+      } else {
+        fetch_x(p, gg, lane, xr);
       }
+#pragma unroll
+      for (int s = 0; s < 4; ++s) xt[swz((lane >> 3) + 4 * s, lane & 7)] = xr[s];
       __syncwarp();
       // |x_m|^2 per (vector, subspace), sequential fp32 (quantization.py:94)
       for (int idx = lane; idx < 16 * M; idx += 32) {
@@ -321,10 +365,8 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1) encode_tc_kernel(const __gri
         rv.z = hsub2_u32(xv.z, cv.z); rv.w = hsub2_u32(xv.w, cv.w);
         rt[swz(i, q)] = rv;
         const int64_t v = g * 16 + i;
-        if (p.residual_out && v < p.nvec) {
-          const int64_t h = v % p.heads, t = (v / p.heads) % p.tokens, b = v / (p.heads * p.tokens);
-          reinterpret_cast<uint4*>(p.residual_out + b * p.sb + t * p.st + h * p.sh)[q] = rv;
-        }
+        if (p.residual_out && v < p.nvec)
+          reinterpret_cast<uint4*>(p.residual_out + vec_offset(p, (uint32_t)v))[q] = rv;
       }
       __syncwarp();
 
@@ -393,8 +435,10 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1) encode_tc_kernel(const __gri
         const int i = lane;
         const int64_t v = g * 16 + i;
         if (v < p.nvec) {
-          const int64_t h = v % p.heads, t = (v / p.heads) % p.tokens, b = v / (p.heads * p.tokens);
-          const int64_t row = b * p.heads + h, tok = p.first + t;
+          const uint32_t heads = (uint32_t)p.heads, tokens = (uint32_t)p.tokens;
+          const uint32_t bt = (uint32_t)v / heads, h = (uint32_t)v - bt * heads;
+          const uint32_t b = bt / tokens, t = bt - b * tokens;
+          const int64_t row = (int64_t)b * heads + h, tok = p.first + t;
           const int fk = kvf * 5;
           uint8_t* f_pq = p.data + field_byte(p.lay, p.rows, p.cap, p.slot, row, tok, fk + 0);
           for (int m = 0; m < M; ++m) f_pq[m] = s_code[i * M + m];
@@ -499,6 +543,7 @@ int encode_tc_launch(const rfsn_quantizer* qz, const uint16_t* x, const uint16_t
   p.smem_warp = (int)off; off += (int64_t)kTcWarps * p.warp_bytes;
   if (off > 227 * 1024) return RFSN_ERR_UNSUPPORTED;
   if (p.nvec == 0) return RFSN_OK;
+  if (p.nvec >= (int64_t(1) << 31)) return RFSN_ERR_UNSUPPORTED;  // 32-bit vector indexing
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -509,19 +554,26 @@ int encode_tc_launch(const rfsn_quantizer* qz, const uint16_t* x, const uint16_t
   // alone would set the kernel's duration
   const int64_t split_ctas = (groups * p.M + kTcWarps - 1) / kTcWarps;
   p.split = (kTcWarps % p.M == 0 && split_ctas <= sms) ? p.M : 1;
-  const int64_t want = p.split > 1 ? split_ctas : (groups + kTcWarps - 1) / kTcWarps;
+  // split mode runs one group per CTA when that still fits one wave (the search of a
+  // subspace is ALU-bound: fewer warps per SM finish it sooner)
+  int warps = kTcWarps;
+  int64_t want = p.split > 1 ? split_ctas : (groups + kTcWarps - 1) / kTcWarps;
+  if (p.split > 1 && groups <= sms) {
+    warps = p.split;
+    want = groups;
+  }
   const int grid = (int)(want < sms ? want : sms);
   cudaError_t e;
   if (qz->subspace_dim == 8) {
     e = cudaFuncSetAttribute(encode_tc_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)off);
     if (e == cudaSuccess) {
-      encode_tc_kernel<8><<<grid, kTcWarps * 32, off, stream>>>(p);
+      encode_tc_kernel<8><<<grid, warps * 32, off, stream>>>(p);
       e = cudaGetLastError();
     }
   } else {
     e = cudaFuncSetAttribute(encode_tc_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)off);
     if (e == cudaSuccess) {
-      encode_tc_kernel<4><<<grid, kTcWarps * 32, off, stream>>>(p);
+      encode_tc_kernel<4><<<grid, warps * 32, off, stream>>>(p);
       e = cudaGetLastError();
     }
   }
