@@ -14,6 +14,7 @@ from pathlib import Path
 _PKG = Path(__file__).resolve().parent
 LIB_PATH = Path(os.environ.get("RFSN_B200_LIB", _PKG / "librfsn_b200.so"))
 
+RFSN_ERR_WORKSPACE_TOO_SMALL = -4  # rfsn_status in include/rfsn_b200.h
 RFSN_MAX_SEGMENTS = 256
 RFSN_MAX_ROWS_PER_KV = 8
 

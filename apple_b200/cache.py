@@ -84,7 +84,7 @@ class RFSNv10KVCacheMLX:
         self._warm_ring = 0
         self._cold: Optional[ColdTier] = None
         self._cold_root: Optional[Path] = None
-        self._plan_cache: Dict[Tuple, Tuple[List, Dict[str, int]]] = {}
+        self._plan_cache: Dict[Tuple, Tuple[List, Dict[str, int], Tuple]] = {}
         # prepared attention calls for cached plans; _store_epoch changes whenever a store
         # buffer or the quantizer is replaced, which retires the calls that point at them
         self._attn_calls: Dict[Tuple, Any] = {}
@@ -421,14 +421,15 @@ class RFSNv10KVCacheMLX:
             return int(current_position)
         return max(self.total_tokens - 1, 0)
 
-    def _window_bounds(self, query_positions, context_window, current_position):
-        """cache.py:210-241 -> (start, end, adjusted or None)."""
+    def _window_bounds(self, query_positions, context_window, current_position, adjusted: bool = True):
+        """cache.py:210-241 -> (start, end, adjusted or None); adjusted=False skips the third."""
         if self.total_tokens == 0:
             return 0, 0, None if query_positions is None else _host_ints(query_positions).astype(np.int32)
-        max_query = self._max_query_position(query_positions, current_position)
+        ints = _int_list(query_positions)
+        max_query = max(ints) if ints else self._max_query_position(query_positions, current_position)
         end = min(max_query + 1, self.total_tokens)
         start = 0 if context_window is None else max(0, end - context_window)
-        if query_positions is None:
+        if query_positions is None or not adjusted:
             return start, end, None
         adjusted = np.maximum(_host_ints(query_positions) - start, -1).astype(np.int32)
         return start, end, adjusted
@@ -548,6 +549,9 @@ class RFSNv10KVCacheMLX:
         B, Qn, Hq, _ = qb.shape
         if query_positions is None:
             return None
+        ints = _int_list(query_positions)
+        if ints and len(ints) == (Qn if self.batch == 1 else B) and min(ints) >= end - 1:
+            return None  # one position per query or sequence, each at the window's end
         pos = _host_ints(query_positions)
         pos = np.maximum(pos - start, -1) + start
         if self.batch == 1:
@@ -578,7 +582,7 @@ class RFSNv10KVCacheMLX:
         if self.quantizer is None:
             raise RuntimeError("Cache cannot run attention before update() provides a quantizer")
         qb, squeeze = self._queries(q)
-        start, end, _ = self._window_bounds(query_positions, context_window, current_position)
+        start, end, _ = self._window_bounds(query_positions, context_window, current_position, adjusted=False)
         # without a cold tier or router the plan depends only on the window and the tier
         # layout, so a decode loop that reads the same window reuses it
         key = None
@@ -587,36 +591,41 @@ class RFSNv10KVCacheMLX:
                    self._warm_start)
         cached = self._plan_cache.get(key) if key is not None else None
         if cached is not None:
-            segs, stats = cached[0], dict(cached[1])
+            segs, stats, shape = cached[0], dict(cached[1]), cached[2]
         else:
             stats = self._begin_stats(start, end, context_window, router)
             segs = self._plan(start, end, router, current_position, context_window, stats)
+            shape = tuple((sg[0], sg[1]) for sg in segs)  # the stores and slots, in order
             if key is not None:
                 if len(self._plan_cache) > 32:
                     self._plan_cache.clear()
-                self._plan_cache[key] = (segs, dict(stats))
+                self._plan_cache[key] = (segs, dict(stats), shape)
         stats["query_tokens"] = int(q.shape[0])
         self.last_access_stats = stats
         if out is None:
             out = torch.empty(qb.shape, dtype=torch.float16, device=qb.device)
         qpos = self._qpos(query_positions, start, end, qb) if causal else None
-        ck = None
-        if key is not None:  # a cached plan: reuse its prepared call (same stores, shapes and masking)
-            ck = (key, qb.shape, qb.stride(0), qpos is not None, self._store_epoch)
+        # without a cold tier or router, a prepared call is reused across steps: its key is
+        # the segments' stores and slots plus the shapes and buffers, and each step patches
+        # the token ranges (a decode loop's window grows or slides by one token per step)
+        ck = entry = None
+        if key is not None:
+            ck = (shape, qb.shape, qb.stride(0), qpos is not None,
+                  self._store_epoch, self._cold is not None)
             entry = self._attn_calls.get(ck)
             if entry is not None:
-                K.run_attention(entry, qb, out, qpos)
-                ck = None
-        if ck is not None or key is None:
+                K.patch_segments(entry, segs)
+        if entry is None:
             entry = K.attention_call(self._qz, qb, out, segs, kv_heads=self.heads, qpos=qpos,
                                      causal=qpos is not None, scale=self.head_dim ** -0.5,
                                      hot=(self._hot_k, self._hot_v) if self._hot_k is not None else None,
-                                     warm=self._warm, cold=self._cold.pool if self._cold is not None else None)
-            K.run_attention(entry, qb, out, qpos)
+                                     warm=self._warm, cold=self._cold.pool if self._cold is not None else None,
+                                     memo=ck is None)
             if ck is not None:
                 if len(self._attn_calls) > 32:
                     self._attn_calls.clear()
                 self._attn_calls[ck] = entry
+        K.run_attention(entry, qb, out, qpos)
         if squeeze:
             return out[0]
         return out.reshape(q.shape) if q.dim() == 3 else out
@@ -658,6 +667,13 @@ class RFSNv10KVCacheMLX:
     def close(self) -> None:
         if self._cold_root is not None:
             unregister_cold_tier(self._cold_root, self.layer_idx)
+
+
+def _int_list(values):
+    """values itself when it is a flat list or tuple of Python ints, else None."""
+    if type(values) in (list, tuple) and all(type(v) is int for v in values):
+        return values
+    return None
 
 
 def _host_ints(values) -> np.ndarray:

@@ -273,10 +273,11 @@ class _AttnCall:
     decode loop calls with the same stores, window and shapes step after step,
     so only the tensor pointers are rewritten."""
 
-    __slots__ = ("args", "segs", "qs", "ws")
+    __slots__ = ("args", "segs", "qs", "ws", "src")
 
     def __init__(self, args, segs, qs, ws):
         self.args, self.segs, self.qs, self.ws = args, segs, qs, ws
+        self.src = None  # the segment list last written into segs (patch_segments)
 
 
 _ATTN_CALLS: "dict" = {}
@@ -318,20 +319,55 @@ def decode_attention(qz: QuantizerBuffers, q: torch.Tensor, out: torch.Tensor, s
 def run_attention(entry: "_AttnCall", q: torch.Tensor, out: torch.Tensor, qpos: Optional[torch.Tensor] = None,
                   device_status: Optional[torch.Tensor] = None) -> None:
     """Launch a prepared call (attention_call) with this step's q / out / qpos.  The caller
-    guarantees they have the shapes, strides and causal setting the call was prepared for."""
+    guarantees they have the shapes, strides and causal setting the call was prepared for.
+    A call whose segments were patched (patch_segments) may need more split-K workspace
+    than it was prepared with: the library then refuses the launch, and it is sized again."""
     a = entry.args
     a.q, a.out = q.data_ptr(), out.data_ptr()
     a.qpos = qpos.data_ptr() if qpos is not None else None
     a.device_status = _ptr(device_status)
-    call("rfsn_decode_attention", C.byref(a), C.byref(entry.qs), _stream(q.device.index))
+    stream = _stream(q.device.index)
+    status = lib().rfsn_decode_attention(C.byref(a), C.byref(entry.qs), stream)
+    if status == _lib.RFSN_ERR_WORKSPACE_TOO_SMALL:
+        _size_workspace(entry, q.device)
+        status = lib().rfsn_decode_attention(C.byref(a), C.byref(entry.qs), stream)
+    _lib.check("rfsn_decode_attention", status)
+
+
+def _size_workspace(entry: "_AttnCall", device: torch.device) -> None:
+    a = entry.args
+    nbytes = C.c_size_t(0)
+    call("rfsn_attention_workspace_size", C.byref(a), C.byref(entry.qs), C.byref(nbytes))
+    ws = workspace(nbytes.value, device)
+    a.workspace, a.workspace_bytes = _ptr(ws), ws.numel()
+    entry.ws = ws
+
+
+def patch_segments(entry: "_AttnCall", segments: Sequence[Tuple]) -> None:
+    """Point a prepared call (attention_call with memo=False) at new token ranges: the
+    segments keep their count, stores and slots, and take new first / count / pos0.  A
+    decode loop over a growing or sliding window patches its call each step instead of
+    preparing a new one.  Passing the same list object as the last patch is a no-op."""
+    if segments is entry.src:
+        return
+    segs = entry.segs
+    if len(segments) != entry.args.num_segments:
+        raise ValueError("patch_segments keeps the number of segments")
+    for i, (st, slot, first, count, pos0) in enumerate(segments):
+        sg = segs[i]
+        if sg.store != st or sg.slot != slot:
+            raise ValueError("patch_segments keeps each segment's store and slot")
+        sg.first, sg.count, sg.pos0 = first, count, pos0
+    entry.src = segments
 
 
 def attention_call(qz: QuantizerBuffers, q: torch.Tensor, out: torch.Tensor, segments: Sequence[Tuple],
                    kv_heads: int, qpos: Optional[torch.Tensor] = None, causal: bool = True,
                    scale: Optional[float] = None, hot: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
                    warm: Optional[CodeStoreBuffers] = None, cold: Optional[CodeStoreBuffers] = None,
-                   num_ctas: int = 0) -> "_AttnCall":
-    """Validate the arguments and return the (memoised) prepared call for them."""
+                   num_ctas: int = 0, memo: bool = True) -> "_AttnCall":
+    """Validate the arguments and return the prepared call for them: memoised by its exact
+    arguments, or (memo=False) a private one that the caller may patch_segments."""
     _need_cuda(q, "q")
     if q.dtype != torch.float16 or q.dim() != 4 or not queries_packed(q):
         raise ValueError("q must be fp16 [B, Q, Hq, D], packed within a sequence (batch stride a multiple of 8)")
@@ -347,7 +383,7 @@ def attention_call(qz: QuantizerBuffers, q: torch.Tensor, out: torch.Tensor, seg
     hot_key = None if hot is None else (_ptr(hot[0]), _ptr(hot[1]), hot[0].shape[1], hot[0].shape[0])
     key = (q.device.index, B, Qn, Hq, D, kv_heads, bool(causal), scale, num_ctas, tuple(map(tuple, segments)),
            hot_key, _store_key(warm), _store_key(cold), _qz_key(qz), q.stride(0) if B > 1 else 0)
-    entry = _ATTN_CALLS.get(key)
+    entry = _ATTN_CALLS.get(key) if memo else None
     if entry is None:
         a = AttnArgs()
         a.batch, a.queries, a.q_heads, a.kv_heads = B, Qn, Hq, kv_heads
@@ -369,13 +405,12 @@ def attention_call(qz: QuantizerBuffers, q: torch.Tensor, out: torch.Tensor, seg
         a.q_batch_stride = q.stride(0) if B > 1 else 0  # one sequence: no stride to follow
         qs = qz.struct()
         a.q, a.out, a.qpos = _ptr(q), _ptr(out), _ptr(qpos) if causal else None
-        nbytes = C.c_size_t(0)
-        call("rfsn_attention_workspace_size", C.byref(a), C.byref(qs), C.byref(nbytes))
-        ws = workspace(nbytes.value, q.device)
-        a.workspace, a.workspace_bytes = _ptr(ws), ws.numel()
-        if len(_ATTN_CALLS) >= 256:
-            _ATTN_CALLS.clear()
-        entry = _ATTN_CALLS[key] = _AttnCall(a, segs, qs, ws)
+        entry = _AttnCall(a, segs, qs, None)
+        _size_workspace(entry, q.device)
+        if memo:
+            if len(_ATTN_CALLS) >= 256:
+                _ATTN_CALLS.clear()
+            _ATTN_CALLS[key] = entry
     return entry
 
 

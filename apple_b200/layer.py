@@ -27,6 +27,11 @@ from .storage import AsyncHierarchicalRouterMLX, RFSNConfig
 logger = logging.getLogger("RFSN_MLX_APPLE")
 
 
+def _as(t: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """t in dtype (t itself when it already is: a decode step makes many such calls)."""
+    return t if t.dtype == dtype else t.to(dtype)
+
+
 class _Linear:
     """y = x @ W^T (no bias); W ~ U(-1/sqrt(in), 1/sqrt(in)) like mlx.nn.Linear, or N(0, 1/in).
     The product runs in the activations' dtype, as mlx.nn.Linear casts W to x's dtype."""
@@ -44,7 +49,7 @@ class _Linear:
         # like mlx.nn.Linear: the weight is cast to the activations' dtype (fp16 in the layer)
         if self._cast is None or self._cast.dtype != x.dtype or self._src is not self.weight:
             self._cast, self._src = self.weight.to(x.dtype), self.weight
-        return torch.matmul(x, self._cast.t())
+        return torch.nn.functional.linear(x, self._cast)
 
 
 class _RMSNorm:
@@ -76,6 +81,7 @@ class RFSNDecoderLayerMLX:
         self.ffn_hidden_dim = max(config.hidden_dim * ffn_multiplier, config.hidden_dim)
         self.scale = config.head_dim ** -0.5
         dev = torch.device(config.device)
+        self._device = dev
         g = torch.Generator().manual_seed(seed + 1000 * layer_idx)
         mk = lambda i, o: _Linear(i, o, dev, weight_dtype, g, init)  # noqa: E731
         self.attn_norm = _RMSNorm(config.hidden_dim, dev)
@@ -111,14 +117,14 @@ class RFSNDecoderLayerMLX:
                 or any(x is not y for x, y in zip(self._qkv_src, ws))):
             self._qkv_w = torch.cat([w.to(a.dtype) for w in ws], 0)
             self._qkv_src = ws
-        y = torch.matmul(a, self._qkv_w.t())
+        y = torch.nn.functional.linear(a, self._qkv_w)
         nq = self.num_heads * self.head_dim
         nk = self.num_kv_heads * self.head_dim
         return y[..., :nq], y[..., nq:nq + nk], y[..., nq + nk:]
 
     def _project_heads(self, projected: torch.Tensor, heads: int) -> torch.Tensor:
         b, s, _ = projected.shape
-        return projected.reshape(b, s, heads, self.head_dim).to(torch.float16)
+        return _as(projected.reshape(b, s, heads, self.head_dim), torch.float16)
 
     def prefill_cache(self, x: torch.Tensor, reset: bool = True) -> None:
         """rfsn_v10_mlx_ane_complete.py:90-104 ([B, S, hidden] with B = config.batch_size)."""
@@ -143,9 +149,9 @@ class RFSNDecoderLayerMLX:
             raise ValueError("Decoder layer expects input shape [batch, seq_len, hidden_dim]")
         if int(x.shape[-1]) != self.model_dim:
             raise ValueError(f"Expected hidden_dim {self.model_dim}, got {int(x.shape[-1])}")
-        x = x.to(device=torch.device(self.config.device))
-        residual = x.to(torch.float16)
-        attn_input = self.attn_norm(residual).to(torch.float16)
+        x = x.to(device=self._device)
+        residual = _as(x, torch.float16)
+        attn_input = _as(self.attn_norm(residual), torch.float16)
         q_p, k_p, v_p = self._qkv(attn_input)
         q_heads = self._project_heads(q_p, self.num_heads)
         k_heads = self._project_heads(k_p, self.num_kv_heads)
@@ -169,7 +175,7 @@ class RFSNDecoderLayerMLX:
             attended = attended.reshape(B, 1, self.num_heads, self.head_dim)
         else:
             attended = _dense_exact_attention(q_heads, k_heads, v_heads, self.scale, causal=True)
-        attn_out = self.o_proj(attended.reshape(B, -1, self.num_heads * self.head_dim)).to(residual.dtype)
+        attn_out = _as(self.o_proj(attended.reshape(B, -1, self.num_heads * self.head_dim)), residual.dtype)
         if residual.is_cuda and residual.dtype == torch.float16 and attn_out.dtype == torch.float16:
             # residual add and FFN RMSNorm in one launch (same roundings)
             hidden, ffn_input = K.add_rms_norm(residual, attn_out, self.ffn_norm.weight, self.ffn_norm.eps)
@@ -178,7 +184,7 @@ class RFSNDecoderLayerMLX:
             ffn_input = self.ffn_norm(hidden).to(torch.float16)
         up = self.ffn_up(ffn_input)
         act = K.gelu_tanh(up) if up.dtype == torch.float16 else _gelu(up)  # one launch for the fp16 chain
-        ffn_out = self.ffn_down(act).to(hidden.dtype)
+        ffn_out = _as(self.ffn_down(act), hidden.dtype)
         return hidden + ffn_out
 
 
