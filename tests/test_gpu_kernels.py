@@ -450,6 +450,52 @@ def test_fused_attention_strided_queries(Qn):
         K.decode_attention(qz, odd, out_v, segs, kv_heads=Hkv, causal=False, hot=(hot_k, hot_v), warm=ws)
 
 
+def test_patched_call_matches_fresh_call():
+    """A prepared call (attention_call with memo=False) whose segments are patched step by
+    step, as a decode loop over a growing window does, gives bit-identical outputs to a
+    call prepared afresh for each window; a workspace the library finds too small is sized
+    again and the launch retried (the library refuses such a launch before it starts)."""
+    rng = np.random.default_rng(23)
+    B, Hkv, G, D, T_hot, T_warm = 3, 2, 4, 64, 48, 1600
+    pq_cb, rvq_cb, k, v = _make_cfg2_like(rng, B, Hkv, G, D, T_hot, T_warm, S=8, ds=4, L=1, thr=-1.0)
+    oq = R.Quantizer(pq_cb, rvq_cb, -1.0, sparse_topk=8)
+    qz = K.QuantizerBuffers(to_dev(pq_cb), to_dev(rvq_cb), -1.0, 8)
+    kc = [oq.compress(k[b, :T_warm]) for b in range(B)]
+    vc = [oq.compress(v[b, :T_warm]) for b in range(B)]
+
+    def rows(cs):
+        return [R.Codes(c.pq[:, h], c.rvq[:, h], c.mask[:, h], c.sp_idx[:, h], c.sp_val[:, h])
+                for c in cs for h in range(Hkv)]
+
+    ws = kv_to_store(qz, rows(kc), rows(vc), cap=T_warm)
+    hot_k = to_dev(np.ascontiguousarray(k[:, T_warm:].transpose(0, 2, 1, 3).reshape(B * Hkv, T_hot, D)))
+    hot_v = to_dev(np.ascontiguousarray(v[:, T_warm:].transpose(0, 2, 1, 3).reshape(B * Hkv, T_hot, D)))
+    q = to_dev(rng.standard_normal((B, 1, Hkv * G, D)).astype(np.float16))
+    kw = dict(kv_heads=Hkv, causal=False, hot=(hot_k, hot_v), warm=ws)
+
+    def segs(n):  # the newest n warm tokens, then the hot tokens
+        return [(K.STORE_WARM, 0, T_warm - n, n, T_warm - n), (K.STORE_HOT, 0, 0, T_hot, T_warm)]
+
+    out_p = torch.empty_like(q)
+    out_f = torch.empty_like(q)
+    entry = K.attention_call(qz, q, out_p, segs(16), memo=False, **kw)
+    for step, n in enumerate([16, 17, 200, 1599, 1600, 40]):
+        s = segs(n)
+        K.patch_segments(entry, s)
+        if step == 3:
+            entry.args.workspace_bytes = 16  # refused by the library, then sized again
+        K.run_attention(entry, q, out_p)
+        K.decode_attention(qz, q, out_f, s, **kw)
+        torch.cuda.synchronize()
+        assert torch.equal(out_p, out_f), f"window of {n} warm tokens"
+    import ctypes as C
+    need = C.c_size_t(0)
+    K.call("rfsn_attention_workspace_size", C.byref(entry.args), C.byref(entry.qs), C.byref(need))
+    assert entry.args.workspace_bytes >= need.value
+    with pytest.raises(ValueError):
+        K.patch_segments(entry, segs(8)[:1])  # the segment count is part of the prepared call
+
+
 @pytest.mark.parametrize("rows,dim,offset", [(32, 2048, 0), (3, 1000, 0)])
 def test_fused_add_rmsnorm(rows, dim, offset):
     """rfsn_add_rmsnorm_f16: the sum is the fp16 tensor add bit for bit, and the normalised
