@@ -671,7 +671,7 @@ class RFSNv10KVCacheMLX:
 
 def _int_list(values):
     """values itself when it is a flat list or tuple of Python ints, else None."""
-    if type(values) in (list, tuple) and all(type(v) is int for v in values):
+    if type(values) in (list, tuple) and set(map(type, values)) <= {int}:
         return values
     return None
 

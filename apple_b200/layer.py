@@ -113,8 +113,9 @@ class RFSNDecoderLayerMLX:
         """q, k and v projections of the same input as one GEMM over the concatenated weights
         (rebuilt when a projection's weight is replaced); returns views of the one product."""
         ws = (self.q_proj.weight, self.k_proj.weight, self.v_proj.weight)
-        if (self._qkv_w is None or self._qkv_w.dtype != a.dtype or len(self._qkv_src) != 3
-                or any(x is not y for x, y in zip(self._qkv_src, ws))):
+        src = self._qkv_src
+        if (self._qkv_w is None or self._qkv_w.dtype != a.dtype or len(src) != 3
+                or src[0] is not ws[0] or src[1] is not ws[1] or src[2] is not ws[2]):
             self._qkv_w = torch.cat([w.to(a.dtype) for w in ws], 0)
             self._qkv_src = ws
         y = torch.nn.functional.linear(a, self._qkv_w)
