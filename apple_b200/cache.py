@@ -530,10 +530,15 @@ class RFSNv10KVCacheMLX:
     def _queries(self, q: torch.Tensor) -> Tuple[torch.Tensor, bool]:
         # a pinned host query is uploaded asynchronously on the current stream (ordered
         # before the attention kernel); keep it unchanged until the call's result is read
-        q = q.to(device=self.device, dtype=torch.float16, non_blocking=bool(not q.is_cuda and q.is_pinned()))
+        uploaded = not q.is_cuda
+        q = q.to(device=self.device, dtype=torch.float16, non_blocking=bool(uploaded and q.is_pinned()))
         # a view whose sequences are each packed (e.g. the query heads of a wider projection
-        # output) is read in place through the kernel's batch stride
-        pack = lambda t: t if K.queries_packed(t) else t.contiguous()  # noqa: E731
+        # output) is read in place through the kernel's batch stride; a contiguous upload is a
+        # fresh allocation, packed and aligned by construction
+        if uploaded and q.is_contiguous():
+            pack = lambda t: t  # noqa: E731
+        else:
+            pack = lambda t: t if K.queries_packed(t) else t.contiguous()  # noqa: E731
         if self.batch == 1 and q.dim() == 3:
             return pack(q.unsqueeze(0)), True                 # [1, Q, Hq, D]
         if q.dim() == 3 and q.shape[0] == self.batch:
