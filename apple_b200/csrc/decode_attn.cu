@@ -14,8 +14,13 @@
 // (max, sum, unnormalised output) per row piece it touches and then takes a
 // ticket for the row; the CTA that completes a row's last piece combines the
 // row's partials by log-sum-exp and writes fp16 (no separate merge launch).
-// Tickets carry the launch's call number in their upper 48 bits, so counts
-// left by earlier or aborted launches are never taken for this launch's.
+// Tickets carry a launch tag in their upper 48 bits, so counts left by
+// earlier or aborted launches are never taken for this launch's.  The tag is a
+// launch counter kept at the start of the workspace: every CTA counts itself
+// done on a second counter, and the last one resets that and advances the
+// launch counter.  Replays of
+// one captured launch (same kernel parameters) therefore get a fresh tag each
+// time, and so does every launch of any shape that shares the workspace.
 //
 // Inside a CTA.  Warp NW (the producer) walks the CTA's tiles and issues 1-D
 // bulk TMA copies (cp.async.bulk): a code tile is a run of whole 16-token
@@ -33,8 +38,6 @@
 #include <cuda_runtime.h>
 #include <math.h>
 
-#include <atomic>
-#include <chrono>
 #include <mutex>
 
 #include "rfsn_api_internal.h"
@@ -81,8 +84,8 @@ struct AttnParams {
   uint16_t* out;
   float* ws_o;
   float* ws_ml;
-  unsigned long long* tickets;  // one per row: (call number << 16) | pieces done
-  unsigned long long epoch;     // this launch's call number (< 2^48)
+  unsigned long long* tickets;  // one per row: (launch tag << 16) | pieces done
+  unsigned long long* gen;      // [0] launch counter, [1] CTAs of this launch done (0 between launches)
   int32_t* dev_status;
   int B, Q, Hq, Hkv, D, G, R, causal;
   float scale;
@@ -133,16 +136,19 @@ __device__ __forceinline__ int row_pieces(const AttnParams& p, int64_t row, int6
   return (int)(c1 - c0 + 1);
 }
 
-// Count this CTA's piece of `row` done; returns 1 if it was the row's last
-// piece of this launch, 0 if not, -1 if the ticket could not be taken.  A
-// ticket holding another launch's call number counts as zero.
-__device__ __forceinline__ int take_row_ticket(const AttnParams& p, int64_t row, int pieces) {
-  unsigned long long* t = p.tickets + row;
+constexpr unsigned long long kTagMask = (1ull << 48) - 1ull;
+
+// Count one arrival on ticket *t for the launch tagged `tag`; returns 1 if it
+// was arrival number `target` of this launch, 0 if not, -1 if the ticket could
+// not be taken.  A ticket holding another launch's tag counts as zero.  Each
+// failed swap means another CTA's succeeded, and at most 0xffff CTAs arrive on
+// one ticket, so the loop bound is never reached in a healthy launch.
+__device__ __forceinline__ int take_ticket(unsigned long long* t, unsigned long long tag, int target) {
   unsigned long long cur = *reinterpret_cast<volatile unsigned long long*>(t);
-  for (int it = 0; it < 4096; ++it) {  // each failed swap means another CTA's succeeded
-    const unsigned long long nxt = ((cur >> 16) == p.epoch) ? cur + 1ull : ((p.epoch << 16) | 1ull);
+  for (int it = 0; it < 0x10000 + 16; ++it) {
+    const unsigned long long nxt = ((cur >> 16) == tag) ? cur + 1ull : ((tag << 16) | 1ull);
     const unsigned long long prev = atomicCAS(t, cur, nxt);
-    if (prev == cur) return (int)(nxt & 0xffffull) == pieces ? 1 : 0;
+    if (prev == cur) return (int)(nxt & 0xffffull) == target ? 1 : 0;
     cur = prev;
   }
   return -1;
@@ -245,6 +251,12 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
     }
     named_bar_sync(1, nthr);  // consumers only
   }
+
+  // launch tag, read by the one thread that takes this CTA's tickets before any
+  // CTA of the launch can advance the generation (that happens only after every
+  // CTA has taken its done ticket, below)
+  unsigned long long tag = 0;
+  if (threadIdx.x == 0) tag = *reinterpret_cast<volatile unsigned long long*>(p.gen) & kTagMask;
 
   const int64_t total = p.rows * p.W;
   const int64_t cta_a = (int64_t)blockIdx.x * p.per_cta;
@@ -547,7 +559,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
       volatile int* merge_flag = abort + 1;
       if (warp == 0 && lane == 0) {
         int64_t c0;
-        const int t = take_row_ticket(p, row, row_pieces(p, row, &c0));
+        const int t = take_ticket(p.tickets + row, tag, row_pieces(p, row, &c0));
         if (t < 0) set_status(p, abort, kDevStatusTicket);
         *merge_flag = t > 0;
       }
@@ -563,6 +575,18 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
     if (++stage == p.stages) {
       stage = 0;
       phase ^= 1u;
+    }
+  }
+  // Every CTA (also one that gave up on a timed-out wait) counts itself done; the
+  // last one advances the launch counter, so the next launch on this workspace --
+  // a graph replay with the same parameters included -- gets a new tag.
+  // The done count is a plain counter that is zero between launches (the last CTA
+  // resets it): one atomicAdd per CTA, where compare-and-swap tickets retried by
+  // 148 CTAs finishing together serialise on round trips.
+  if (threadIdx.x == 0) {
+    if (atomicAdd(p.gen + 1, 1ull) == (unsigned long long)gridDim.x - 1ull) {
+      atomicExch(p.gen + 1, 0ull);
+      atomicAdd(p.gen, 1ull);
     }
   }
 }
@@ -758,32 +782,28 @@ static int make_plan(const rfsn_attn_args* a, const rfsn_quantizer* qz, Plan& pl
     pl.grid = 0;
     p.max_pieces = 1;
   }
-  if (p.max_pieces > 0xffff) return RFSN_ERR_UNSUPPORTED;  // tickets count pieces in 16 bits
+  if (p.max_pieces > 0xffff || pl.grid > 0xffff) return RFSN_ERR_UNSUPPORTED;  // tickets count in 16 bits
   pl.ws_bytes = workspace_layout(p, nullptr);
   return RFSN_OK;
 }
 
-// Workspace: per (row, piece, query row) partial (max, sum) pairs, then the
-// unnormalised outputs, then one 8-byte ticket per row.  Returns the bytes
-// needed; with a base pointer, binds the regions into the parameters.
+// Workspace: a control region first -- the launch counter, the CTA done
+// ticket and one 8-byte ticket per row, at the same offsets whatever the call's
+// shape, so every launch that uses this workspace advances the one counter --
+// then per (row, piece, query row) partial (max, sum) pairs and the
+// unnormalised outputs.  Returns the bytes needed; with a base pointer, binds
+// the regions into the parameters.
 static size_t workspace_layout(AttnParams& p, void* base) {
+  const int64_t ctl = align_up(16 + (int64_t)p.rows * 8, 256);
   const int64_t n_ml = align_up((int64_t)p.rows * p.max_pieces * p.R * 2, 64);
   const int64_t n_o = align_up((int64_t)p.rows * p.max_pieces * p.R * p.D, 64);
   if (base) {
-    p.ws_ml = reinterpret_cast<float*>(base);
+    p.gen = reinterpret_cast<unsigned long long*>(base);
+    p.tickets = p.gen + 2;
+    p.ws_ml = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(base) + ctl);
     p.ws_o = p.ws_ml + n_ml;
-    p.tickets = reinterpret_cast<unsigned long long*>(p.ws_o + n_o);
   }
-  return (size_t)(n_ml + n_o) * sizeof(float) + (size_t)p.rows * 8 + 256;
-}
-
-// Call numbers tag row tickets (48 bits); the start is taken from the clock so
-// that stale ticket values from another process's use of the same memory are
-// not mistaken for a current launch's.
-static unsigned long long next_epoch() {
-  static std::atomic<unsigned long long> counter{
-      ((unsigned long long)std::chrono::steady_clock::now().time_since_epoch().count() & ((1ull << 40) - 1)) + 1};
-  return counter.fetch_add(1) & ((1ull << 48) - 1);
+  return (size_t)ctl + (size_t)(n_ml + n_o) * sizeof(float);
 }
 
 template <int D, int RMAX, int NW, int LP>
@@ -855,7 +875,6 @@ extern "C" int rfsn_decode_attention(const rfsn_attn_args* args, const rfsn_quan
   if (reinterpret_cast<uintptr_t>(args->workspace) & 15) return RFSN_ERR_ALIGNMENT;
   workspace_layout(pl.p, args->workspace);
   pl.p.out = args->out;
-  pl.p.epoch = next_epoch();
   return check_cuda(launch(pl, s));
 }
 
@@ -873,9 +892,11 @@ extern "C" int rfsn_decode_attention(const rfsn_attn_args* args, const rfsn_quan
 // cached; that first call may load the module, so make it before capturing
 // the stream into a graph.  Nothing here calls an allocator.  Every partial
 // the merge reads is written by the attention kernel of the same call, and the
-// per-row completion tickets carry each launch's own call number, so values
-// left by earlier (or aborted) calls are never counted: the buffer needs no
-// clearing.  Calls that overlap in time on one device
+// per-row completion tickets carry each launch's own tag (a launch counter in
+// the buffer that every launch advances; the buffer starts zeroed like every
+// __device__ array), so values left by earlier (or aborted) calls are never
+// counted: the buffer needs no clearing between calls.  Calls that
+// overlap in time on one device
 // (different streams, or threads without ordering) share the buffer and race;
 // calls on one stream are ordered and safe.
 // ---------------------------------------------------------------------------
@@ -927,6 +948,5 @@ extern "C" int rfsn_decode_attention_noalloc(const rfsn_attn_args* args, const r
   if (st != RFSN_OK) return st;
   workspace_layout(pl.p, scratch);
   pl.p.out = args->out;
-  pl.p.epoch = next_epoch();
   return check_cuda(launch(pl, s));
 }

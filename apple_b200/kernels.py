@@ -259,11 +259,12 @@ _WORKSPACE: dict = {}
 
 
 def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
-    """Per-device scratch buffer for the split-K partials (grown on demand)."""
+    """Per-device scratch buffer for the split-K partials (grown on demand).  It starts
+    zeroed: its leading launch counter and row tickets are then kept by the library."""
     key = (device.type, device.index)
     buf = _WORKSPACE.get(key)
     if buf is None or buf.numel() < nbytes:
-        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
         _WORKSPACE[key] = buf
     return buf
 

@@ -36,6 +36,7 @@ import math
 import os
 import statistics
 import sys
+import tempfile
 import time
 from pathlib import Path
 
@@ -49,6 +50,19 @@ UNIT = "steps/s"
 DTYPE = "f16 operands, f32 accumulate"
 CFG = dict(batch=8, q_heads=32, kv_heads=8, head_dim=64, context=32768, hot=1024, M=16, ds=4, K=256, L=1, Kr=256,
            sparse=8, outliers=4, seed=1)
+
+
+_SCRATCH = None
+
+
+def scratch_dir(name: str) -> Path:
+    """A private temporary directory of this run (clock samples, cold-tier directories)."""
+    global _SCRATCH
+    if _SCRATCH is None:
+        _SCRATCH = Path(tempfile.mkdtemp(prefix="rfsn_bench_"))
+    p = _SCRATCH / name
+    p.mkdir(parents=True, exist_ok=True)
+    return p
 
 
 def workload_desc(n_gpus: int) -> dict:
@@ -141,7 +155,7 @@ class ClockSampler:
         self.active = active
         self.devices = devices  # sample cuda:0 .. cuda:devices-1 (one rank per local GPU)
         self.proc = None
-        self.path = ROOT / "gpurun_out" / f"clocks_{os.getpid()}.json"
+        self.path = scratch_dir("clocks") / f"clocks_{os.getpid()}.json"
         self.error = None
 
     def _ident(self) -> str:
@@ -163,7 +177,6 @@ class ClockSampler:
             self.error = "clock sampling disabled (RFSN_CLOCK_PERIOD_MS <= 0)"
             return self
         try:
-            self.path.parent.mkdir(exist_ok=True)
             self.proc = subprocess.Popen([sys.executable, str(Path(__file__).resolve()), "--clock-sampler",
                                           self._ident(), str(self.path)], stdout=subprocess.PIPE, text=True,
                                          env=dict(os.environ))
@@ -374,7 +387,7 @@ def public_api_cache(w, dev):
                      num_subspaces=c["M"], subspace_dim=c["ds"], num_rvq_layers=c["L"], rvq_codebook_size=c["Kr"],
                      rvq_sparsity_threshold=-1.0, hot_capacity=c["hot"], warm_capacity=c["context"] - c["hot"],
                      block_size_seq=128, num_kv_heads=c["kv_heads"], batch_size=c["batch"], hot_policy="recent",
-                     sparse_topk=c["sparse"], device=str(dev), disk_cache_dir=str(ROOT / "gpurun_out" / "bench_cold"))
+                     sparse_topk=c["sparse"], device=str(dev), disk_cache_dir=str(scratch_dir("bench_cold")))
     qz = HybridQuantizerMLX(cfg)
     qz.pq.codebooks = w["qz"].pq_codebooks
     qz.rvq.codebooks = w["qz"].rvq_codebooks
@@ -436,6 +449,22 @@ def e2e_public_api(w, args, dev, world: int = 1, rank: int = 0, shards=None) -> 
             "d2h_bytes_per_step": nb * (world if world > 1 else 1),
             "api": "RFSNv10KVCacheMLX.attention_forward" + (" + NCCL all-gather of outputs" if world > 1 else ""),
             "max_abs_diff_vs_kernel_call": err}
+
+
+def replay_check(w, graph, out, eager_call) -> dict:
+    """A replay of the captured step computes on the inputs it finds: new queries written
+    into the captured query buffer, the output filled with NaN, one replay, compared with
+    an eager call on the same queries (max |diff| and whether every output was written)."""
+    import torch
+    g = torch.Generator(device=w["q"].device).manual_seed(12345)
+    w["q"].copy_(torch.randn(w["q"].shape, generator=g, device=w["q"].device).half())
+    out.fill_(float("nan"))
+    graph.replay()
+    ref = torch.empty_like(out)
+    eager_call(ref)
+    torch.cuda.synchronize()
+    return {"max_abs_diff_replay_vs_eager": float((out.float() - ref.float()).abs().max()),
+            "all_written": bool(torch.isfinite(out).all())}
 
 
 def run_b200(args) -> None:
@@ -513,6 +542,9 @@ def run_b200(args) -> None:
     e3.record(stream)
     torch.cuda.synchronize()
     kern_ms = e2.elapsed_time(e3) / args.steps
+    replay = replay_check(w, graph, out, lambda o: K.decode_attention(
+        w["qz"], w["q"], o, w["segs"], kv_heads=CFG["kv_heads"], qpos=w["qpos"], causal=True, hot=w["hot"],
+        warm=w["warm"]))
 
     e2e = e2e_public_api(w, args, dev, world, rank, shards)
     del graph
@@ -533,7 +565,8 @@ def run_b200(args) -> None:
                              "traffic_source": traffic["source"],
                              "algorithmic_bytes_per_step": nbytes, "kernel_ms": kern_ms,
                              "kernel_ms_covers": "fused attention incl. in-kernel LSE merge (one graph replay per step)"},
-                "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "clocks": clocks.summary()}
+                "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "clocks": clocks.summary(),
+                "replay_check": replay}
         if world == 1:
             # the spawned pool starts only after the GPU measurements: its idle workers cost
             # the host-bound e2e loop about 6% when they were alive during it
@@ -723,7 +756,7 @@ def run_layer(args) -> None:
         cfg = RFSNConfig(hidden_dim=c["hidden"], num_heads=c["heads"], head_dim=c["head_dim"], num_subspaces=c["M"],
                          subspace_dim=c["ds"], num_rvq_layers=0, hot_capacity=c["hot"], warm_capacity=4096,
                          block_size_seq=128, hot_policy="recent", device=str(dev),
-                         disk_cache_dir=str(ROOT / "gpurun_out" / "bench_layer_cold"))
+                         disk_cache_dir=str(scratch_dir("bench_layer_cold")))
         layer = RFSNDecoderLayerMLX(cfg, layer_idx=0)
         for k, v in w.items():
             getattr(layer, k).weight = torch.from_numpy(v.astype(np.float32)).to(dev)
@@ -838,7 +871,7 @@ def longctx_setup(dev):
                      rvq_sparsity_threshold=-1.0, sparse_topk=c["sparse"], hot_capacity=c["hot"],
                      warm_capacity=c["warm"], block_size_seq=128, cold_chunk_tokens=ch,
                      cold_pool_chunks=nchunks, batch_size=B, hot_policy="recent", device=str(dev),
-                     prefetch_throttle_s=0.0, disk_cache_dir=str(ROOT / "gpurun_out" / "bench_long_cold"))
+                     prefetch_throttle_s=0.0, disk_cache_dir=str(scratch_dir("bench_long_cold")))
     hq = HybridQuantizerMLX(cfg)
     flat = torch.cat([k[:, ::97].reshape(-1, D), v[:, ::97].reshape(-1, D)], 0)
     idx = torch.randint(0, flat.shape[0], (c["M"], c["K"]), generator=g, device=dev)
@@ -1017,7 +1050,7 @@ def stack_config(b_local: int, world: int, dev) -> "object":
                       head_dim=c["head_dim"], num_layers=c["layers"], num_subspaces=c["M"], subspace_dim=c["ds"],
                       num_rvq_layers=0, hot_capacity=c["hot"], warm_capacity=c["context"] + 512, block_size_seq=128,
                       batch_size=b_local, device=str(dev),
-                      disk_cache_dir=str(ROOT / "gpurun_out" / "bench_stack_cold"))
+                      disk_cache_dir=str(scratch_dir("bench_stack_cold")))
 
 
 def stack_setup(dev, b_local: int, rank: int, world: int, prefill: int):
@@ -1137,7 +1170,7 @@ def run_stack(args) -> None:
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
     # one more (untimed) replay inside an NVTX range, so a profiler can select exactly one step:
-    # ncu --nvtx --nvtx-include "rfsn_stack_step/" ...
+    # ncu --clock-control none --metrics gpu__time_duration.sum --nvtx --nvtx-include "rfsn_stack_step/" ...
     torch.cuda.nvtx.range_push("rfsn_stack_step")
     graph.replay()
     torch.cuda.nvtx.range_pop()

@@ -173,7 +173,11 @@ typedef struct rfsn_attn_args {
   const rfsn_segment* segments;
   int32_t num_segments;
   int32_t num_ctas;                /* 0 = one CTA per SM */
-  void* workspace;                 /* device scratch, >= rfsn_attention_workspace_size() bytes */
+  void* workspace;                 /* device scratch, >= rfsn_attention_workspace_size() bytes.  Its first
+                                      bytes hold a launch counter and per-row completion tickets that every
+                                      launch advances (so CUDA-graph replays of one call stay correct):
+                                      it must be zeroed once when allocated; reuse it without clearing.
+                                      Calls that overlap in time must not share a workspace. */
   size_t workspace_bytes;
   int32_t* device_status;          /* optional device int32, set non-zero on a device-side failure: 1/2 a bounded
                                       wait timed out, 4 a row ticket could not be taken */

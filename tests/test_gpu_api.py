@@ -283,19 +283,27 @@ def _stack(tmp_path, n_layers, batch, prefill):
 
 def test_decoder_stack_graph_replay_matches_eager(tmp_path):
     """A multi-layer cache-backed decode step through the public layer API captures into one
-    CUDA graph (no host syncs or pageable uploads on the path); its replay equals the eager
-    step at the same position, and a second replay reproduces it."""
-    eager = _stack(tmp_path / "a", 3, 2, 200)
-    graphed = _stack(tmp_path / "b", 3, 2, 200)
-    g = torch.Generator().manual_seed(11)
-    xs = torch.randn((4, 2, 1, 256), generator=g).half().cuda()
+    CUDA graph (no host syncs or pageable uploads on the path).  Each replay re-encodes the
+    step's token into the same slot and reruns every layer's attention: replays with new
+    inputs written into the captured input buffer (output first filled with NaN) equal the
+    eager step at the same position on those inputs."""
+    xs = torch.randn((5, 2, 1, 256), generator=torch.Generator().manual_seed(11)).half().cuda()
 
     def step(layers, x):
         for layer in layers:
             x = layer(x, use_cache=True)
         return x
 
-    ref = [step(eager, xs[t]) for t in range(4)]
+    refs = {}
+    for last in (3, 4):  # eager stacks stepped with xs[0..2], then xs[last] as the fourth token
+        eager = _stack(tmp_path / f"e{last}", 3, 2, 200)
+        for t in range(3):
+            step(eager, xs[t])
+        refs[last] = step(eager, xs[last]).float().cpu().numpy()
+        assert eager[0].cache.total_tokens == 204
+        for layer in eager:
+            layer.cache.close()
+    graphed = _stack(tmp_path / "g", 3, 2, 200)
     for t in range(3):
         step(graphed, xs[t])
     torch.cuda.synchronize()
@@ -306,14 +314,15 @@ def test_decoder_stack_graph_replay_matches_eager(tmp_path):
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=side):
         out.copy_(step(graphed, xin))
-    graph.replay()
-    torch.cuda.synchronize()
-    first = out.clone()
-    graph.replay()
-    torch.cuda.synchronize()
-    assert torch.equal(first, out)
-    close(first.float().cpu().numpy(), ref[3].float().cpu().numpy(), "graph replay vs eager")
-    assert graphed[0].cache.total_tokens == eager[0].cache.total_tokens == 204
+    for last in (3, 4, 3, 4):
+        xin.copy_(xs[last])
+        out.fill_(float("nan"))
+        graph.replay()
+        torch.cuda.synchronize()
+        got = out.float().cpu().numpy()
+        assert np.isfinite(got).all()
+        close(got, refs[last], f"graph replay with token {last} vs eager")
+    assert graphed[0].cache.total_tokens == 204
     del graph
-    for layer in eager + graphed:
+    for layer in graphed:
         layer.cache.close()

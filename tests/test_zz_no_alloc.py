@@ -91,7 +91,7 @@ def test_noalloc_matches_workspace_entry_point_twice():
         ref = torch.empty_like(q)
         got = torch.full_like(q, float("nan"))
         a_ref = _args(qz, q, ref, qpos, segs, Hkv, hot=hot, warm=warm)
-        ws = torch.empty(_workspace(a_ref, qz), dtype=torch.uint8, device="cuda")
+        ws = torch.zeros(_workspace(a_ref, qz), dtype=torch.uint8, device="cuda")
         a_ref.workspace, a_ref.workspace_bytes = ws.data_ptr(), ws.numel()
         _run("rfsn_decode_attention", a_ref, qz)
         _run("rfsn_decode_attention_noalloc", _args(qz, q, got, qpos, segs, Hkv, hot=hot, warm=warm), qz)
