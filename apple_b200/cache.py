@@ -605,7 +605,7 @@ class RFSNv10KVCacheMLX:
                 if len(self._plan_cache) > 32:
                     self._plan_cache.clear()
                 self._plan_cache[key] = (segs, dict(stats), shape)
-        stats["query_tokens"] = int(q.shape[0])
+        stats["query_tokens"] = int(qb.shape[1])  # queries per sequence (q.shape[0] for one sequence)
         self.last_access_stats = stats
         if out is None:
             out = torch.empty(qb.shape, dtype=torch.float16, device=qb.device)

@@ -1,9 +1,8 @@
 """Generate golden fixtures by running the *reference's own* RFSN code.
 
-Run in a checkout that has the reference sources (default location
-``/root/reference``, override with RFSN_REFERENCE_DIR):
+Run with RFSN_REFERENCE_DIR pointing at a checkout of the reference sources:
 
-    python tests/golden/make_golden.py
+    RFSN_REFERENCE_DIR=<reference checkout> python tests/golden/make_golden.py
 
 The reference is imported unmodified through the torch-CPU ``mlx`` shim
 (``oracle/mlx_shim``).  Inputs and codebooks come from numpy generators with
@@ -269,6 +268,58 @@ def case_calibration(ref, name, seed, n=2048, iters=10):
                         sparsity_fraction=np.array(metrics["sparsity_fraction"], np.float64), threshold=np.float32(0.5))
 
 
+def case_gqa_batch(ref, name, seed, batch=3, kv_heads=2, group=4, n_tokens=60, queries=(59, 44, 20),
+                   windows=(None, 8, 30)):
+    """GQA and batch > 1 pinned to the reference.  GQA: the reference's own Llama adapter
+    repeats each KV head over its query group with _repeat_kv (llama32_adapter.py:380-386,
+    580-581) before the cache sees it, so the reference result is a cache over the repeated
+    heads.  Batch: the reference cache holds one sequence, so a batch is a loop of reference
+    caches, one per sequence, each asked at the same query position and window.  Codebooks:
+    PQ 16x4 and one dense RVQ stage (threshold -1), the headline configuration's layout."""
+    mx = sys.modules["mlx.core"]
+    import importlib
+    repeat_kv = importlib.import_module("llama32_adapter")._repeat_kv
+    rng = np.random.default_rng(seed)
+    hq, d = kv_heads * group, 64
+    tmp = Path(tempfile.mkdtemp(prefix="rfsn_gqa_"))
+    try:
+        pq_cb, rvq_cb = seeded_codebooks(rng, 16, 256, 4, 1, 256, d)
+        keys = rng.standard_normal((batch, n_tokens, kv_heads, d)).astype(np.float32)
+        keys[..., rng.choice(d, size=4, replace=False)] *= 10.0
+        keys = keys.astype(np.float16)
+        values = rng.standard_normal((batch, n_tokens, kv_heads, d)).astype(np.float16)
+        q = rng.standard_normal((batch, hq, d)).astype(np.float16)
+        split = n_tokens - 3
+        outs = np.zeros((len(queries) * len(windows), batch, hq, d), np.float16)
+        stats = np.zeros((len(queries) * len(windows), batch, len(STAT_KEYS)), np.int64)
+        cases = []
+        for b in range(batch):
+            config = make_config(ref, hidden_dim=hq * d, num_heads=hq, head_dim=d, num_subspaces=16, subspace_dim=4,
+                                 num_rvq_layers=1, rvq_sparsity_threshold=-1.0, disk_cache_dir=str(tmp / f"s{b}"))
+            hqz = make_quantizer(ref, config, pq_cb, rvq_cb)
+            cache = ref["cache"].RFSNv10KVCacheMLX(config, layer_idx=0)
+            rk = repeat_kv(mx.array(keys[b:b + 1]), group)[0]
+            rv = repeat_kv(mx.array(values[b:b + 1]), group)[0]
+            cache.update(rk[:split], rv[:split], hqz, disk_dir=tmp / f"s{b}")
+            cache.update(rk[split:], rv[split:], hqz, disk_dir=tmp / f"s{b}")
+            i = 0
+            for qpos in queries:
+                for win in windows:
+                    out = cache.attention_forward(mx.array(q[b:b + 1]), causal=True,
+                                                  query_positions=mx.array([qpos], dtype=mx.int32), context_window=win)
+                    outs[i, b] = np.asarray(out)[0]
+                    st = cache.get_last_access_stats()
+                    stats[i, b] = [st[k] for k in STAT_KEYS]
+                    if b == 0:
+                        cases.append((qpos, -1 if win is None else win))
+                    i += 1
+        np.savez_compressed(OUT / f"{name}.npz", keys=keys, values=values, q=q, pq_codebooks=pq_cb,
+                            rvq_codebooks=rvq_cb, threshold=np.float32(-1.0), update_split=np.int32(split),
+                            group=np.int32(group), cases=np.array(cases, np.int32), out=outs, stats=stats)
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+
+
 CASES = {
     "quant": lambda ref: (
         case_quantizer(ref, "quant_d128_m8x16_rvq3", seed=11, cfg_kw={}, n=96, scale_half=0.01),
@@ -287,6 +338,7 @@ CASES = {
     "router": lambda ref: case_router(ref, "router_order"),
     "layer": lambda ref: case_decoder_layer(ref, "decoder_layer", seed=41),
     "calibration": lambda ref: case_calibration(ref, "calibration_kmeans", seed=51),
+    "gqa_batch": lambda ref: case_gqa_batch(ref, "gqa_batch_cache", seed=61),
 }
 
 

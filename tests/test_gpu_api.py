@@ -92,6 +92,29 @@ def test_cache_tiers_golden(tmp_path):
     cache.close()
 
 
+def test_gqa_batch_cache_golden(tmp_path):
+    """GQA and batch > 1 pinned to the reference: one batched, grouped-head cache against the
+    reference's cache over _repeat_kv'd heads (llama32_adapter.py:380-386), one reference cache
+    per sequence, at 3 query positions x 3 windows."""
+    g = dict(np.load(GOLDEN / "gqa_batch_cache.npz"))
+    B, T, Hkv, D = g["keys"].shape
+    Hq = g["q"].shape[1]
+    cfg = tiers_config(tmp_path, hidden_dim=Hq * D, num_heads=Hq, head_dim=D, num_subspaces=16, subspace_dim=4,
+                       num_rvq_layers=1, rvq_sparsity_threshold=-1.0, num_kv_heads=Hkv, batch_size=B)
+    qz = golden_quantizer(cfg, g)
+    cache = RFSNv10KVCacheMLX(cfg, layer_idx=0)
+    s = int(g["update_split"])
+    cache.update(torch.from_numpy(g["keys"][:, :s]).cuda(), torch.from_numpy(g["values"][:, :s]).cuda(), qz)
+    cache.update(torch.from_numpy(g["keys"][:, s:]).cuda(), torch.from_numpy(g["values"][:, s:]).cuda(), qz)
+    q = torch.from_numpy(g["q"]).cuda()
+    for i, (qpos, win) in enumerate(g["cases"]):
+        win = None if win < 0 else int(win)
+        out = cache.attention_forward(q, causal=True, query_positions=[int(qpos)], context_window=win)
+        assert [cache.last_access_stats[k] for k in STAT_KEYS] == list(g["stats"][i, 0]), i
+        close(out.cpu().numpy(), g["out"][i], f"case {i}")
+    cache.close()
+
+
 def test_cache_tiers_with_router(tmp_path):
     """Router-driven prefetch: same outputs, hit/miss statistics as the oracle with the router's loads."""
     g = dict(np.load(GOLDEN / "cache_tiers.npz"))

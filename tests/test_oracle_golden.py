@@ -112,6 +112,26 @@ def test_cache_tiers_materialize_and_attention():
         np.testing.assert_array_equal(adj, g[f"{tag}_adjusted"])
 
 
+def test_gqa_and_batch_match_reference_loop():
+    """GQA (the reference's _repeat_kv then its cache) and batch > 1 (a loop of reference caches)
+    against the oracle's grouped-head, batched cache."""
+    g = load("gqa_batch_cache")
+    B, T, Hkv, D = g["keys"].shape
+    Hq = g["q"].shape[1]
+    cfg = R.OracleConfig(hidden_dim=Hq * D, num_heads=Hq, head_dim=D, num_subspaces=16, subspace_dim=4,
+                         num_rvq_layers=1, rvq_codebook_size=256, rvq_sparsity_threshold=-1.0, hot_capacity=16,
+                         warm_capacity=24, block_size_seq=16, num_kv_heads=Hkv)
+    cache = R.OracleCache(cfg, R.Quantizer(g["pq_codebooks"], g["rvq_codebooks"], -1.0), batch=B)
+    split = int(g["update_split"])
+    cache.update(g["keys"][:, :split], g["values"][:, :split])
+    cache.update(g["keys"][:, split:], g["values"][:, split:])
+    for i, (qpos, win) in enumerate(g["cases"]):
+        win = None if win < 0 else int(win)
+        out = cache.attention_forward(g["q"][:, None], causal=True, query_positions=[int(qpos)], context_window=win)
+        assert [cache.last_access_stats[k] for k in STAT_KEYS] == list(g["stats"][i, 0]), i
+        np.testing.assert_allclose(out[:, 0].astype(np.float32), g["out"][i].astype(np.float32), atol=1e-3)
+
+
 def test_router_candidate_order():
     g = load("router_order")
     for (pos, win, k), want in zip(g["queries"], g["loaded"]):
