@@ -89,6 +89,7 @@ class RFSNv10KVCacheMLX:
         # buffer or the quantizer is replaced, which retires the calls that point at them
         self._attn_calls: Dict[Tuple, Any] = {}
         self._store_epoch = 0
+        self.last_routed_chunks: List[int] = []  # centroid routing: the cold chunks the last call attended
 
     # ------------------------------------------------------------------ stats
     def _empty_access_stats(self) -> Dict[str, int]:
@@ -242,6 +243,7 @@ class RFSNv10KVCacheMLX:
         root = Path(self.config.disk_cache_dir) if disk_dir is None else Path(disk_dir)
         if self._cold is None:
             self._cold = ColdTier(self._qz, self.rows, self.chunk_tokens, self.config.cold_pool_chunks, self.device)
+            self._cold.track_centroids = self.config.cold_routing == "centroid"
             self._cold_root = root
             register_cold_tier(root, self.layer_idx, self._cold)
         return self._cold
@@ -347,7 +349,7 @@ class RFSNv10KVCacheMLX:
             elif within:
                 tier.load_stage(chunk, stream)  # keep the chunk's earlier tokens in the image
             self._encode_kv(k[:, off:off + take], v[:, off:off + take], tier.stage, 0, within)
-            tier.store_stage(chunk, stream)
+            tier.store_stage(chunk, stream, num_tokens=within + take)
             chunk.end_token += take
             self._record_chunk_meta(cid, pos, take)
             off += take
@@ -406,7 +408,7 @@ class RFSNv10KVCacheMLX:
             nb = ct // K.BLOCK_TOKENS
             with torch.cuda.stream(stream):
                 tier.stage.data[0].copy_(self._warm.data[0, :, b0:b0 + nb])
-            tier.store_stage(chunk, stream)
+            tier.store_stage(chunk, stream, num_tokens=ct)
             chunk.end_token = pos + ct
             self._record_chunk_meta(cid, pos, ct)
         self._warm_start += evict
@@ -440,8 +442,12 @@ class RFSNv10KVCacheMLX:
         return [("warm", self._warm_start, self._warm_start + self.num_warm),
                 ("hot", self._hot_start, self._hot_start + self.num_hot)]
 
-    def _plan(self, start: int, end: int, router, current_position, context_window, stats) -> List[Tuple]:
-        """Segments of the window [start, end) in position order + reference stats (cache.py:250-342)."""
+    def _plan(self, start: int, end: int, router, current_position, context_window, stats,
+              routed: Optional[Tuple[List[int], set]] = None) -> List[Tuple]:
+        """Segments of the window [start, end) in position order + reference stats (cache.py:250-342).
+
+        routed (centroid routing): (chosen cold chunk ids, ids resident before the choice);
+        only the chosen cold chunks enter the window, and they count as router hits or misses."""
         segs: List[Tuple[int, Tuple]] = []
         bs = max(1, self.config.block_size_seq)
         for kind, s, e in self._spans():
@@ -459,7 +465,24 @@ class RFSNv10KVCacheMLX:
                 for idx, cnt, p in self._warm_runs(a, b - a):
                     segs.append((p, (K.STORE_WARM, 0, idx, cnt, p)))
         tier = self._cold
-        if tier is not None and self.cold_chunk_metadata:
+        if tier is not None and self.cold_chunk_metadata and routed is not None:
+            chosen, hits = routed
+            keep = set(chosen)
+            stream = torch.cuda.current_stream()
+            for meta in self.cold_chunk_metadata:
+                a, b = max(start, meta["start_token"]), min(end, meta["end_token"])
+                cid = meta["chunk_id"]
+                if a >= b or cid not in keep:
+                    continue
+                stats["cold_chunk_cache_hits" if cid in hits else "cold_chunk_cache_misses"] += 1
+                stats["cold_tokens_materialized"] += b - a
+                stats["reconstructed_tokens"] += b - a
+                stats["cold_chunk_decodes"] += 1
+                stats["cold_chunks_touched"] += 1
+                slot = tier.ensure_resident(cid, stream, keep)
+                tier.wait_ready(slot, stream)
+                segs.append((a, (K.STORE_COLD, slot, a - meta["start_token"], b - a, a)))
+        elif tier is not None and self.cold_chunk_metadata:
             if router is not None and current_position is not None and context_window is not None:
                 ct = self.chunk_tokens
                 router.prefetch_sync(current_position=current_position, context_window=context_window,
@@ -595,11 +618,17 @@ class RFSNv10KVCacheMLX:
             key = (start, end, context_window, self.total_tokens, self.num_hot, self.num_warm, self._hot_start,
                    self._warm_start)
         cached = self._plan_cache.get(key) if key is not None else None
+        routed = None
+        if self.config.cold_routing == "centroid" and router is not None and self._cold is not None:
+            eligible = [m["chunk_id"] for m in self.cold_chunk_metadata
+                        if m["start_token"] < end and m["end_token"] > start]
+            routed = router.route_centroids(qb, self.heads, self.config.cold_route_top_k, eligible)
+            self.last_routed_chunks = list(routed[0])
         if cached is not None:
             segs, stats, shape = cached[0], dict(cached[1]), cached[2]
         else:
             stats = self._begin_stats(start, end, context_window, router)
-            segs = self._plan(start, end, router, current_position, context_window, stats)
+            segs = self._plan(start, end, router, current_position, context_window, stats, routed)
             shape = tuple((sg[0], sg[1]) for sg in segs)  # the stores and slots, in order
             if key is not None:
                 if len(self._plan_cache) > 32:

@@ -415,6 +415,31 @@ def attention_call(qz: QuantizerBuffers, q: torch.Tensor, out: torch.Tensor, seg
     return entry
 
 
+def route_topk(q: torch.Tensor, centroids: torch.Tensor, kv_heads: int, k: int,
+               scores: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Centroid routing (rfsn_route_topk): q fp16 [B, Q, Hq, D] (packed per sequence),
+    centroids fp32 [C, B * kv_heads, D] -> (ids int32 [k] on the device, descending score,
+    ties to the lower index; scores fp32 [C])."""
+    _need_cuda(q, "q")
+    _need_cuda(centroids, "centroids")
+    if q.dtype != torch.float16 or q.dim() != 4 or not queries_packed(q):
+        raise ValueError("q must be fp16 [B, Q, Hq, D], packed within a sequence")
+    B, Qn, Hq, D = q.shape
+    C = centroids.shape[0]
+    if centroids.dtype != torch.float32 or not centroids.is_contiguous() or \
+            tuple(centroids.shape[1:]) != (B * kv_heads, D):
+        raise ValueError(f"centroids must be contiguous fp32 [C, {B * kv_heads}, {D}]")
+    if not 0 <= k <= min(C, 64):
+        raise ValueError("route_topk: 0 <= k <= min(num_chunks, 64)")
+    if scores is None or scores.numel() < C:
+        scores = torch.empty(max(C, 1), dtype=torch.float32, device=q.device)
+    ids = torch.empty(max(k, 1), dtype=torch.int32, device=q.device)
+    scratch = torch.empty(max(C, 1), dtype=torch.uint8, device=q.device)
+    call("rfsn_route_topk", _ptr(q), q.stride(0) if B > 1 else 0, B, Qn, Hq, kv_heads, D, _ptr(centroids), C, k,
+         _ptr(scores), _ptr(ids), _ptr(scratch), _stream(q.device.index))
+    return ids[:k], scores[:C]
+
+
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
     """fp16 RMSNorm over the last dim in one launch (fp32 math, fp32 weight)."""
     _need_cuda(x, "x")

@@ -43,6 +43,11 @@ class RFSNConfig:
       sparse_topk       top-S |error| fp16 residual entries per token (0 = off).
       cold_chunk_tokens cold chunk length (None = block_size_seq, as cache.py:144).
       cold_pool_chunks  device-resident cold chunk slots (LRU).
+      cold_routing      "exact" (reference: attention reads every cold chunk the window
+                        overlaps, cache.py:293-342) or "centroid": with a router, attention
+                        reads only the cold_route_top_k chunks whose mean key scores highest
+                        against the step's queries (rfsn_route_topk).
+      cold_route_top_k  chunks a centroid-routed step attends (at most 64).
       device            CUDA device of the cache and quantizer.
     """
 
@@ -82,6 +87,8 @@ class RFSNConfig:
     sparse_topk: int = 0
     cold_chunk_tokens: Optional[int] = None
     cold_pool_chunks: int = 32
+    cold_routing: str = "exact"
+    cold_route_top_k: int = 8
     device: str = "cuda"
 
     def __post_init__(self) -> None:
@@ -93,6 +100,10 @@ class RFSNConfig:
             )
         if self.hot_policy not in ("prefix", "recent"):
             raise ValueError("hot_policy must be 'prefix' or 'recent'")
+        if self.cold_routing not in ("exact", "centroid"):
+            raise ValueError("cold_routing must be 'exact' or 'centroid'")
+        if not 1 <= self.cold_route_top_k <= 64:
+            raise ValueError("cold_route_top_k must be in [1, 64]")
         if self.num_kv_heads is not None and self.num_heads % self.num_kv_heads:
             raise ValueError("num_heads must be a multiple of num_kv_heads")
         if self.hot_policy == "recent" and self.chunk_tokens % 16:
@@ -268,6 +279,11 @@ class ColdTier:
         self.lock = threading.Lock()
         self.h2d_bytes = 0
         self.d2h_bytes = 0
+        # centroid routing: mean decoded key of every chunk per row, fp32 [capacity, rows, D]
+        self.track_centroids = False
+        self.centroids: Optional[torch.Tensor] = None
+        self.centroid_ids: List[int] = []          # table index -> chunk id
+        self.centroid_index: Dict[int, int] = {}   # chunk id -> table index
 
     @property
     def image_bytes(self) -> int:
@@ -289,8 +305,11 @@ class ColdTier:
         self.h2d_bytes += self.image_bytes
         return self.stage
 
-    def store_stage(self, chunk: ColdChunk, stream: torch.cuda.Stream) -> None:
-        """Write the device stage back as the chunk's image (device -> pinned host)."""
+    def store_stage(self, chunk: ColdChunk, stream: torch.cuda.Stream, num_tokens: Optional[int] = None) -> None:
+        """Write the device stage back as the chunk's image (device -> pinned host); with
+        centroid routing, also record the mean decoded key of its ``num_tokens`` tokens."""
+        if self.track_centroids and num_tokens:
+            self.set_centroid(chunk.chunk_id, num_tokens, stream)
         K.call("rfsn_cold_evict", chunk.store.data.data_ptr(), self.stage.data.data_ptr(), self.image_bytes,
                stream.cuda_stream)
         self.d2h_bytes += self.image_bytes
@@ -299,6 +318,24 @@ class ColdTier:
         chunk.ready = ev
         chunk.version += 1
         self.invalidate(chunk.chunk_id)
+
+    def set_centroid(self, chunk_id: int, num_tokens: int, stream: torch.cuda.Stream) -> None:
+        """Mean of the stage's decoded keys over its first num_tokens tokens, per row, in fp32."""
+        D = self.qz.D
+        with torch.cuda.stream(stream):
+            keys = torch.empty((1, num_tokens, self.rows, D), dtype=torch.float16, device=self.device)
+            K.decode_codes(self.qz, self.stage, 0, 0, num_tokens, keys, kv=0)
+            idx = self.centroid_index.get(chunk_id)
+            if idx is None:
+                idx = len(self.centroid_ids)
+                if self.centroids is None or idx >= self.centroids.shape[0]:
+                    grown = torch.zeros((max(64, 2 * idx), self.rows, D), dtype=torch.float32, device=self.device)
+                    if self.centroids is not None:
+                        grown[:idx].copy_(self.centroids[:idx])
+                    self.centroids = grown
+                self.centroid_ids.append(chunk_id)
+                self.centroid_index[chunk_id] = idx
+            self.centroids[idx].copy_(keys[0].float().mean(dim=0))
 
     def invalidate(self, chunk_id: int) -> None:
         slot = self.slot_of.pop(chunk_id, None)
@@ -483,6 +520,35 @@ class AsyncHierarchicalRouterMLX:
         tier.pinned_by_router.add(chunk_id)
         c = tier.chunks[chunk_id]
         return {"chunk_id": chunk_id, "slot": slot, "num_tokens": c.num_tokens, "start_token": c.start_token}
+
+    def route_centroids(self, q: torch.Tensor, kv_heads: int, top_k: int, eligible: List[int]) -> Tuple[List[int], set]:
+        """Centroid routing (extension): the top_k of the ``eligible`` cold chunk ids by the
+        score of rfsn_route_topk for queries q fp16 [B, Q, Hq, D], prefetched into the device
+        pool on the router's side stream (the reference's router orders by distance from the
+        position instead, storage.py:166-182).  Returns (chunk ids in score order, ids that
+        were already resident before this call)."""
+        tier = self._tier()
+        if tier is None or tier.centroids is None or not eligible:
+            return [], set()
+        idx = [tier.centroid_index[c] for c in eligible]
+        n = len(tier.centroid_ids)
+        if idx == list(range(n)):
+            cent = tier.centroids[:n]
+        else:
+            cent = tier.centroids.index_select(0, torch.as_tensor(idx, device=tier.centroids.device))
+        k = min(top_k, len(idx))
+        # the scores read q on the compute stream; the chunk copies go on the router's stream
+        ids_dev, _ = K.route_topk(q, cent, kv_heads, k)
+        chosen = [eligible[i] for i in ids_dev.tolist()]
+        hits = {c for c in chosen if tier.resident(c)}
+        for cid in chosen:
+            if cid not in hits or cid not in self._cache:
+                self._cache[cid] = self._load_chunk_sync(cid)
+            self._cache.move_to_end(cid)
+        while len(self._cache) > max(self._max_cache_size, top_k):
+            old, _ = self._cache.popitem(last=False)
+            tier.pinned_by_router.discard(old)
+        return chosen, hits
 
     def get_chunk(self, chunk_id: int) -> Optional[Dict[str, object]]:
         entry = self._cache.get(chunk_id)

@@ -852,8 +852,9 @@ def long_bytes() -> int:
         2 * c["batch"] * c["q_heads"] * c["head_dim"] * 2
 
 
-def longctx_setup(dev):
-    """Build the configs[3] cache (hot/warm/cold tiers filled) on `dev`; returns (cfg, cache, q)."""
+def longctx_setup(dev, **overrides):
+    """Build the configs[3] cache (hot/warm/cold tiers filled) on `dev`; returns (cfg, cache, q).
+    overrides: RFSNConfig fields (the routed workload sets cold_routing and a smaller pool)."""
     import torch
     from apple_b200.cache import RFSNv10KVCacheMLX
     from apple_b200.quantization import HybridQuantizerMLX
@@ -870,8 +871,9 @@ def longctx_setup(dev):
                      num_subspaces=c["M"], subspace_dim=c["ds"], num_rvq_layers=1, rvq_codebook_size=c["Kr"],
                      rvq_sparsity_threshold=-1.0, sparse_topk=c["sparse"], hot_capacity=c["hot"],
                      warm_capacity=c["warm"], block_size_seq=128, cold_chunk_tokens=ch,
-                     cold_pool_chunks=nchunks, batch_size=B, hot_policy="recent", device=str(dev),
-                     prefetch_throttle_s=0.0, disk_cache_dir=str(scratch_dir("bench_long_cold")))
+                     batch_size=B, hot_policy="recent", device=str(dev), prefetch_throttle_s=0.0,
+                     disk_cache_dir=str(scratch_dir("bench_long_cold")),
+                     **{"cold_pool_chunks": nchunks, **overrides})
     hq = HybridQuantizerMLX(cfg)
     flat = torch.cat([k[:, ::97].reshape(-1, D), v[:, ::97].reshape(-1, D)], 0)
     idx = torch.randint(0, flat.shape[0], (c["M"], c["K"]), generator=g, device=dev)
@@ -1009,6 +1011,186 @@ def run_longctx(args) -> None:
                 "d2h_bytes_per_step": hqh.numel() * 2, "api": "RFSNv10KVCacheMLX.attention_forward with router"},
         "max_abs_diff_api_vs_graph": err, "gpu_launches": steps, "clocks": clocks.summary(),
         "cpu_baseline": longctx_cpu_baseline()}))
+    cache.close()
+
+
+# ---------------------------------------------------------------------------
+# Routed long-context decode (BASELINE configs[3] with the router it names)
+# ---------------------------------------------------------------------------
+# The configs[3] cache with cold_routing="centroid": every step the router scores
+# the 188 cold chunks by their mean key against the step's queries
+# (rfsn_route_topk), prefetches the top 8 into a 24-slot device pool (smaller than
+# the cold set, so steps copy chunks in) on its side stream, and the fused kernel
+# attends hot + warm + those 8 chunks.  Queries drift as a random walk from step to
+# step (step 0.35 of their scale), as consecutive decode queries are correlated.
+
+ROUTED = dict(top_k=8, pool=24, drift=0.35)
+
+
+def routed_bytes() -> int:
+    c = LONG
+    rows = c["batch"] * c["kv_heads"]
+    coded = c["warm"] + ROUTED["top_k"] * c["chunk"]
+    return rows * (c["hot"] * 2 * c["head_dim"] * 2 + coded * 2 * (c["M"] + 1 + 3 * c["sparse"])) + \
+        2 * c["batch"] * c["q_heads"] * c["head_dim"] * 2
+
+
+def routed_queries(dev, steps: int, seed: int):
+    import torch
+    c = LONG
+    g = torch.Generator(device=dev).manual_seed(seed)
+    q = torch.randn((c["batch"], c["q_heads"], c["head_dim"]), generator=g, device=dev)
+    out = []
+    for _ in range(steps):
+        q = q + ROUTED["drift"] * torch.randn(q.shape, generator=g, device=dev)
+        out.append((q / (1 + ROUTED["drift"] ** 2) ** 0.5).half())
+    return out
+
+
+def routed_cpu_baseline(steps: int = 2) -> dict:
+    """The numpy cache (oracle/restate.py) on ONE (sequence, KV head) row of the routed configs[3]
+    workload: centroid scores of the 188 cold chunks, the top 8, attention over hot 2048 + warm
+    32768 + those chunks; the batch's step time extrapolated x32 rows."""
+    from oracle import restate as R
+    c = LONG
+    rng = np.random.default_rng(c["seed"])
+    T, ch, D = c["context"], c["chunk"], c["head_dim"]
+    G = c["q_heads"] // c["kv_heads"]
+    walk = np.cumsum(rng.standard_normal((T // ch, D), dtype=np.float32) * 0.05, axis=0)
+    k = (np.repeat(walk, ch, axis=0) + rng.standard_normal((T, D), dtype=np.float32)).astype(np.float16)[None, :, None]
+    v = rng.standard_normal((1, T, 1, D), dtype=np.float32).astype(np.float16)
+    flat = np.concatenate([k[0, ::97, 0], v[0, ::97, 0]], 0)
+    idx = rng.integers(0, flat.shape[0], (c["M"], c["K"]))
+    pq = np.stack([flat[idx[m], c["ds"] * m:c["ds"] * (m + 1)] for m in range(c["M"])]).astype(np.float16)
+    _, res = R.pq_quantize(flat[rng.integers(0, flat.shape[0], c["Kr"])], pq)
+    rvq = res.reshape(1, c["Kr"], D).astype(np.float16).copy()
+    rvq[:, 0] = 0
+    cfg = R.OracleConfig(hidden_dim=G * D, num_heads=G, num_kv_heads=1, head_dim=D, num_subspaces=c["M"],
+                         subspace_dim=c["ds"], num_rvq_layers=1, rvq_codebook_size=c["Kr"],
+                         rvq_sparsity_threshold=-1.0, hot_capacity=c["hot"], warm_capacity=c["warm"],
+                         block_size_seq=128, sparse_topk=c["sparse"], hot_policy="recent", cold_chunk_tokens=ch)
+    cache = R.OracleCache(cfg, R.Quantizer(pq, rvq, -1.0, sparse_topk=c["sparse"]), batch=1)
+    for a in range(0, T, 8192):
+        cache.update(k[:, a:a + 8192], v[:, a:a + 8192])
+    ids, cent = cache.chunk_centroids()
+    q = rng.standard_normal((1, 1, G, D), dtype=np.float32).astype(np.float16)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        sel, _ = R.route_topk(q, cent, 1, ROUTED["top_k"])
+        cache.attention_forward(q, causal=True, context_window=T, current_position=T - 1,
+                                routed_chunks=[ids[i] for i in sel])
+    dt = (time.perf_counter() - t0) / steps
+    rows = c["batch"] * c["kv_heads"]
+    return {"value": 1.0 / (dt * rows), "unit": "steps/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"numpy cache (oracle/restate.py), one (sequence, KV head) row: centroid scores of 188 cold "
+                      f"chunks, top 8, attention over hot 2048 + warm 32768 + 8 x 512; mean of {steps} steps = "
+                      f"{dt * 1e3:.0f} ms; step time extrapolated x{rows} rows"}
+
+
+def run_routed(args) -> None:
+    import torch
+    from apple_b200 import kernels as K
+    from apple_b200.storage import AsyncHierarchicalRouterMLX
+    c = LONG
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    cfg, cache, q0 = longctx_setup(dev, cold_routing="centroid", cold_route_top_k=ROUTED["top_k"],
+                                   cold_pool_chunks=ROUTED["pool"])
+    B, Hkv, T, Hq = c["batch"], c["kv_heads"], c["context"], c["q_heads"]
+    router = AsyncHierarchicalRouterMLX(cfg, layer_idx=0)
+    steps = max(10, args.steps)
+    warm = max(3, args.warmup)
+    qs = routed_queries(dev, warm + 2 * steps, seed=c["seed"] + 100)
+    tier = cache._cold
+    outs = [torch.empty((B, Hq, c["head_dim"]), dtype=torch.float16, device=dev) for _ in range(2)]
+
+    def step(q, out):
+        return cache.attention_forward(q, causal=True, router=router, current_position=T - 1, context_window=T,
+                                       out=out)
+
+    for i in range(warm):
+        step(qs[i], outs[i % 2].unsqueeze(1))
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h0 = tier.h2d_bytes
+    hits = misses = 0
+    with ClockSampler(dev) as clocks:
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for i in range(steps):
+            step(qs[warm + i], outs[i % 2].unsqueeze(1))
+            st = cache.last_access_stats
+            hits += st["cold_chunk_cache_hits"]
+            misses += st["cold_chunk_cache_misses"]
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    h2d = (tier.h2d_bytes - h0) / steps
+    # the attention kernel alone over one step's routed window, replayed from a graph
+    start, end, _ = cache._window_bounds(None, T, T - 1)
+    eligible = [m["chunk_id"] for m in cache.cold_chunk_metadata]
+    qb = qs[0].unsqueeze(1).contiguous()
+    routed = router.route_centroids(qb, Hkv, ROUTED["top_k"], eligible)
+    segs = cache._plan(start, end, None, None, None, cache._begin_stats(start, end, T, None), routed)
+    out = torch.empty_like(qb)
+    qpos = torch.full((B, 1, Hq), T - 1, dtype=torch.int32, device=dev)
+
+    def attn():
+        K.decode_attention(cache._qz, qb, out, segs, kv_heads=Hkv, qpos=qpos, causal=True,
+                           hot=(cache._hot_k, cache._hot_v), warm=cache._warm, cold=tier.pool)
+
+    for _ in range(3):
+        attn()
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        attn()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for _ in range(steps):
+        graph.replay()
+    e3.record(stream)
+    torch.cuda.synchronize()
+    kern_ms = e2.elapsed_time(e3) / steps
+    ref = step(qs[0], None)
+    err = float((out[:, 0].float() - ref.float()).abs().max())
+    # e2e: pinned host query in, host output out, every step
+    hq = [qs[warm + steps + i].cpu().pin_memory() for i in range(steps)]
+    hout = torch.empty_like(hq[0]).pin_memory()
+    t0 = time.perf_counter()
+    for i in range(steps):
+        hout.copy_(step(hq[i], None))
+    e2e_s = (time.perf_counter() - t0) / steps
+    nbytes = routed_bytes()
+    peak, _ = measured_peak()
+    del graph
+    print(json.dumps({
+        "metric": "routed long-context decode steps/s (131K ctx, top-8 cold chunks by centroid score)",
+        "value": 1e3 / ms, "unit": "steps/s", "n_gpus": 1, "steps": steps, "warmup": warm, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16 operands, f32 accumulate",
+        "data": "synthetic",
+        "config": {"workload": "BASELINE configs[3] routed: batch 4, 131072 ctx, hot 2048 / warm 32768 / cold 188 x 512 "
+                               "in pinned host memory, top 8 chunks by centroid score per step",
+                   "device_pool_chunks": ROUTED["pool"], "query_drift": ROUTED["drift"],
+                   "step": "route (scores + top-8 on the GPU, ids to the host) + prefetch of missing chunks on the "
+                           "router stream + fused attention; device-resident queries"},
+        "h2d": {"bytes_per_step": h2d, "gbs_over_step": h2d / (ms * 1e-3) / 1e9,
+                "chunk_hit_rate": hits / max(1, hits + misses), "chunk_image_bytes": tier.image_bytes},
+        "roofline": {"bound": "hbm", "achieved": nbytes / (kern_ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": nbytes / (kern_ms * 1e-3) / 1e9 / peak, "traffic": None,
+                     "algorithmic_bytes_per_step": nbytes, "kernel_ms": kern_ms,
+                     "kernel_ms_covers": "fused attention over the routed window (graph replay, resident chunks)"},
+        "e2e": {"value": 1.0 / e2e_s, "unit": "steps/s", "h2d_bytes_per_step": hq[0].numel() * 2 + h2d,
+                "d2h_bytes_per_step": hq[0].numel() * 2,
+                "api": "RFSNv10KVCacheMLX.attention_forward with router, cold_routing='centroid'"},
+        "max_abs_diff_api_vs_graph": err, "gpu_launches": 3 * steps, "clocks": clocks.summary(),
+        "cpu_baseline": routed_cpu_baseline()}))
     cache.close()
 
 
@@ -1252,7 +1434,8 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=0,
                     help="stack workload only: number of layers (default: the 22 of configs[2]); fewer layers "
                          "make a small case for profiling captures")
-    ap.add_argument("--workload", default="decode", choices=["decode", "encode", "layer", "longctx", "stack"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "encode", "layer", "longctx", "routed",
+                                                             "stack"],
                     help="decode: fused decode attention (configs[1], the headline); encode: spill encoder "
                          "(configs[4]); layer: single decoder layer decode (configs[0]); longctx: 131K three-tier "
                          "decode (configs[3]); stack: 22-layer decode stack (configs[2])")
@@ -1282,6 +1465,17 @@ def main() -> None:
                                                                "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
         else:
             run_longctx(args)
+    elif args.workload == "routed":
+        if args.impl == "reference":
+            if int(os.environ.get("RANK", "0")) == 0:
+                cb = routed_cpu_baseline()
+                print(json.dumps({"metric": "routed long-context decode steps/s (131K ctx, top-8 cold chunks by "
+                                            "centroid score)", "value": cb["value"], "unit": "steps/s",
+                                  "n_gpus": args.gpus, "impl": "reference", "cpu_baseline": cb,
+                                  "e2e": {"value": cb["value"], "unit": "steps/s", "h2d_bytes_per_step": 0,
+                                          "d2h_bytes_per_step": 0}}))
+        else:
+            run_routed(args)
     elif args.workload == "layer":
         if args.impl == "reference":
             if int(os.environ.get("RANK", "0")) == 0:

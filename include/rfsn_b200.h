@@ -205,6 +205,18 @@ int rfsn_decode_attention(const rfsn_attn_args* args, const rfsn_quantizer* qz, 
 #define RFSN_NOALLOC_SCRATCH_BYTES (4u << 20)
 int rfsn_decode_attention_noalloc(const rfsn_attn_args* args, const rfsn_quantizer* qz, void* stream);
 
+/* Centroid routing of the cold tier (extension; the reference's router, storage.py:166-182,
+ * orders chunks by distance from the position and the cache then decodes every chunk the window
+ * overlaps, cache.py:293-342).  centroids: fp32 [num_chunks][batch * kv_heads][head_dim], the
+ * mean decoded key of each chunk per row.  q: fp16 [batch][queries][q_heads][head_dim] with
+ * batch stride q_batch_stride elements (0 = packed).  scores[c] = max over (b, i, h) of
+ * q[b, i, h] . centroids[c][b * kv_heads + h / (q_heads / kv_heads)] (fp32); ids[0..k) = the k
+ * highest-scoring chunk indices, descending, ties to the lower index.  scratch: num_chunks bytes
+ * of device memory.  k <= 64.  Device outputs, stream-ordered. */
+int rfsn_route_topk(const uint16_t* q, int64_t q_batch_stride, int32_t batch, int32_t queries, int32_t q_heads,
+                    int32_t kv_heads, int32_t head_dim, const float* centroids, int32_t num_chunks, int32_t k,
+                    float* scores, int32_t* ids, uint8_t* scratch, void* stream);
+
 /* Cold tier transfer — replaces load_compressed_chunk / np.load in the router's
  * executor (storage.py:138-140, 226-234): one cudaMemcpyAsync of `bytes` from
  * pinned host memory to device memory on `stream` (the router's side stream),

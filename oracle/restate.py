@@ -540,8 +540,19 @@ class OracleCache:
                 ("hot", self.hot_start, self.hot_start + self.num_hot)]
 
     # -- materialize ------------------------------------------------------------
+    def chunk_centroids(self) -> Tuple[List[int], np.ndarray]:
+        """Centroid routing (extension): (cold chunk ids, fp32 [C, B * Hkv, D] mean decoded key of
+        each chunk per row, row = b * Hkv + h)."""
+        ids, cents = [], []
+        for meta in self.cold:
+            dec = np.stack([self.q.decode(c) for c in meta["k"]])  # [B, n, Hkv, D] fp16
+            cents.append(dec.astype(F32).mean(axis=1).reshape(self.batch * self.h, self.d))
+            ids.append(meta["chunk_id"])
+        return ids, (np.stack(cents).astype(F32) if cents else np.zeros((0, self.batch * self.h, self.d), F32))
+
     def materialize_window(self, query_positions=None, context_window=None, current_position=None,
-                           cold_hits: Optional[set] = None, used_router: bool = False):
+                           cold_hits: Optional[set] = None, used_router: bool = False,
+                           routed_chunks: Optional[Sequence[int]] = None):
         """cache.py:344-393 — dense fp16 window [B, W, H, D] in position order + stats.
 
         Sparse residuals (an extension) are added in fp32 and the sum is rounded
@@ -575,7 +586,7 @@ class OracleCache:
                     stats["warm_chunk_decodes"] += 1
         for meta in self.cold:  # cache.py:293-342
             ov = _overlap(start, end, meta["start_token"], meta["end_token"])
-            if ov is None:
+            if ov is None or (routed_chunks is not None and meta["chunk_id"] not in routed_chunks):
                 continue
             if used_router:
                 if cold_hits is not None and meta["chunk_id"] in cold_hits:
@@ -604,9 +615,11 @@ class OracleCache:
         return keys, vals, adjusted
 
     def attention_forward(self, q: np.ndarray, causal=True, query_positions=None, context_window=None,
-                          current_position=None) -> np.ndarray:
-        """cache.py:395-428 — q [B, Q, Hq, D] (one query set per sequence)."""
-        keys, vals, adjusted = self.materialize_window(query_positions, context_window, current_position)
+                          current_position=None, routed_chunks: Optional[Sequence[int]] = None) -> np.ndarray:
+        """cache.py:395-428 — q [B, Q, Hq, D] (one query set per sequence).  routed_chunks
+        (centroid routing, extension): only these cold chunks enter the window."""
+        keys, vals, adjusted = self.materialize_window(query_positions, context_window, current_position,
+                                                       routed_chunks=routed_chunks)
         self.last_access_stats["query_tokens"] = int(q.shape[1])
         if keys.shape[1] == 0:
             return np.zeros_like(q)
@@ -630,6 +643,20 @@ def router_candidates(existing_chunk_ids: Sequence[int], current_position: int, 
     cands = [c for c in range(start_chunk, end_chunk + 1) if c in existing]
     cands.sort(key=lambda c: abs(c * cs - current_position))
     return cands[:top_k]
+
+
+def route_topk(q: np.ndarray, centroids: np.ndarray, kv_heads: int, k: int) -> Tuple[np.ndarray, np.ndarray]:
+    """Centroid routing (extension, rfsn_route_topk): q [B, Q, Hq, D], centroids fp32 [C, B * Hkv, D].
+    score[c] = max over (b, i, h) of q[b, i, h] . centroids[c, b * Hkv + h // G] in fp32; returns
+    (the k highest-scoring chunk indices, descending, ties to the lower index; scores [C])."""
+    b_, nq, hq, d = q.shape
+    g = hq // kv_heads
+    cent = centroids.astype(F32).reshape(centroids.shape[0], b_, kv_heads, d)
+    cent = np.repeat(cent, g, axis=2)                                  # [C, B, Hq, D]
+    dots = np.einsum("bihd,cbhd->cbih", q.astype(F32), cent)           # [C, B, Q, Hq]
+    scores = dots.reshape(centroids.shape[0], -1).max(axis=1).astype(F32)
+    order = np.lexsort((np.arange(scores.shape[0]), -scores))          # descending, ties to lower index
+    return order[:k], scores
 
 
 def centroid_router_scores(q: np.ndarray, chunk_centroids: np.ndarray) -> np.ndarray:

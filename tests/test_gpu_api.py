@@ -185,6 +185,59 @@ def test_cache_extensions_vs_oracle(tmp_path, policy):
     cache.close()
 
 
+@pytest.mark.parametrize("policy", ["recent", "prefix"])
+def test_centroid_routed_cold_tier_vs_oracle(tmp_path, policy):
+    """Centroid routing (extension): each step attends hot + warm + the top-4 cold chunks by
+    mean-key score, prefetched on the router's stream into a 5-slot pool (smaller than the
+    12 cold chunks, so steps copy chunks in).  The chosen chunks equal the oracle's choice
+    except where two scores tie to fp32 rounding, and the output equals the oracle's
+    attention over the same routed window."""
+    rng = np.random.default_rng(23)
+    kw = dict(hidden_dim=512, num_heads=8, head_dim=64, num_subspaces=16, subspace_dim=4, num_rvq_layers=1,
+              rvq_codebook_size=256, rvq_sparsity_threshold=-1.0, hot_capacity=32, warm_capacity=64,
+              block_size_seq=32, num_kv_heads=2, sparse_topk=8, hot_policy=policy)
+    cfg = RFSNConfig(batch_size=2, disk_cache_dir=str(tmp_path), cold_routing="centroid", cold_route_top_k=4,
+                     cold_pool_chunks=5, prefetch_throttle_s=0.0, **kw)
+    pq = (rng.standard_normal((16, 256, 4)) * 0.7).astype(np.float16)
+    rvq = (rng.standard_normal((1, 256, 64)) * 0.3).astype(np.float16)
+    oc = R.OracleCache(R.OracleConfig(**kw), R.Quantizer(pq, rvq, -1.0, sparse_topk=8), batch=2)
+    qz = HybridQuantizerMLX(cfg)
+    qz.pq.codebooks, qz.rvq.codebooks = torch.from_numpy(pq).cuda(), torch.from_numpy(rvq).cuda()
+    cache = RFSNv10KVCacheMLX(cfg, layer_idx=2)
+    router = AsyncHierarchicalRouterMLX(cfg, layer_idx=2)
+    T = 480
+    walk = np.cumsum(rng.standard_normal((T // 32, 1, 64)) * 0.5, axis=0).repeat(32, axis=0)
+    k = (rng.standard_normal((2, T, 2, 64)) + walk[None]).astype(np.float16)
+    v = rng.standard_normal((2, T, 2, 64)).astype(np.float16)
+    for a in range(0, T, 96):
+        cache.update(torch.from_numpy(k[:, a:a + 96]).cuda(), torch.from_numpy(v[:, a:a + 96]).cuda(), qz)
+        oc.update(k[:, a:a + 96], v[:, a:a + 96])
+    assert (cache.num_hot, cache.num_warm, cache.num_cold) == (oc.num_hot, oc.num_warm, oc.num_cold)
+    assert len(cache.cold_chunk_metadata) == 12
+    ids, cent = oc.chunk_centroids()
+    misses = 0
+    for step in range(6):
+        q = (rng.standard_normal((2, 8, 64)) * (1 + step)).astype(np.float16)
+        out = cache.attention_forward(torch.from_numpy(q).cuda(), causal=True, router=router,
+                                      current_position=T - 1, context_window=T)
+        chosen = cache.last_routed_chunks
+        st = cache.get_last_access_stats()
+        assert st["cold_chunks_touched"] == 4
+        assert st["cold_chunk_cache_hits"] + st["cold_chunk_cache_misses"] == 4
+        misses += st["cold_chunk_cache_misses"]
+        sel, scores = R.route_topk(q[:, None], cent, 2, 4)
+        want = [ids[i] for i in sel]
+        if set(chosen) != set(want):  # only fp32 ties may swap: the scores at the boundary agree closely
+            got_s = sorted(scores[ids.index(c)] for c in chosen)
+            want_s = sorted(scores[i] for i in sel)
+            np.testing.assert_allclose(got_s, want_s, rtol=1e-5, atol=1e-5)
+        ref = oc.attention_forward(q[:, None], causal=True, context_window=T, current_position=T - 1,
+                                   routed_chunks=chosen)
+        close(out.cpu().numpy(), ref[:, 0], f"step {step}")
+    assert misses >= 4  # the first step finds an empty pool
+    cache.close()
+
+
 def test_quantizer_api_golden():
     """HybridQuantizerMLX encode/decode and the compressed-tensor helpers vs reference vectors."""
     g = dict(np.load(GOLDEN / "quant_d128_m8x16_rvq3.npz"))
