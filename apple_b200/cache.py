@@ -242,7 +242,11 @@ class RFSNv10KVCacheMLX:
     def _ensure_cold(self, disk_dir: Optional[Path]) -> ColdTier:
         root = Path(self.config.disk_cache_dir) if disk_dir is None else Path(disk_dir)
         if self._cold is None:
-            self._cold = ColdTier(self._qz, self.rows, self.chunk_tokens, self.config.cold_pool_chunks, self.device)
+            # the reference's merges can make a prefix-policy chunk up to 2 * chunk_tokens - 1 long
+            cap = 2 * self.chunk_tokens if self.policy == "prefix" else self.chunk_tokens
+            self._cold = ColdTier(self._qz, self.rows, self.chunk_tokens, self.config.cold_pool_chunks, self.device,
+                                  spill_dir=root, layer_idx=self.layer_idx, host_chunks=self.config.cold_host_chunks,
+                                  capacity=cap)
             self._cold.track_centroids = self.config.cold_routing == "centroid"
             self._cold_root = root
             register_cold_tier(root, self.layer_idx, self._cold)
@@ -327,7 +331,9 @@ class RFSNv10KVCacheMLX:
             meta["num_tokens"] += n
 
     def _add_to_cold(self, k, v, disk_dir) -> None:
-        """cache.py:134-191: chunk id = start // chunk, contiguous merge into partial chunks."""
+        """cache.py:134-191: the appended tokens in pieces of chunk_tokens from the update's start;
+        a piece's chunk id = its start // chunk_tokens, and a piece whose id exists is merged onto
+        that chunk (which must end where the piece starts)."""
         tier = self._ensure_cold(disk_dir)
         ct = self.chunk_tokens
         start_token = self.num_hot + self.num_warm + self.num_cold
@@ -341,12 +347,14 @@ class RFSNv10KVCacheMLX:
             if chunk is not None and pos != chunk.end_token:
                 raise ValueError("Cold chunk append must be contiguous with existing metadata: "
                                  f"chunk_id={cid} start={pos} expected={chunk.end_token}")
-            within = pos - cid * ct if chunk is None else chunk.end_token - chunk.start_token
-            take = min(n - off, ct - within) if chunk is not None else min(n - off, ct)
+            take = min(n - off, ct)  # the reference's piece (cache.py:146-149)
             if chunk is None:
                 chunk = tier.new_chunk(cid, pos)
                 within = 0
-            elif within:
+            else:
+                within = chunk.end_token - chunk.start_token
+                if within + take > tier.capacity:
+                    raise ValueError(f"cold chunk {cid} would hold {within + take} tokens (capacity {tier.capacity})")
                 tier.load_stage(chunk, stream)  # keep the chunk's earlier tokens in the image
             self._encode_kv(k[:, off:off + take], v[:, off:off + take], tier.stage, 0, within)
             tier.store_stage(chunk, stream, num_tokens=within + take)
@@ -680,23 +688,22 @@ class RFSNv10KVCacheMLX:
                 "cold_chunks": len(self.cold_chunk_paths), "cold_tokens": self.num_cold}
 
     def load_cold_chunk(self, chunk_id: int) -> Dict[str, np.ndarray]:
-        """cache.py:193-194: the chunk's codes (host arrays) by id; KeyError for unknown ids."""
+        """cache.py:193-194: the chunk's codes by id, as the arrays of its chunk file
+        (storage.py:117-135, apple_b200/chunk_io.py); KeyError for unknown ids."""
+        from .chunk_io import _arrays, load_compressed_chunk
+        from .storage import CompressedTensorMLX
         if self._cold is None or chunk_id not in self._cold.chunks:
             raise KeyError(chunk_id)
         c = self._cold.chunks[chunk_id]
+        if c.store is None:
+            return load_compressed_chunk(c.spill_path)
         if c.ready is not None:
             c.ready.synchronize()
         n = c.num_tokens
-        out = {"num_tokens": np.array([n], np.int32), "num_heads": np.array([self.heads], np.int32)}
-        for kv, name in ((0, "key"), (1, "value")):
-            out[f"{name}_pq_codes"] = c.store.read_rows(kv, "pq", 0, 0, n).numpy().copy()
-            if self._qz.L:
-                out[f"{name}_rvq"] = c.store.read_rows(kv, "rvq", 0, 0, n).numpy().copy()
-                out[f"{name}_rvq_mask"] = c.store.read_rows(kv, "active", 0, 0, n)[..., 0].numpy().astype(bool)
-            if self._qz.sparse_topk:
-                out[f"{name}_sp_idx"] = c.store.read_rows(kv, "sp_idx", 0, 0, n).numpy().copy()
-                out[f"{name}_sp_val"] = c.store.read_rows(kv, "sp_val", 0, 0, n).numpy().copy()
-        return out
+        keys = CompressedTensorMLX.from_store(c.store, 0, 0, 0, n, self.rows)
+        values = CompressedTensorMLX.from_store(c.store, 1, 0, 0, n, self.rows)
+        return {"num_tokens": np.array([n], np.int32), "num_heads": np.array([self.rows], np.int32),
+                **_arrays(keys, "key"), **_arrays(values, "value")}
 
     def close(self) -> None:
         if self._cold_root is not None:

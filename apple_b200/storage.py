@@ -48,6 +48,9 @@ class RFSNConfig:
                         reads only the cold_route_top_k chunks whose mean key scores highest
                         against the step's queries (rfsn_route_topk).
       cold_route_top_k  chunks a centroid-routed step attends (at most 64).
+      cold_host_chunks  chunk images kept in pinned host memory (None = all); beyond it the
+                        least recently used chunks spill to layer{L}_chunk{id}.npz files in
+                        the reference's format under disk_cache_dir and come back on use.
       device            CUDA device of the cache and quantizer.
     """
 
@@ -89,6 +92,7 @@ class RFSNConfig:
     cold_pool_chunks: int = 32
     cold_routing: str = "exact"
     cold_route_top_k: int = 8
+    cold_host_chunks: Optional[int] = None
     device: str = "cuda"
 
     def __post_init__(self) -> None:
@@ -104,6 +108,8 @@ class RFSNConfig:
             raise ValueError("cold_routing must be 'exact' or 'centroid'")
         if not 1 <= self.cold_route_top_k <= 64:
             raise ValueError("cold_route_top_k must be in [1, 64]")
+        if self.cold_host_chunks is not None and self.cold_host_chunks < 1:
+            raise ValueError("cold_host_chunks must be at least 1 (or None: every chunk stays in host memory)")
         if self.num_kv_heads is not None and self.num_heads % self.num_kv_heads:
             raise ValueError("num_heads must be a multiple of num_kv_heads")
         if self.hot_policy == "recent" and self.chunk_tokens % 16:
@@ -244,9 +250,10 @@ class ColdChunk:
     chunk_id: int
     start_token: int
     end_token: int
-    store: K.CodeStoreBuffers  # pinned host, one slot: K and V codes of every row, chunk_tokens tokens
+    store: Optional[K.CodeStoreBuffers]  # pinned host, one slot: K and V codes of every row (None: spilled)
     ready: Optional[torch.cuda.Event] = None  # device-to-host writes into `store` done
     version: int = 0
+    spill_path: Optional[Path] = None  # set while the chunk lives only in its NPZ file
 
     @property
     def num_tokens(self) -> int:
@@ -263,15 +270,26 @@ class ColdTier:
     (rfsn_cold_prefetch / rfsn_cold_evict).
     """
 
-    def __init__(self, qz: K.QuantizerBuffers, rows: int, chunk_tokens: int, slots: int, device):
+    def __init__(self, qz: K.QuantizerBuffers, rows: int, chunk_tokens: int, slots: int, device,
+                 spill_dir: Optional[Path] = None, layer_idx: int = 0, host_chunks: Optional[int] = None,
+                 capacity: Optional[int] = None):
         self.qz = qz
+        # tokens one chunk image holds: chunk_tokens, or more where the reference's merges of a
+        # partial chunk with a whole piece make longer chunks (cache.py:144-176)
+        self.capacity = K.align16(max(chunk_tokens, capacity or chunk_tokens))
+        self.spill_dir = None if spill_dir is None else Path(spill_dir)
+        self.layer_idx = layer_idx
+        self.host_chunks = host_chunks
+        self.host_lru: "OrderedDict[int, None]" = OrderedDict()  # chunks with a pinned image, LRU first
+        self.spills = 0
+        self.unspills = 0
         self.rows = rows
         self.chunk_tokens = chunk_tokens
         self.device = torch.device(device)
         self.chunks: "OrderedDict[int, ColdChunk]" = OrderedDict()
         self.slots = max(1, slots)
-        self.pool = K.CodeStoreBuffers(qz, rows, chunk_tokens, self.slots, device=self.device)
-        self.stage = K.CodeStoreBuffers(qz, rows, chunk_tokens, 1, device=self.device)
+        self.pool = K.CodeStoreBuffers(qz, rows, self.capacity, self.slots, device=self.device)
+        self.stage = K.CodeStoreBuffers(qz, rows, self.capacity, 1, device=self.device)
         self.slot_of: "OrderedDict[int, int]" = OrderedDict()  # chunk id -> slot (LRU order)
         self.slot_version: Dict[int, int] = {}
         self.slot_ready: Dict[int, torch.cuda.Event] = {}
@@ -290,14 +308,61 @@ class ColdTier:
         return self.stage.nbytes_per_slot()
 
     # -- host side -------------------------------------------------------
+    def _pinned_store(self) -> K.CodeStoreBuffers:
+        return K.CodeStoreBuffers(self.qz, self.rows, self.capacity, 1, pin_memory=True)
+
     def new_chunk(self, chunk_id: int, start: int) -> ColdChunk:
-        c = ColdChunk(chunk_id, start, start, K.CodeStoreBuffers(self.qz, self.rows, self.chunk_tokens, 1,
-                                                                 pin_memory=True))
+        c = ColdChunk(chunk_id, start, start, self._pinned_store())
         self.chunks[chunk_id] = c
+        self.host_lru[chunk_id] = None
         return c
+
+    # -- NPZ spill below the pinned tier ----------------------------------
+    def _spill_one(self, keep: set) -> bool:
+        """Write the least recently used pinned image (not in keep) to its NPZ file and free it."""
+        from .chunk_io import store_to_npz
+        for cid in self.host_lru:
+            if cid in keep:
+                continue
+            c = self.chunks[cid]
+            if c.ready is not None:
+                c.ready.synchronize()  # the image's device-to-host copy is complete
+            path = chunk_file_path(self.spill_dir, self.layer_idx, cid)
+            store_to_npz(c.store, c.num_tokens, path)
+            c.store = None
+            c.spill_path = path
+            del self.host_lru[cid]
+            self.spills += 1
+            return True
+        return False
+
+    def enforce_host_limit(self, keep: set = frozenset()) -> None:
+        if self.host_chunks is None or self.spill_dir is None:
+            return
+        while len(self.host_lru) > self.host_chunks and self._spill_one(set(keep)):
+            pass
+
+    def host_image(self, chunk: ColdChunk, keep: set = frozenset()) -> K.CodeStoreBuffers:
+        """The chunk's pinned image, read back from its NPZ file if it was spilled."""
+        if chunk.store is None:
+            from .chunk_io import npz_to_store
+            st = self._pinned_store()
+            n = npz_to_store(chunk.spill_path, st)
+            if n != chunk.num_tokens:
+                raise ValueError(f"{chunk.spill_path}: {n} tokens, the chunk has {chunk.num_tokens}")
+            chunk.store = st
+            chunk.spill_path = None
+            chunk.ready = None
+            self.unspills += 1
+            self.host_lru[chunk.chunk_id] = None
+            self.enforce_host_limit(set(keep) | {chunk.chunk_id})
+        else:
+            self.host_lru.move_to_end(chunk.chunk_id)
+        return chunk.store
 
     def load_stage(self, chunk: ColdChunk, stream: torch.cuda.Stream) -> K.CodeStoreBuffers:
         """Bring a chunk's current image into the device stage (for a partial-chunk append)."""
+        self.host_image(chunk)
         if chunk.ready is not None:
             stream.wait_event(chunk.ready)
         K.call("rfsn_cold_prefetch", self.stage.data.data_ptr(), chunk.store.data.data_ptr(), self.image_bytes,
@@ -318,6 +383,8 @@ class ColdTier:
         chunk.ready = ev
         chunk.version += 1
         self.invalidate(chunk.chunk_id)
+        self.host_lru.move_to_end(chunk.chunk_id)
+        self.enforce_host_limit({chunk.chunk_id})
 
     def set_centroid(self, chunk_id: int, num_tokens: int, stream: torch.cuda.Stream) -> None:
         """Mean of the stage's decoded keys over its first num_tokens tokens, per row, in fp32."""
@@ -347,7 +414,7 @@ class ColdTier:
     # -- device pool ------------------------------------------------------
     def _grow(self, need: int) -> None:
         new_slots = max(need, self.slots * 2)
-        new = K.CodeStoreBuffers(self.qz, self.rows, self.chunk_tokens, new_slots, device=self.device)
+        new = K.CodeStoreBuffers(self.qz, self.rows, self.capacity, new_slots, device=self.device)
         new.data[: self.slots].copy_(self.pool.data)
         self.pool = new
         self.slots = new_slots
@@ -380,6 +447,7 @@ class ColdTier:
                 self.slot_of.move_to_end(chunk_id)
                 return self.slot_of[chunk_id]
             chunk = self.chunks[chunk_id]
+            self.host_image(chunk, set(keep) | {chunk_id})
             slot = self._free_slot(set(keep) | {chunk_id})
             if chunk.ready is not None:
                 stream.wait_event(chunk.ready)

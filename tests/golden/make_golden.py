@@ -320,6 +320,39 @@ def case_gqa_batch(ref, name, seed, batch=3, kv_heads=2, group=4, n_tokens=60, q
         shutil.rmtree(tmp, ignore_errors=True)
 
 
+def case_chunk_files(ref, name, seed, n_tokens=70, split=44):
+    """Cold chunk files written by the reference cache itself (cache.py:134-191 through
+    save_compressed_chunk, storage.py:117-135), copied to tests/golden/<name>/ beside an index
+    of the inputs that made them.  The first update leaves a 4-token partial chunk; the second
+    update's first 16-token piece merges onto it (a 20-token chunk), its rest opens the next."""
+    mx = sys.modules["mlx.core"]
+    rng = np.random.default_rng(seed)
+    tmp = Path(tempfile.mkdtemp(prefix="rfsn_chunks_"))
+    try:
+        config = make_config(ref, hidden_dim=256, num_heads=4, head_dim=64, num_subspaces=16, subspace_dim=4,
+                             num_rvq_layers=1, rvq_sparsity_threshold=0.4, disk_cache_dir=str(tmp))
+        pq_cb, rvq_cb = seeded_codebooks(rng, 16, 256, 4, 1, 256, 64)
+        hq = make_quantizer(ref, config, pq_cb, rvq_cb)
+        keys = rng.standard_normal((n_tokens, 4, 64)).astype(np.float16)
+        values = rng.standard_normal((n_tokens, 4, 64)).astype(np.float16)
+        cache = ref["cache"].RFSNv10KVCacheMLX(config, layer_idx=0)
+        cache.update(mx.array(keys[:split]), mx.array(values[:split]), hq, disk_dir=tmp)
+        cache.update(mx.array(keys[split:]), mx.array(values[split:]), hq, disk_dir=tmp)
+        outdir = OUT / name
+        if outdir.exists():
+            shutil.rmtree(outdir)
+        outdir.mkdir()
+        meta = cache.cold_chunk_metadata
+        for m in meta:
+            shutil.copy(m["path"], outdir / Path(m["path"]).name)
+        np.savez_compressed(outdir / "index.npz", keys=keys, values=values, pq_codebooks=pq_cb, rvq_codebooks=rvq_cb,
+                            threshold=np.float32(0.4), update_split=np.int32(split),
+                            chunk_ids=np.array([m["chunk_id"] for m in meta], np.int32),
+                            chunk_bounds=np.array([[m["start_token"], m["end_token"]] for m in meta], np.int32))
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+
+
 CASES = {
     "quant": lambda ref: (
         case_quantizer(ref, "quant_d128_m8x16_rvq3", seed=11, cfg_kw={}, n=96, scale_half=0.01),
@@ -339,6 +372,7 @@ CASES = {
     "layer": lambda ref: case_decoder_layer(ref, "decoder_layer", seed=41),
     "calibration": lambda ref: case_calibration(ref, "calibration_kmeans", seed=51),
     "gqa_batch": lambda ref: case_gqa_batch(ref, "gqa_batch_cache", seed=61),
+    "chunk_files": lambda ref: case_chunk_files(ref, "ref_chunks", seed=71),
 }
 
 

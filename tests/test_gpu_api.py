@@ -238,6 +238,84 @@ def test_centroid_routed_cold_tier_vs_oracle(tmp_path, policy):
     cache.close()
 
 
+def _ref_chunk_cache(tmp_path, spill):
+    idx = dict(np.load(GOLDEN / "ref_chunks" / "index.npz"))
+    cfg = RFSNConfig(hidden_dim=256, num_heads=4, head_dim=64, num_subspaces=16, subspace_dim=4, num_rvq_layers=1,
+                     rvq_codebook_size=256, rvq_sparsity_threshold=0.4, hot_capacity=16, warm_capacity=24,
+                     block_size_seq=16, prefetch_throttle_s=0.0, disk_cache_dir=str(tmp_path), cold_host_chunks=spill)
+    qz = golden_quantizer(cfg, idx)
+    cache = RFSNv10KVCacheMLX(cfg, layer_idx=0)
+    s = int(idx["update_split"])
+    for a, b in ((0, s), (s, idx["keys"].shape[0])):
+        cache.update(torch.from_numpy(idx["keys"][a:b]).cuda(), torch.from_numpy(idx["values"][a:b]).cuda(), qz)
+    return idx, cache
+
+
+def test_cold_tier_spills_to_reference_chunk_files(tmp_path):
+    """cold_host_chunks=1 keeps one chunk image in pinned memory and spills the other to its
+    layer0_chunk{id}.npz file: the files and load_cold_chunk hold exactly what the reference
+    cache wrote for the same tokens (the 20-token merged chunk included), and attention over
+    every tier equals the non-spilling cache's and the oracle's."""
+    idx, full = _ref_chunk_cache(tmp_path / "full", None)
+    _, sp = _ref_chunk_cache(tmp_path / "spill", 1)
+    assert [[m["start_token"], m["end_token"]] for m in sp.cold_chunk_metadata] == idx["chunk_bounds"].tolist()
+    assert sp._cold.spills >= 1
+    files = 0
+    for cid in idx["chunk_ids"]:
+        ref = np.load(GOLDEN / "ref_chunks" / f"layer0_chunk{int(cid)}.npz")
+        written = tmp_path / "spill" / f"layer0_chunk{int(cid)}.npz"
+        got = [sp.load_cold_chunk(int(cid)), full.load_cold_chunk(int(cid))]
+        if written.exists():
+            files += 1
+            got.append(dict(np.load(written)))
+        for d in got:
+            assert sorted(d) == sorted(ref.files)
+            for k in ref.files:
+                np.testing.assert_array_equal(d[k], ref[k], err_msg=k)
+    assert files >= 1
+    oc = R.OracleCache(R.OracleConfig(hidden_dim=256, num_heads=4, head_dim=64, num_subspaces=16, subspace_dim=4,
+                                      num_rvq_layers=1, rvq_codebook_size=256, rvq_sparsity_threshold=0.4,
+                                      hot_capacity=16, warm_capacity=24, block_size_seq=16),
+                       R.Quantizer(idx["pq_codebooks"], idx["rvq_codebooks"], 0.4))
+    s = int(idx["update_split"])
+    oc.update(idx["keys"][None, :s], idx["values"][None, :s])
+    oc.update(idx["keys"][None, s:], idx["values"][None, s:])
+    q = np.random.default_rng(5).standard_normal((1, 4, 64)).astype(np.float16)
+    for pos, win in ((69, None), (55, 30), (45, 10)):
+        a = full.attention_forward(torch.from_numpy(q).cuda(), query_positions=[pos], context_window=win)
+        b = sp.attention_forward(torch.from_numpy(q).cuda(), query_positions=[pos], context_window=win)
+        assert torch.equal(a, b), (pos, win)
+        ref = oc.attention_forward(q[None], query_positions=[pos], context_window=win)
+        close(b.cpu().numpy(), ref[0], f"position {pos} window {win}")
+    assert sp._cold.unspills >= 1  # attention brought a spilled chunk back from its file
+    full.close()
+    sp.close()
+
+
+def test_reference_chunk_file_into_device_store():
+    """A chunk file written by the reference, read into a device code store, decodes on the GPU
+    bit-exactly as the oracle decodes the file's codes."""
+    from apple_b200.chunk_io import load_compressed_chunk, npz_to_store
+    from apple_b200 import kernels as K
+    idx = dict(np.load(GOLDEN / "ref_chunks" / "index.npz"))
+    qz = K.QuantizerBuffers(torch.from_numpy(idx["pq_codebooks"]).cuda(), torch.from_numpy(idx["rvq_codebooks"]).cuda(),
+                            0.4, 0)
+    oq = R.Quantizer(idx["pq_codebooks"], idx["rvq_codebooks"], 0.4)
+    path = GOLDEN / "ref_chunks" / f"layer0_chunk{int(idx['chunk_ids'][0])}.npz"
+    st = K.CodeStoreBuffers(qz, rows=4, cap=32)
+    n = npz_to_store(path, st)
+    f = load_compressed_chunk(path)
+    for kv, prefix in ((0, "key"), (1, "value")):
+        mask = f[f"{prefix}_rvq_mask"]
+        rvq = np.zeros((n * 4, 1), np.uint16)
+        rvq[f[f"{prefix}_rvq_offsets"]] = f[f"{prefix}_rvq_codes"]
+        codes = R.Codes(f[f"{prefix}_pq_codes"], rvq.reshape(n, 4, 1), mask, np.zeros((n, 4, 0), np.uint8),
+                        np.zeros((n, 4, 0), np.float16))
+        out = torch.empty((1, n, 4, 64), dtype=torch.float16, device="cuda")
+        K.decode_codes(qz, st, 0, 0, n, out, kv=kv)
+        np.testing.assert_array_equal(u16(out[0]), u16(oq.decode(codes)))
+
+
 def test_quantizer_api_golden():
     """HybridQuantizerMLX encode/decode and the compressed-tensor helpers vs reference vectors."""
     g = dict(np.load(GOLDEN / "quant_d128_m8x16_rvq3.npz"))
