@@ -472,6 +472,72 @@ def add_rms_norm(x: torch.Tensor, b: torch.Tensor, weight: torch.Tensor,
     return s, y
 
 
+def llama_rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float,
+                   residual: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """The Llama adapter's RMSNorm (rfsn_llama_rmsnorm_f16): fp16 x [..., dim] and an fp16 weight.
+    With ``residual``, normalises s = fp16(x + residual) and returns (y, s); else (y, None)."""
+    _need_cuda(x, "x")
+    if x.dtype != torch.float16 or weight.dtype != torch.float16 or weight.numel() != x.shape[-1]:
+        raise ValueError("llama_rms_norm expects fp16 x [..., dim] and an fp16 weight of dim")
+    x = x.contiguous()
+    w = weight.contiguous()
+    y = torch.empty_like(x)
+    s = None
+    if residual is not None:
+        if residual.shape != x.shape or residual.dtype != torch.float16:
+            raise ValueError("residual must be fp16 like x")
+        residual = residual.contiguous()
+        s = torch.empty_like(x)
+    dim = int(x.shape[-1])
+    call("rfsn_llama_rmsnorm_f16", _ptr(x), _ptr(residual), _ptr(s), _ptr(w), _ptr(y), x.numel() // dim, dim,
+         float(eps), _stream(x.device.index))
+    return y, s
+
+
+def rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Rotary embedding of fp16 x [B, S, H, D] (any strides, D contiguous) with fp16 tables [S, D]
+    (rfsn_rope_f16); out defaults to a new contiguous tensor (it may be x itself)."""
+    _need_cuda(x, "x")
+    B, S, H, D = x.shape
+    if x.dtype != torch.float16 or x.stride(-1) != 1:
+        raise ValueError("rope expects fp16 [B, S, H, D] with a contiguous last dim")
+    cos = cos.to(device=x.device, dtype=torch.float16).reshape(S, D).contiguous()
+    sin = sin.to(device=x.device, dtype=torch.float16).reshape(S, D).contiguous()
+    y = torch.empty((B, S, H, D), dtype=torch.float16, device=x.device) if out is None else out
+    if y.shape != x.shape or y.stride(-1) != 1 or y.dtype != torch.float16:
+        raise ValueError("out must be fp16 like x with a contiguous last dim")
+    call("rfsn_rope_f16", _ptr(x), x.stride(0), x.stride(1), x.stride(2), _ptr(y), y.stride(0), y.stride(1),
+         y.stride(2), _ptr(cos), _ptr(sin), B, S, H, D, _stream(x.device.index))
+    return y
+
+
+def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """fp16(fp16(g * sigmoid(g)) * up) in one launch (rfsn_silu_mul_f16)."""
+    _need_cuda(gate, "gate")
+    if gate.dtype != torch.float16 or up.dtype != torch.float16 or gate.shape != up.shape:
+        raise ValueError("silu_mul expects fp16 gate and up of one shape")
+    gate, up = gate.contiguous(), up.contiguous()
+    y = torch.empty_like(gate)
+    call("rfsn_silu_mul_f16", _ptr(gate), _ptr(up), _ptr(y), gate.numel(), _stream(gate.device.index))
+    return y
+
+
+def affine_quantize(w: torch.Tensor, bits: int, group: int):
+    """Affine quantization of fp32 w [rows, cols] in groups along the last dim
+    (rfsn_affine_quantize_f32) -> (q uint8 [rows, cols], scales, biases fp32 [rows, cols/group],
+    dequantized fp32 [rows, cols])."""
+    _need_cuda(w, "w")
+    w = w.to(torch.float32).contiguous()
+    rows, cols = w.shape
+    q = torch.empty((rows, cols), dtype=torch.uint8, device=w.device)
+    sc = torch.empty((rows, cols // group), dtype=torch.float32, device=w.device)
+    bi = torch.empty_like(sc)
+    deq = torch.empty_like(w)
+    call("rfsn_affine_quantize_f32", _ptr(w), rows, cols, group, bits, _ptr(q), _ptr(sc), _ptr(bi), _ptr(deq),
+         _stream(w.device.index))
+    return q, sc, bi, deq
+
+
 def gelu_tanh(x: torch.Tensor) -> torch.Tensor:
     """Tanh-approximate GELU of fp16 x in one launch, rounded to fp16 after every operation."""
     _need_cuda(x, "x")

@@ -77,6 +77,32 @@ def _choose_group_size(last_dim: int, preferred: int) -> Optional[int]:
     return None
 
 
+def _quantize_matrix(matrix: torch.Tensor, bits: int, preferred_group_size: int) -> Optional[QuantizedMatrix]:
+    """quantization.py:36-76: affine quantization of a 2-D codebook in groups along its last
+    dim (the first of the preferred, 128, 64, 32 sizes that divides it; else along the other
+    dim, transposed), by rfsn_affine_quantize_f32.  None when no group size fits."""
+    if matrix.dim() != 2:
+        return None
+    shape = tuple(int(d) for d in matrix.shape)
+    cand = matrix.to(torch.float32)
+    transposed = False
+    group = _choose_group_size(int(cand.shape[-1]), preferred_group_size)
+    if group is None:
+        cand = cand.transpose(0, 1)
+        group = _choose_group_size(int(cand.shape[-1]), preferred_group_size)
+        if group is None:
+            return None
+        transposed = True
+    q, scales, biases, deq = K.affine_quantize(cand.contiguous(), bits, group)
+    return QuantizedMatrix(q, scales, biases, bits, group, transposed, shape,
+                           deq.transpose(0, 1).contiguous() if transposed else deq)
+
+
+def _dequantize_matrix(matrix: QuantizedMatrix, dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """quantization.py:79-89: q * scale + bias in the original orientation, as dtype."""
+    return matrix.dequantized.to(dtype)
+
+
 class ProductQuantizerMLX:
     """Product quantizer (quantization.py:99-175): codebooks fp16 [M, 2^pq_bits, ds]."""
 
@@ -91,8 +117,21 @@ class ProductQuantizerMLX:
         self.codebooks = cb.to(torch.float16).to(_device(config))
         self._ane_codebooks: List[Optional[QuantizedMatrix]] = [None] * self.num_subspaces
 
+    def effective_codebooks(self) -> torch.Tensor:
+        """The codebooks the kernels read: the dequantized affine codebook of every subspace that
+        quantize_codebooks_for_ane quantized (quantization.py:118-122), the fp16 codebook
+        elsewhere.  The B200 path carries codebooks in fp16, so the dequantized values are
+        rounded to fp16 for encoding as well as decoding (the reference encodes with them in
+        fp32)."""
+        if not any(m is not None for m in self._ane_codebooks):
+            return self.codebooks
+        parts = [_dequantize_matrix(m, torch.float16) if m is not None else self.codebooks[i].to(torch.float16)
+                 for i, m in enumerate(self._ane_codebooks)]
+        return torch.stack(parts).contiguous()
+
     def _buffers(self) -> K.QuantizerBuffers:
-        return K.QuantizerBuffers(_as_half_cuda(self.codebooks, _device(self.config)), None, float("inf"), 0)
+        return K.QuantizerBuffers(_as_half_cuda(self.effective_codebooks(), _device(self.config)), None,
+                                  float("inf"), 0)
 
     def quantize(self, vectors: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
         """quantization.py:124-144 -> (codes uint8 [N, M], residual fp16 [N, D])."""
@@ -120,8 +159,14 @@ class ProductQuantizerMLX:
         return out.view(n, qz.D)
 
     def quantize_codebooks_for_ane(self) -> Dict[str, int]:
-        """quantization.py:159-175: Apple-specific 6-bit affine codebooks; not part of the B200 path."""
-        return {"quantized_subspaces": 0, "total_subspaces": self.num_subspaces}
+        """quantization.py:159-175: affine ane_quant_bits-bit codebooks (group ane_group_size)."""
+        quantized = 0
+        for m in range(self.num_subspaces):
+            packed = _quantize_matrix(self.codebooks[m], self.config.ane_quant_bits, self.config.ane_group_size)
+            self._ane_codebooks[m] = packed
+            quantized += packed is not None
+        logger.info("PQ codebook fast path prepared for %d/%d subspaces", quantized, self.num_subspaces)
+        return {"quantized_subspaces": quantized, "total_subspaces": self.num_subspaces}
 
 
 class ResidualVQMLX:
@@ -142,9 +187,17 @@ class ResidualVQMLX:
         self.codebooks = cb.to(_device(config))
         self._ane_codebooks: List[Optional[QuantizedMatrix]] = [None] * self.num_layers
 
+    def effective_codebooks(self) -> torch.Tensor:
+        """As ProductQuantizerMLX.effective_codebooks, per RVQ layer (quantization.py:200-204)."""
+        if not any(m is not None for m in self._ane_codebooks):
+            return self.codebooks
+        parts = [_dequantize_matrix(m, torch.float16) if m is not None else self.codebooks[i].to(torch.float16)
+                 for i, m in enumerate(self._ane_codebooks)]
+        return torch.stack(parts).contiguous()
+
     def _buffers(self) -> K.QuantizerBuffers:
         dev = _device(self.config)
-        return K.QuantizerBuffers(_zero_pq(self.head_dim, dev), _as_half_cuda(self.codebooks, dev),
+        return K.QuantizerBuffers(_zero_pq(self.head_dim, dev), _as_half_cuda(self.effective_codebooks(), dev),
                                   float(self.sparsity_threshold), 0)
 
     def encode(self, residuals: torch.Tensor, base_codes: Optional[torch.Tensor] = None
@@ -188,7 +241,14 @@ class ResidualVQMLX:
         return out.view(n, self.head_dim)
 
     def quantize_codebooks_for_ane(self) -> Dict[str, int]:
-        return {"quantized_layers": 0, "total_layers": self.num_layers}
+        """quantization.py:277-293."""
+        quantized = 0
+        for layer in range(self.num_layers):
+            packed = _quantize_matrix(self.codebooks[layer], self.config.ane_quant_bits, self.config.ane_group_size)
+            self._ane_codebooks[layer] = packed
+            quantized += packed is not None
+        logger.info("RVQ codebook fast path prepared for %d/%d layers", quantized, self.num_layers)
+        return {"quantized_layers": quantized, "total_layers": self.num_layers}
 
 
 class HybridQuantizerMLX:
@@ -206,9 +266,11 @@ class HybridQuantizerMLX:
         """Device description of the current codebooks (rebuilt when they change)."""
         pq, rvq = self.pq.codebooks, self.rvq.codebooks
         key = (id(pq), getattr(pq, "_version", 0), id(rvq), getattr(rvq, "_version", 0),
-               self.config.rvq_sparsity_threshold, self.config.sparse_topk)
+               self.config.rvq_sparsity_threshold, self.config.sparse_topk,
+               tuple(id(m) for m in self.pq._ane_codebooks), tuple(id(m) for m in self.rvq._ane_codebooks))
         if key != self._cache_key:
             dev = _device(self.config)
+            pq, rvq = self.pq.effective_codebooks(), self.rvq.effective_codebooks()
             self._cache_val = K.QuantizerBuffers(_as_half_cuda(pq, dev),
                                                  _as_half_cuda(rvq, dev) if self.config.num_rvq_layers else None,
                                                  float(self.config.rvq_sparsity_threshold),
@@ -241,7 +303,10 @@ class HybridQuantizerMLX:
         return out.view(n, qz.D)
 
     def quantize_codebooks_for_ane(self) -> Dict[str, int]:
-        return {"pq_quantized": 0, "rvq_quantized": 0}
+        """quantization.py:321-327."""
+        pq_report = self.pq.quantize_codebooks_for_ane()
+        rvq_report = self.rvq.quantize_codebooks_for_ane()
+        return {"pq_quantized": pq_report["quantized_subspaces"], "rvq_quantized": rvq_report["quantized_layers"]}
 
 
 def _compress_tensor_sequence(tensor: torch.Tensor, quantizer: HybridQuantizerMLX) -> CompressedTensorMLX:

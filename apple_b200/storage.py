@@ -127,8 +127,9 @@ class RFSNConfig:
 
 @dataclass
 class QuantizedMatrix:
-    """Affine-quantised 2-D tensor (storage.py:62-72).  Kept for API parity; the
-    Apple-specific 6-bit codebook path is not part of the B200 build."""
+    """Affine-quantised 2-D tensor (storage.py:62-72).  weights holds one code per byte (uint8,
+    the B200 build's layout; MLX packs them into uint32 words); scales and biases are fp32 per
+    group; dequantized caches q * scale + bias (fp32, in the original orientation)."""
     weights: torch.Tensor
     scales: torch.Tensor
     biases: torch.Tensor
@@ -136,6 +137,7 @@ class QuantizedMatrix:
     group_size: int
     transposed: bool
     original_shape: Tuple[int, ...]
+    dequantized: Optional[torch.Tensor] = None
 
 
 class CompressedTensorMLX:

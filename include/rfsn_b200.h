@@ -248,6 +248,37 @@ int rfsn_gelu_tanh_f16(const uint16_t* x, uint16_t* y, int64_t n, void* stream);
 int rfsn_add_rmsnorm_f16(const uint16_t* x, const uint16_t* b, uint16_t* sum, const float* weight, uint16_t* y,
                          int64_t rows, int dim, float eps, void* stream);
 
+/* Affine low-bit codebook quantization — the reference's quantize_codebooks_for_ane path
+ * (_quantize_matrix / _dequantize_matrix, quantization.py:36-89, used at :159-175 and :277-293),
+ * which calls MLX's mx.quantize / mx.dequantize (affine mode).  For each group of `group`
+ * consecutive elements of a row of w (fp32 [rows][cols], cols % group == 0, group <= 128):
+ * scale = (max - min) / (2^bits - 1), bias = min, q = clip(round_half_even((w - bias) / scale),
+ * 0, 2^bits - 1) and dequantized = q * scale + bias, all fp32 (a constant group: scale 0, q 0).
+ * Outputs: q uint8 [rows][cols], scales and biases fp32 [rows][cols / group], dequantized fp32
+ * [rows][cols]. */
+int rfsn_affine_quantize_f32(const float* w, int64_t rows, int cols, int group, int bits, uint8_t* q, float* scales,
+                             float* biases, float* dequantized, void* stream);
+
+/* Llama adapter layer element-wise steps (Llama32DecoderLayerMLX, llama32_adapter.py:417-662), one
+ * launch each, in the adapter's operation order and rounding points:
+ *
+ * rfsn_llama_rmsnorm_f16: y[r] = fp16(x[r] / sqrt(mean(x[r]^2) + eps) * weight) in fp32 with an fp16
+ * weight (_rms_norm, :497-500).  With b != NULL the row is first sum = fp16(x + b) (the residual
+ * add before the post-attention norm) and sum is normalised.
+ *
+ * rfsn_rope_f16: y = fp16(x * cos + rotate_half(x) * sin) in fp32 (_apply_rope, :555-568) for
+ * x [batch][seq][heads][dim] (element strides; dim contiguous) and fp16 tables [seq][dim]; y may
+ * alias x.
+ *
+ * rfsn_silu_mul_f16: y = fp16(fp16(g * sigmoid(g)) * up) over n values (_silu and the gated
+ * product of _forward_mlp, :502-504, 584-589). */
+int rfsn_llama_rmsnorm_f16(const uint16_t* x, const uint16_t* b, uint16_t* sum, const uint16_t* weight, uint16_t* y,
+                           int64_t rows, int dim, float eps, void* stream);
+int rfsn_rope_f16(const uint16_t* x, int64_t stride_b, int64_t stride_s, int64_t stride_h, uint16_t* y,
+                  int64_t y_stride_b, int64_t y_stride_s, int64_t y_stride_h, const uint16_t* cos_table,
+                  const uint16_t* sin_table, int64_t batch, int seq, int heads, int dim, void* stream);
+int rfsn_silu_mul_f16(const uint16_t* gate, const uint16_t* up, uint16_t* y, int64_t n, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

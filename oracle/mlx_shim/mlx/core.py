@@ -385,6 +385,11 @@ def softmax(x: array, axis=-1) -> array:
     return _wrap(_torch.softmax(x._t, dim=axis), x._dtype)
 
 
+def matmul(a: array, b: array) -> array:
+    """mx.matmul (used by the reference's Llama adapter, llama32_adapter.py:493)."""
+    return _wrap(_unwrap(a) @ _unwrap(b))
+
+
 def where(cond, a, b) -> array:
     tc = _unwrap(cond)
     ta, tb = _unwrap(a), _unwrap(b)

@@ -758,3 +758,110 @@ class OracleDecoderLayer:
         hidden = residual + linear(att.reshape(b, s, self.h * self.d).astype(F16), self.w["o_proj"])
         f = rms_norm(hidden)
         return hidden + linear(gelu(linear(f, self.w["ffn_up"])), self.w["ffn_down"])
+
+
+# ---------------------------------------------------------------------------
+# Llama adapter layer (llama32_adapter.py:374-386, 417-662)
+# ---------------------------------------------------------------------------
+
+def llama_rms_norm(x: np.ndarray, weight: np.ndarray, eps: float) -> np.ndarray:
+    """llama32_adapter.py:497-500 — fp32 x / sqrt(mean(x^2) + eps) * weight, to fp16."""
+    xf = x.astype(F32)
+    var = np.mean(xf ** 2, axis=-1, keepdims=True, dtype=F32)
+    return ((xf / np.sqrt(var + F32(eps))) * weight.astype(F32)).astype(F16)
+
+
+def llama_linear(x: np.ndarray, w: np.ndarray) -> np.ndarray:
+    """llama32_adapter.py:492-494 — fp32 matmul of fp16 operands, to fp16."""
+    return (x.astype(F32) @ w.astype(F32).T).astype(F16)
+
+
+def rotate_half(x: np.ndarray) -> np.ndarray:
+    """llama32_adapter.py:375-377."""
+    half = x.shape[-1] // 2
+    return np.concatenate([-x[..., half:], x[..., :half]], axis=-1)
+
+
+def apply_rope(q: np.ndarray, k: np.ndarray, cos: np.ndarray, sin: np.ndarray) -> Tuple[np.ndarray, np.ndarray]:
+    """llama32_adapter.py:555-568 — tables fp16 [1, S, D] (as _normalize_position_component
+    leaves them), x * cos + rotate_half(x) * sin in fp32, to fp16."""
+    c = cos.astype(F16).astype(F32)[:, :, None, :]
+    s = sin.astype(F16).astype(F32)[:, :, None, :]
+    q32, k32 = q.astype(F32), k.astype(F32)
+    return ((q32 * c + rotate_half(q32) * s).astype(F16), (k32 * c + rotate_half(k32) * s).astype(F16))
+
+
+def silu(x: np.ndarray) -> np.ndarray:
+    """llama32_adapter.py:502-504 — fp32 x * sigmoid(x), to fp16."""
+    xf = x.astype(F32)
+    return (xf * (F32(1.0) / (F32(1.0) + np.exp(-xf)))).astype(F16)
+
+
+class OracleLlamaLayer:
+    """Llama32DecoderLayerMLX restated for batch 1 (the reference's limit): RMSNorm with a
+    weight, q/k/v projections, RoPE from given tables, the RFSN cache (GQA heads stored once,
+    which equals the reference's cache over _repeat_kv'd heads), o_proj + residual, RMSNorm,
+    SwiGLU MLP + residual.  weights: fp16 [out, in] projections and fp16 norm weights."""
+
+    def __init__(self, config: OracleConfig, quantizer: Quantizer, weights: Dict[str, np.ndarray], kv_heads: int,
+                 eps: float):
+        self.cfg = replace(config, num_kv_heads=kv_heads)
+        self.w = weights
+        self.h, self.hkv, self.d, self.eps = config.num_heads, kv_heads, config.head_dim, eps
+        self.cache = OracleCache(self.cfg, quantizer, batch=1)
+
+    def _qkv(self, x: np.ndarray, cos: np.ndarray, sin: np.ndarray):
+        """llama32_adapter.py:570-582 (without the repeat: the cache keeps the KV heads)."""
+        b, s, _ = x.shape
+        a = llama_rms_norm(x, self.w["input_layernorm"], self.eps)
+        q = llama_linear(a, self.w["q_proj"]).reshape(b, s, self.h, self.d)
+        k = llama_linear(a, self.w["k_proj"]).reshape(b, s, self.hkv, self.d)
+        v = llama_linear(a, self.w["v_proj"]).reshape(b, s, self.hkv, self.d)
+        q, k = apply_rope(q, k, cos, sin)
+        return q, k, v
+
+    def prefill_cache(self, x: np.ndarray, cos: np.ndarray, sin: np.ndarray) -> None:
+        """llama32_adapter.py:591-614."""
+        _, k, v = self._qkv(x.astype(F16), cos, sin)
+        self.cache.update(k, v)
+
+    def __call__(self, x: np.ndarray, cos: np.ndarray, sin: np.ndarray, use_cache: bool = False,
+                 context_window: Optional[int] = None) -> np.ndarray:
+        """llama32_adapter.py:616-662."""
+        residual = x.astype(F16)
+        q, k, v = self._qkv(residual, cos, sin)
+        b, s = x.shape[:2]
+        if use_cache:
+            self.cache.update(k, v)
+            total = self.cache.total_tokens
+            att = self.cache.attention_forward(q[:, :1], causal=True, query_positions=[total - 1],
+                                               current_position=total - 1, context_window=context_window)
+            att = att.reshape(b, 1, self.h, self.d)
+        else:
+            att = dense_exact_attention(q, k, v, self.d ** -0.5, causal=True)
+        hidden = residual + llama_linear(att.reshape(b, s, self.h * self.d).astype(F16), self.w["o_proj"])
+        m = llama_rms_norm(hidden, self.w["post_attention_layernorm"], self.eps)
+        act = silu(llama_linear(m, self.w["gate_proj"])) * llama_linear(m, self.w["up_proj"])
+        return hidden + llama_linear(act.astype(F16), self.w["down_proj"])
+
+
+# ---------------------------------------------------------------------------
+# Affine codebook quantization (quantization.py:36-89; MLX 0.29.3 mx.quantize, affine mode)
+# ---------------------------------------------------------------------------
+
+def affine_quantize(w: np.ndarray, bits: int, group: int) -> Tuple[np.ndarray, np.ndarray, np.ndarray, np.ndarray]:
+    """The published affine scheme of mx.quantize / mx.dequantize, per group of `group`
+    consecutive elements of a row (fp32): scale = (max - min) / (2^bits - 1), bias = min,
+    q = clip(round_half_even((w - bias) / scale), 0, 2^bits - 1), w' = q * scale + bias.
+    A constant group has scale 0, codes 0 and w' = bias.  MLX is not installed here, so this
+    restatement is not pinned to MLX's own output.  Returns (q uint8, scales, biases, w')."""
+    w32 = np.asarray(w, F32)
+    rows, cols = w32.shape
+    g = w32.reshape(rows, cols // group, group)
+    mx_, mn = g.max(-1), g.min(-1)
+    nbins = F32((1 << bits) - 1)
+    scale = ((mx_ - mn) / nbins).astype(F32)
+    safe = np.where(scale > 0, scale, F32(1)).astype(F32)
+    q = np.where(scale[..., None] > 0, np.clip(np.rint((g - mn[..., None]) / safe[..., None]), 0, nbins), 0).astype(F32)
+    deq = (q * scale[..., None]).astype(F32) + mn[..., None]
+    return q.astype(np.uint8).reshape(rows, cols), scale, mn.astype(F32), deq.astype(F32).reshape(rows, cols)

@@ -353,6 +353,65 @@ def case_chunk_files(ref, name, seed, n_tokens=70, split=44):
         shutil.rmtree(tmp, ignore_errors=True)
 
 
+def rope_tables(positions, head_dim, theta=500000.0):
+    """Standard rotary tables cos/sin [1, len, head_dim] (the half-split layout of the Llama
+    rotary module), as float32."""
+    inv = 1.0 / (theta ** (np.arange(0, head_dim, 2, dtype=np.float64) / head_dim))
+    ang = np.asarray(positions, np.float64)[:, None] * inv[None]
+    emb = np.concatenate([ang, ang], axis=-1)
+    return np.cos(emb)[None].astype(np.float32), np.sin(emb)[None].astype(np.float32)
+
+
+def case_llama_layer(ref, name, seed):
+    """Llama32DecoderLayerMLX (llama32_adapter.py:417-662): RMSNorm with weights, q/k/v
+    projections, RoPE from given position tables, GQA by _repeat_kv, the RFSN cache (prefill,
+    then cache-backed decode steps through hot, warm and cold), o_proj, SwiGLU MLP, residuals;
+    plus the dense path.  Weights are seeded and injected as fp16."""
+    import importlib
+    mx = sys.modules["mlx.core"]
+    adapter = importlib.import_module("llama32_adapter")
+    rng = np.random.default_rng(seed)
+    tmp = Path(tempfile.mkdtemp(prefix="rfsn_llama_"))
+    try:
+        hidden, heads, kv_heads, hd, inter = 128, 2, 1, 64, 256
+        config = make_config(ref, hidden_dim=hidden, num_heads=heads, head_dim=hd, num_subspaces=16, subspace_dim=4,
+                             num_rvq_layers=1, rvq_codebook_size=256, rvq_sparsity_threshold=0.2, hot_capacity=16,
+                             warm_capacity=24, block_size_seq=16, disk_cache_dir=str(tmp))
+        w = {}
+        for nm, (o, i) in dict(q_proj=(heads * hd, hidden), k_proj=(kv_heads * hd, hidden),
+                               v_proj=(kv_heads * hd, hidden), o_proj=(hidden, heads * hd), gate_proj=(inter, hidden),
+                               up_proj=(inter, hidden), down_proj=(hidden, inter)).items():
+            w[nm] = (rng.standard_normal((o, i)) / np.sqrt(i)).astype(np.float16)
+        w["input_layernorm"] = (1.0 + 0.1 * rng.standard_normal(hidden)).astype(np.float16)
+        w["post_attention_layernorm"] = (1.0 + 0.1 * rng.standard_normal(hidden)).astype(np.float16)
+        layer = adapter.Llama32DecoderLayerMLX(
+            config, 0, kv_heads, 1e-5, mx.array(w["input_layernorm"]), mx.array(w["post_attention_layernorm"]),
+            *(mx.array(w[k]) for k in ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")))
+        pq_cb, rvq_cb = seeded_codebooks(rng, 16, 256, 4, 1, 256, hd)
+        layer.quantizer.pq.codebooks = mx.array(pq_cb, dtype=mx.float16)
+        layer.quantizer.rvq.codebooks = mx.array(rvq_cb, dtype=mx.float16)
+        n_prefill, n_decode = 40, 20
+        x = rng.standard_normal((1, n_prefill + n_decode, hidden)).astype(np.float16)
+        cos, sin = rope_tables(np.arange(n_prefill + n_decode), hd)
+        layer.prefill_cache(mx.array(x[:, :n_prefill]), position_embeddings=(cos[:, :n_prefill], sin[:, :n_prefill]))
+        outs = []
+        for t in range(n_prefill, n_prefill + n_decode):
+            outs.append(np.asarray(layer(mx.array(x[:, t:t + 1]), position_embeddings=(cos[:, t:t + 1], sin[:, t:t + 1]),
+                                         use_cache=True)))
+        stats = layer.cache.get_last_access_stats()
+        x2 = rng.standard_normal((1, 6, hidden)).astype(np.float16)
+        c2, s2 = rope_tables(np.arange(6), hd)
+        dense = np.asarray(layer(mx.array(x2), position_embeddings=(c2, s2), use_cache=False))
+        np.savez_compressed(OUT / f"{name}.npz", **{f"w_{k}": v for k, v in w.items()}, pq_codebooks=pq_cb,
+                            rvq_codebooks=rvq_cb, x=x, n_prefill=np.int32(n_prefill), cos=cos, sin=sin,
+                            decode_out=np.concatenate(outs, 1), x_dense=x2, cos_dense=c2, sin_dense=s2,
+                            dense_out=dense, last_stats=np.array([stats[k] for k in STAT_KEYS], np.int64),
+                            tiers=np.array([layer.cache.num_hot, layer.cache.num_warm, layer.cache.num_cold],
+                                           np.int32), kv_heads=np.int32(kv_heads), eps=np.float32(1e-5))
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+
+
 CASES = {
     "quant": lambda ref: (
         case_quantizer(ref, "quant_d128_m8x16_rvq3", seed=11, cfg_kw={}, n=96, scale_half=0.01),
@@ -373,6 +432,7 @@ CASES = {
     "calibration": lambda ref: case_calibration(ref, "calibration_kmeans", seed=51),
     "gqa_batch": lambda ref: case_gqa_batch(ref, "gqa_batch_cache", seed=61),
     "chunk_files": lambda ref: case_chunk_files(ref, "ref_chunks", seed=71),
+    "llama": lambda ref: case_llama_layer(ref, "llama_layer", seed=81),
 }
 
 

@@ -316,6 +316,106 @@ def test_reference_chunk_file_into_device_store():
         np.testing.assert_array_equal(u16(out[0]), u16(oq.decode(codes)))
 
 
+def test_llama_layer_golden(tmp_path):
+    """Llama32DecoderLayerMLX (llama32_adapter.py:417-662) against the reference run through the
+    shim: prefill, 20 cache-backed decode steps through hot, warm and cold, and the dense path.
+    fp16 outputs up to ~5 in magnitude: within one fp16 step (atol 4e-3) plus 2e-3 relative."""
+    from apple_b200.llama import Llama32DecoderLayerMLX
+    g = dict(np.load(GOLDEN / "llama_layer.npz"))
+    D = 64
+    hidden = g["x"].shape[-1]
+    heads = g["w_q_proj"].shape[0] // D
+    cfg = tiers_config(tmp_path, hidden_dim=hidden, num_heads=heads, head_dim=D, num_subspaces=16, subspace_dim=4,
+                       num_rvq_layers=1, rvq_sparsity_threshold=0.2)
+    w = {k[2:]: torch.from_numpy(v) for k, v in g.items() if k.startswith("w_")}
+    layer = Llama32DecoderLayerMLX(cfg, 0, int(g["kv_heads"]), float(g["eps"]), w["input_layernorm"],
+                                   w["post_attention_layernorm"], w["q_proj"], w["k_proj"], w["v_proj"], w["o_proj"],
+                                   w["gate_proj"], w["up_proj"], w["down_proj"])
+    layer.quantizer.pq.codebooks = torch.from_numpy(g["pq_codebooks"]).cuda()
+    layer.quantizer.rvq.codebooks = torch.from_numpy(g["rvq_codebooks"]).cuda()
+    n = int(g["n_prefill"])
+    x = torch.from_numpy(g["x"]).cuda()
+    layer.prefill_cache(x[:, :n], position_embeddings=(g["cos"][:, :n], g["sin"][:, :n]))
+    outs = [layer(x[:, t:t + 1], position_embeddings=(g["cos"][:, t:t + 1], g["sin"][:, t:t + 1]), use_cache=True)
+            for t in range(n, x.shape[1])]
+    assert [layer.cache.num_hot, layer.cache.num_warm, layer.cache.num_cold] == list(g["tiers"])
+    assert [layer.cache.last_access_stats[k] for k in STAT_KEYS] == list(g["last_stats"])
+    got = torch.cat(outs, 1).float().cpu().numpy()
+    np.testing.assert_allclose(got, g["decode_out"].astype(np.float32), atol=4e-3, rtol=2e-3)
+    dense = layer(torch.from_numpy(g["x_dense"]).cuda(), position_embeddings=(g["cos_dense"], g["sin_dense"]))
+    np.testing.assert_allclose(dense.float().cpu().numpy(), g["dense_out"].astype(np.float32), atol=4e-3, rtol=2e-3)
+    with pytest.raises(RuntimeError):
+        layer(x[:, :1], use_cache=True)  # no position tables and no rotary module
+    layer.cache.close()
+
+
+def test_llama_ops_vs_oracle():
+    """The Llama adapter's RMSNorm (+ residual add), RoPE and SwiGLU kernels against the numpy
+    restatement: fp16 results within one fp16 step (the last fp32 bit of sqrt, exp or the mean
+    can cross an fp16 rounding boundary), and equal in most elements."""
+    from apple_b200 import kernels as K
+    rng = np.random.default_rng(9)
+    x = (rng.standard_normal((5, 3, 256)) * 2).astype(np.float16)
+    r = rng.standard_normal((5, 3, 256)).astype(np.float16)
+    w = (1 + 0.1 * rng.standard_normal(256)).astype(np.float16)
+    y, s = K.llama_rms_norm(torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda(), 1e-5,
+                            residual=torch.from_numpy(r).cuda())
+    s_ref = (x.astype(np.float32) + r.astype(np.float32)).astype(np.float16)
+    np.testing.assert_array_equal(u16(s), u16(s_ref))
+    ref = R.llama_rms_norm(s_ref, w, 1e-5).astype(np.float32)
+    got = y.float().cpu().numpy()
+    np.testing.assert_allclose(got, ref, rtol=1e-3, atol=1e-3)
+    assert (got == ref).mean() > 0.99
+    q = rng.standard_normal((2, 7, 4, 64)).astype(np.float16)
+    k = rng.standard_normal((2, 7, 2, 64)).astype(np.float16)
+    ang = np.arange(7)[:, None] * (1.0 / (10000 ** (np.arange(0, 64, 2) / 64)))[None]
+    cos = np.cos(np.concatenate([ang, ang], -1)).astype(np.float16)[None]
+    sin = np.sin(np.concatenate([ang, ang], -1)).astype(np.float16)[None]
+    qr, kr = R.apply_rope(q, k, cos, sin)
+    np.testing.assert_array_equal(u16(K.rope(torch.from_numpy(q).cuda(), torch.from_numpy(cos), torch.from_numpy(sin))),
+                                  u16(qr))
+    np.testing.assert_array_equal(u16(K.rope(torch.from_numpy(k).cuda(), torch.from_numpy(cos), torch.from_numpy(sin))),
+                                  u16(kr))
+    gt = (rng.standard_normal(4096) * 3).astype(np.float16)
+    up = rng.standard_normal(4096).astype(np.float16)
+    got = K.silu_mul(torch.from_numpy(gt).cuda(), torch.from_numpy(up).cuda()).float().cpu().numpy()
+    ref = (R.silu(gt).astype(np.float32) * up.astype(np.float32)).astype(np.float16).astype(np.float32)
+    np.testing.assert_allclose(got, ref, rtol=2e-3, atol=1e-4)
+    assert (got == ref).mean() > 0.99
+
+
+def test_affine_codebooks_for_ane():
+    """quantize_codebooks_for_ane (quantization.py:159-175, 277-293, 321-327): the kernel's codes,
+    scales, biases and dequantized values equal the oracle's affine restatement; the quantizer then
+    reads the dequantized codebooks (the reference's quantized fast path test, rfsn_v10_mlx_ane_
+    complete.py:404-416: every codebook quantized, finite round-trip error)."""
+    from apple_b200 import kernels as K
+    rng = np.random.default_rng(2)
+    w = (rng.standard_normal((64, 256)) * 0.5).astype(np.float16).astype(np.float32)
+    q, sc, bi, deq = K.affine_quantize(torch.from_numpy(w).cuda(), 6, 128)
+    rq, rsc, rbi, rdeq = R.affine_quantize(w, 6, 128)
+    np.testing.assert_array_equal(q.cpu().numpy(), rq)
+    np.testing.assert_array_equal(sc.cpu().numpy(), rsc)
+    np.testing.assert_array_equal(bi.cpu().numpy(), rbi)
+    np.testing.assert_array_equal(deq.cpu().numpy(), rdeq)
+    cfg = RFSNConfig(hidden_dim=512, num_heads=8, head_dim=64, num_subspaces=16, subspace_dim=4, num_rvq_layers=2,
+                     rvq_codebook_size=256, rvq_sparsity_threshold=0.3)
+    hq = HybridQuantizerMLX(cfg)
+    x = torch.randn((512, 64), generator=torch.Generator().manual_seed(3)).half().cuda()
+    mse0 = float(((x.float() - hq.decode(*hq.encode(x)).float()) ** 2).mean())
+    pq_before = hq.pq.codebooks.clone()
+    report = hq.quantize_codebooks_for_ane()
+    assert report == {"pq_quantized": 16, "rvq_quantized": 2}
+    # PQ codebooks [256, 4] quantize transposed in groups of 128 along the centroids; RVQ [256, 64]
+    # in groups of 64 along each row
+    m0 = hq.pq._ane_codebooks[0]
+    assert m0.transposed and m0.group_size == 128 and hq.rvq._ane_codebooks[0].group_size == 64
+    _, _, _, d0 = R.affine_quantize(pq_before[0].float().cpu().numpy().T.copy(), 6, 128)
+    np.testing.assert_array_equal(u16(hq.pq.effective_codebooks()[0]), u16(d0.T.astype(np.float16)))
+    mse1 = float(((x.float() - hq.decode(*hq.encode(x)).float()) ** 2).mean())
+    assert np.isfinite(mse1) and mse1 < 1.5 * mse0 + 1e-3
+
+
 def test_quantizer_api_golden():
     """HybridQuantizerMLX encode/decode and the compressed-tensor helpers vs reference vectors."""
     g = dict(np.load(GOLDEN / "quant_d128_m8x16_rvq3.npz"))

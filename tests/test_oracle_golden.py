@@ -220,3 +220,43 @@ def _layer_close(out, ref):
     out, ref = np.asarray(out, np.float32), np.asarray(ref, np.float32)
     tol = 2e-3 * np.abs(ref) + 2e-3 * float(np.sqrt(np.mean(ref ** 2)))
     assert (np.abs(out - ref) <= tol).all(), float(np.abs(out - ref).max())
+
+
+def test_oracle_llama_layer_matches_reference():
+    """Llama32DecoderLayerMLX (llama32_adapter.py:417-662): prefill, 20 cache-backed decode steps
+    through every tier, and the dense path, against the reference run through the shim."""
+    g = load("llama_layer")
+    D = 64
+    hidden = g["x"].shape[-1]
+    heads = g["w_q_proj"].shape[0] // D
+    cfg = R.OracleConfig(hidden_dim=hidden, num_heads=heads, head_dim=D, num_subspaces=16, subspace_dim=4,
+                         num_rvq_layers=1, rvq_codebook_size=256, rvq_sparsity_threshold=0.2, hot_capacity=16,
+                         warm_capacity=24, block_size_seq=16)
+    w = {k[2:]: v for k, v in g.items() if k.startswith("w_")}
+    layer = R.OracleLlamaLayer(cfg, R.Quantizer(g["pq_codebooks"], g["rvq_codebooks"], 0.2), w, int(g["kv_heads"]),
+                               float(g["eps"]))
+    n = int(g["n_prefill"])
+    layer.prefill_cache(g["x"][:, :n], g["cos"][:, :n], g["sin"][:, :n])
+    outs = [layer(g["x"][:, t:t + 1], g["cos"][:, t:t + 1], g["sin"][:, t:t + 1], use_cache=True)
+            for t in range(n, g["x"].shape[1])]
+    assert [layer.cache.num_hot, layer.cache.num_warm, layer.cache.num_cold] == list(g["tiers"])
+    assert [layer.cache.last_access_stats[k] for k in STAT_KEYS] == list(g["last_stats"])
+    # fp16 outputs of magnitude up to ~5: one fp16 step (the fp32 matmul summation order differs)
+    np.testing.assert_allclose(np.concatenate(outs, 1).astype(np.float32), g["decode_out"].astype(np.float32),
+                               atol=4e-3, rtol=2e-3)
+    dense = layer(g["x_dense"], g["cos_dense"], g["sin_dense"], use_cache=False)
+    np.testing.assert_allclose(dense.astype(np.float32), g["dense_out"].astype(np.float32), atol=4e-3, rtol=2e-3)
+
+
+def test_affine_codebook_quantization_properties():
+    """The affine scheme (quantization.py:36-89 via mx.quantize): codes in range, the group's
+    minimum exact, every value within half a step, a constant group exact."""
+    rng = np.random.default_rng(4)
+    w = (rng.standard_normal((4, 256)) * 0.7).astype(np.float16).astype(np.float32)
+    w[3, 128:] = 0.25
+    q, sc, bi, deq = R.affine_quantize(w, 6, 128)
+    assert q.max() <= 63 and q.dtype == np.uint8 and sc.shape == (4, 2)
+    g = w.reshape(4, 2, 128)
+    np.testing.assert_array_equal(bi, g.min(-1))
+    assert (np.abs(deq - w).reshape(4, 2, 128) <= sc[..., None] * 0.5 * (1 + 1e-5) + 1e-7).all()
+    np.testing.assert_array_equal(deq[3, 128:], w[3, 128:])
