@@ -53,6 +53,15 @@ class Segment(C.Structure):
                 ("pos0", C.c_int32), ("reserved", C.c_int32 * 3)]
 
 
+RFSN_MAX_PEERS = 8
+
+
+class PeerGather(C.Structure):
+    _fields_ = [("num_ranks", C.c_int32), ("rank", C.c_int32), ("seq_offset", C.c_int64), ("total_seqs", C.c_int64),
+                ("buffers", C.c_void_p * RFSN_MAX_PEERS), ("flags", C.c_void_p * RFSN_MAX_PEERS),
+                ("step", C.c_void_p), ("out_full", C.c_void_p)]
+
+
 class AttnArgs(C.Structure):
     _fields_ = [("q", C.c_void_p), ("qpos", C.c_void_p), ("out", C.c_void_p), ("batch", C.c_int32),
                 ("queries", C.c_int32), ("q_heads", C.c_int32), ("kv_heads", C.c_int32), ("head_dim", C.c_int32),
@@ -60,7 +69,7 @@ class AttnArgs(C.Structure):
                 ("cold", CodeStore),
                 ("segments", C.POINTER(Segment)), ("num_segments", C.c_int32), ("num_ctas", C.c_int32),
                 ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t), ("device_status", C.c_void_p),
-                ("q_batch_stride", C.c_int64)]
+                ("q_batch_stride", C.c_int64), ("gather", C.POINTER(PeerGather))]
 
 
 # exported symbol -> (restype, argtypes); must match include/rfsn_b200.h
@@ -84,6 +93,10 @@ SIGNATURES = {
     "rfsn_decode_attention_noalloc": (C.c_int, [C.POINTER(AttnArgs), C.POINTER(Quantizer), C.c_void_p]),
     "rfsn_route_topk": (C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                                   C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "rfsn_peer_alloc": (C.c_int, [C.c_size_t, C.POINTER(C.c_void_p), C.c_void_p]),
+    "rfsn_peer_open": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
+    "rfsn_peer_close": (C.c_int, [C.c_void_p]),
+    "rfsn_peer_free": (C.c_int, [C.c_void_p]),
     "rfsn_cold_prefetch": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p]),
     "rfsn_cold_evict": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
     "rfsn_rmsnorm_f16": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int, C.c_float, C.c_void_p]),

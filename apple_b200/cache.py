@@ -612,8 +612,12 @@ class RFSNv10KVCacheMLX:
     def attention_forward(self, q: torch.Tensor, pq_codebook=None, rvq_codebook=None, causal: bool = True,
                           query_positions=None, router: Optional[AsyncHierarchicalRouterMLX] = None,
                           current_position: Optional[int] = None, context_window: Optional[int] = None,
-                          out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """cache.py:395-428 — fused decode attention over hot/warm/cold without a dense window."""
+                          out: Optional[torch.Tensor] = None, gather=None) -> torch.Tensor:
+        """cache.py:395-428 — fused decode attention over hot/warm/cold without a dense window.
+
+        gather (extension, multi-GPU): a sharding.PeerGather whose ranks each hold an equal batch
+        shard; the kernel then also all-gathers the outputs over peer memory and the call returns
+        the whole batch's output (gather.full, [total, Q, Hq, D], as [total, Hq, D] for one query)."""
         del pq_codebook, rvq_codebook  # ignored by the reference too (cache.py:406)
         if self.quantizer is None:
             raise RuntimeError("Cache cannot run attention before update() provides a quantizer")
@@ -653,7 +657,7 @@ class RFSNv10KVCacheMLX:
         ck = entry = None
         if key is not None:
             ck = (shape, qb.shape, qb.stride(0), qpos is not None,
-                  self._store_epoch, self._cold is not None)
+                  self._store_epoch, self._cold is not None, None if gather is None else id(gather))
             entry = self._attn_calls.get(ck)
             if entry is not None:
                 K.patch_segments(entry, segs)
@@ -662,12 +666,15 @@ class RFSNv10KVCacheMLX:
                                      causal=qpos is not None, scale=self.head_dim ** -0.5,
                                      hot=(self._hot_k, self._hot_v) if self._hot_k is not None else None,
                                      warm=self._warm, cold=self._cold.pool if self._cold is not None else None,
-                                     memo=ck is None)
+                                     memo=ck is None, gather=gather)
             if ck is not None:
                 if len(self._attn_calls) > 32:
                     self._attn_calls.clear()
                 self._attn_calls[ck] = entry
         K.run_attention(entry, qb, out, qpos)
+        if gather is not None:
+            full = gather.full
+            return full[:, 0] if (q.dim() == 3 and not squeeze) else full
         if squeeze:
             return out[0]
         return out.reshape(q.shape) if q.dim() == 3 else out

@@ -92,3 +92,40 @@ extern "C" int rfsn_cold_evict(void* dst_pinned_host, const void* src_device, si
   return rfsn::check_cuda(cudaMemcpyAsync(dst_pinned_host, src_device, bytes, cudaMemcpyDeviceToHost,
                                           reinterpret_cast<cudaStream_t>(stream)));
 }
+
+extern "C" int rfsn_peer_alloc(size_t bytes, void** ptr, void* ipc_handle) {
+  if (!ptr || !ipc_handle || !bytes) return RFSN_ERR_INVALID_ARGUMENT;
+  *ptr = nullptr;
+  void* p = nullptr;
+  int st = rfsn::check_cuda(cudaMalloc(&p, bytes));
+  if (st != RFSN_OK) return st;
+  st = rfsn::check_cuda(cudaMemset(p, 0, bytes));
+  if (st == RFSN_OK) {
+    cudaIpcMemHandle_t h;
+    st = rfsn::check_cuda(cudaIpcGetMemHandle(&h, p));
+    if (st == RFSN_OK) memcpy(ipc_handle, &h, sizeof(h));
+  }
+  if (st != RFSN_OK) {
+    cudaFree(p);
+    return st;
+  }
+  *ptr = p;
+  return RFSN_OK;
+}
+
+extern "C" int rfsn_peer_open(const void* ipc_handle, void** ptr) {
+  if (!ipc_handle || !ptr) return RFSN_ERR_INVALID_ARGUMENT;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  return rfsn::check_cuda(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+extern "C" int rfsn_peer_close(void* ptr) {
+  if (!ptr) return RFSN_ERR_INVALID_ARGUMENT;
+  return rfsn::check_cuda(cudaIpcCloseMemHandle(ptr));
+}
+
+extern "C" int rfsn_peer_free(void* ptr) {
+  if (!ptr) return RFSN_ERR_INVALID_ARGUMENT;
+  return rfsn::check_cuda(cudaFree(ptr));
+}

@@ -103,6 +103,14 @@ struct AttnParams {
   int nseg;
   int smem_pq, smem_pqsw, smem_rvq, smem_scr, scr_bytes, smem_ml, smem_desc, smem_bar, smem_flag;
   int stages, stage_bytes, ring_off;  // ring depth, bytes per stage, ring offset in smem
+  // fused output all-gather over peer memory (npeers == 0: off)
+  int npeers, my_rank;
+  int64_t seq_offset;  // this rank's first sequence in the gathered output
+  int64_t full_elems;  // elements of one gathered-output buffer
+  uint16_t* peer_buf[RFSN_MAX_PEERS];
+  unsigned long long* peer_flags[RFSN_MAX_PEERS];
+  unsigned long long* step;
+  uint16_t* out_full;
   SegDev seg[RFSN_MAX_SEGMENTS];
 };
 
@@ -156,7 +164,54 @@ __device__ __forceinline__ int take_ticket(unsigned long long* t, unsigned long 
 
 // Log-sum-exp merge of a row's pieces (m in log2 units) and the fp16 output
 // (attention.py:104-105: a row whose every key is masked outputs zeros).
-__device__ __forceinline__ void merge_row(const AttnParams& p, int64_t row, int tid, int nthr) {
+__device__ __forceinline__ void st_release_sys(unsigned long long* a, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* a) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+  return v;
+}
+
+// The launch's last CTA (gather mode): signal every rank that this rank's stores of the launch
+// are done, wait (bounded) for every rank's signal, then copy the gathered output of this
+// launch's parity into out_full.  `threads` consumer threads take part; thread 0 signals.
+__device__ __noinline__ void gather_finish(const AttnParams& p, int parity, volatile int* abort, int threads) {
+  volatile int* ok = abort + 3;
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const unsigned long long s = *reinterpret_cast<volatile unsigned long long*>(p.step) + 1ull;
+    *reinterpret_cast<volatile unsigned long long*>(p.step) = s;
+    for (int k = 0; k < p.npeers; ++k) st_release_sys(p.peer_flags[k] + p.my_rank, s);
+    int good = 1;
+    const unsigned long long* mine = p.peer_flags[p.my_rank];
+    const uint64_t t0 = global_timer_ns();
+    for (int r = 0; r < p.npeers && good; ++r) {
+      for (uint32_t it = 0; ld_acquire_sys(mine + r) < s; ++it) {
+        if ((it & 63u) == 63u && global_timer_ns() - t0 > kWaitLimitNs) {
+          good = 0;
+          break;
+        }
+      }
+    }
+    if (!good && p.dev_status) atomicExch(p.dev_status, kDevStatusPeerTimeout);
+    *ok = good;
+  }
+  named_bar_sync(2, threads);
+  if (!*ok) return;
+  const uint4* src = reinterpret_cast<const uint4*>(p.peer_buf[p.my_rank] + (int64_t)parity * p.full_elems);
+  uint4* dst = reinterpret_cast<uint4*>(p.out_full);
+  for (int64_t i = threadIdx.x; i < p.full_elems / 8; i += threads) dst[i] = __ldcg(src + i);
+}
+
+// Gather mode: one output element into every rank's gathered-output buffer of this parity.
+__device__ __noinline__ void push_to_peers(const AttnParams& p, int parity, int b, int qi, int h, int d, uint16_t v) {
+  const int64_t gi = (int64_t)parity * p.full_elems + (((p.seq_offset + b) * p.Q + qi) * p.Hq + h) * (int64_t)p.D + d;
+  for (int k = 0; k < p.npeers; ++k) p.peer_buf[k][gi] = v;
+}
+
+__device__ __forceinline__ void merge_row(const AttnParams& p, int64_t row, int tid, int nthr, int parity) {
   int64_t c0;
   const int np = row_pieces(p, row, &c0);
   const int b = (int)(row / p.Hkv), kvh = (int)(row % p.Hkv);
@@ -178,7 +233,9 @@ __device__ __forceinline__ void merge_row(const AttnParams& p, int64_t row, int 
     }
     const float o = L > 0.f ? O / L : 0.f;
     const int qi = r / p.G, g = r - qi * p.G;
-    p.out[(((size_t)b * p.Q + qi) * p.Hq + kvh * p.G + g) * p.D + d] = f2h(o);
+    const uint16_t h = f2h(o);
+    p.out[(((size_t)b * p.Q + qi) * p.Hq + kvh * p.G + g) * p.D + d] = h;
+    if (p.npeers) push_to_peers(p, parity, b, qi, kvh * p.G + g, d, h);
   }
 }
 
@@ -205,6 +262,8 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
     }
     mbar_init(sync_bar, NW);
     *abort = 0;
+    // gather mode: this launch's buffer parity (the last CTA advances the step afterwards)
+    abort[2] = p.npeers ? (int)(*reinterpret_cast<volatile unsigned long long*>(p.step) & 1ull) : 0;
     fence_mbar_init();
   }
   __syncthreads();  // barriers initialised; the producer starts streaming at once
@@ -569,7 +628,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
       }
       if (*merge_flag) {  // this CTA finished the row: merge its pieces
         __threadfence();
-        merge_row(p, row, threadIdx.x, NW * 32);
+        merge_row(p, row, threadIdx.x, NW * 32, abort[2]);
       }
     }
     if (++stage == p.stages) {
@@ -583,11 +642,21 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
   // The done count is a plain counter that is zero between launches (the last CTA
   // resets it): one atomicAdd per CTA, where compare-and-swap tickets retried by
   // 148 CTAs finishing together serialise on round trips.
+  if (p.npeers) {  // every consumer's peer stores are ordered before this CTA counts itself done
+    __threadfence_system();
+    named_bar_sync(2, NW * 32);
+  }
   if (threadIdx.x == 0) {
-    if (atomicAdd(p.gen + 1, 1ull) == (unsigned long long)gridDim.x - 1ull) {
+    const bool last = atomicAdd(p.gen + 1, 1ull) == (unsigned long long)gridDim.x - 1ull;
+    if (last) {
       atomicExch(p.gen + 1, 0ull);
       atomicAdd(p.gen, 1ull);
     }
+    if (p.npeers) abort[1] = last;  // (the loop's merge flag: every consumer warp has left the loop)
+  }
+  if (p.npeers) {
+    named_bar_sync(2, NW * 32);
+    if (abort[1]) gather_finish(p, abort[2], abort, NW * 32);
   }
 }
 
@@ -783,6 +852,26 @@ static int make_plan(const rfsn_attn_args* a, const rfsn_quantizer* qz, Plan& pl
     p.max_pieces = 1;
   }
   if (p.max_pieces > 0xffff || pl.grid > 0xffff) return RFSN_ERR_UNSUPPORTED;  // tickets count in 16 bits
+  if (a->gather) {  // fused output all-gather over peer memory
+    const rfsn_peer_gather& g = *a->gather;
+    if (g.num_ranks < 2 || g.num_ranks > RFSN_MAX_PEERS || g.rank < 0 || g.rank >= g.num_ranks || !g.step ||
+        !g.out_full || g.seq_offset < 0 || g.seq_offset + a->batch > g.total_seqs)
+      return RFSN_ERR_INVALID_ARGUMENT;
+    if (reinterpret_cast<uintptr_t>(g.out_full) & 15) return RFSN_ERR_ALIGNMENT;
+    for (int k = 0; k < g.num_ranks; ++k) {
+      if (!g.buffers[k] || !g.flags[k]) return RFSN_ERR_INVALID_ARGUMENT;
+      if ((reinterpret_cast<uintptr_t>(g.buffers[k]) & 15) || (reinterpret_cast<uintptr_t>(g.flags[k]) & 7))
+        return RFSN_ERR_ALIGNMENT;
+      p.peer_buf[k] = g.buffers[k];
+      p.peer_flags[k] = reinterpret_cast<unsigned long long*>(g.flags[k]);
+    }
+    p.npeers = g.num_ranks;
+    p.my_rank = g.rank;
+    p.seq_offset = g.seq_offset;
+    p.full_elems = g.total_seqs * a->queries * a->q_heads * a->head_dim;
+    p.step = reinterpret_cast<unsigned long long*>(g.step);
+    p.out_full = g.out_full;
+  }
   pl.ws_bytes = workspace_layout(p, nullptr);
   return RFSN_OK;
 }

@@ -23,6 +23,7 @@ constexpr int kDevStatusTimeoutFull = 1;
 constexpr int kDevStatusTimeoutEmpty = 2;
 constexpr int kDevStatusBadSegment = 3;
 constexpr int kDevStatusTicket = 4;
+constexpr int kDevStatusPeerTimeout = 5;  // a peer rank's gather signal did not arrive in time
 
 __device__ __forceinline__ uint64_t global_timer_ns() {
   uint64_t t;

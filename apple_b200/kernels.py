@@ -305,14 +305,15 @@ def decode_attention(qz: QuantizerBuffers, q: torch.Tensor, out: torch.Tensor, s
                      hot: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
                      warm: Optional[CodeStoreBuffers] = None,
                      cold: Optional[CodeStoreBuffers] = None,
-                     num_ctas: int = 0, device_status: Optional[torch.Tensor] = None) -> torch.Tensor:
+                     num_ctas: int = 0, device_status: Optional[torch.Tensor] = None, gather=None) -> torch.Tensor:
     """Fused decode attention.  q/out fp16 [B, Q, Hq, D]; qpos int32 [B, Q, Hq] (global positions).
 
     hot: (k, v) fp16 [rows, cap, D]; warm/cold: code stores (K and V fields).
     segments: (store, slot, first, count, pos0) tuples in window order.
+    gather: a sharding.PeerGather; the whole batch's output then also lands in gather.full.
     """
     entry = attention_call(qz, q, out, segments, kv_heads, qpos=qpos, causal=causal, scale=scale, hot=hot, warm=warm,
-                           cold=cold, num_ctas=num_ctas)
+                           cold=cold, num_ctas=num_ctas, gather=gather)
     run_attention(entry, q, out, qpos if causal else None, device_status)
     return out
 
@@ -366,9 +367,10 @@ def attention_call(qz: QuantizerBuffers, q: torch.Tensor, out: torch.Tensor, seg
                    kv_heads: int, qpos: Optional[torch.Tensor] = None, causal: bool = True,
                    scale: Optional[float] = None, hot: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
                    warm: Optional[CodeStoreBuffers] = None, cold: Optional[CodeStoreBuffers] = None,
-                   num_ctas: int = 0, memo: bool = True) -> "_AttnCall":
+                   num_ctas: int = 0, memo: bool = True, gather=None) -> "_AttnCall":
     """Validate the arguments and return the prepared call for them: memoised by its exact
-    arguments, or (memo=False) a private one that the caller may patch_segments."""
+    arguments, or (memo=False) a private one that the caller may patch_segments.  gather: a
+    sharding.PeerGather, to fuse the output all-gather over peer memory into the launch."""
     _need_cuda(q, "q")
     if q.dtype != torch.float16 or q.dim() != 4 or not queries_packed(q):
         raise ValueError("q must be fp16 [B, Q, Hq, D], packed within a sequence (batch stride a multiple of 8)")
@@ -383,7 +385,8 @@ def attention_call(qz: QuantizerBuffers, q: torch.Tensor, out: torch.Tensor, seg
     scale = float(D ** -0.5 if scale is None else scale)
     hot_key = None if hot is None else (_ptr(hot[0]), _ptr(hot[1]), hot[0].shape[1], hot[0].shape[0])
     key = (q.device.index, B, Qn, Hq, D, kv_heads, bool(causal), scale, num_ctas, tuple(map(tuple, segments)),
-           hot_key, _store_key(warm), _store_key(cold), _qz_key(qz), q.stride(0) if B > 1 else 0)
+           hot_key, _store_key(warm), _store_key(cold), _qz_key(qz), q.stride(0) if B > 1 else 0,
+           None if gather is None else id(gather))
     entry = _ATTN_CALLS.get(key) if memo else None
     if entry is None:
         a = AttnArgs()
@@ -404,6 +407,8 @@ def attention_call(qz: QuantizerBuffers, q: torch.Tensor, out: torch.Tensor, seg
         a.num_segments = len(segments)
         a.num_ctas = num_ctas
         a.q_batch_stride = q.stride(0) if B > 1 else 0  # one sequence: no stride to follow
+        if gather is not None:
+            a.gather = gather.pointer
         qs = qz.struct()
         a.q, a.out, a.qpos = _ptr(q), _ptr(out), _ptr(qpos) if causal else None
         entry = _AttnCall(a, segs, qs, None)

@@ -12,12 +12,20 @@ the kernel:
 
 The one exchange is the all-gather of the attention outputs (fp16
 [b, Q, Hq_local, D] per rank), since the output projection needs every head
-of every sequence.  It runs over the process group's backend (NCCL on GPUs,
-gloo for the CPU tests); shards of unequal size are padded to the largest.
+of every sequence.  Two forms:
+
+* ``PeerGather``: fused into the attention kernel over NVLink peer memory
+  (rfsn_peer_gather): the CTA that merges a row stores its output into every
+  rank's gathered-output buffer, and the launch's last CTA waits for every
+  rank before copying the complete output out (batch shards of equal size).
+* ``gather_outputs``: a separate collective over the process group's backend
+  (NCCL on GPUs, gloo for the CPU tests); shards of unequal size are padded
+  to the largest.
 """
 from __future__ import annotations
 
 from dataclasses import dataclass
+import ctypes as C
 from typing import List, Optional
 
 import torch
@@ -94,3 +102,68 @@ def gather_outputs(local: torch.Tensor, shards: List[Shard], rank: int, group_si
         full[s.batch0:s.batch1, :, s.head0 * q_per_kv:s.head1 * q_per_kv] = \
             allbuf[r, : s.batch, :, : s.kv_heads * q_per_kv]
     return full
+
+
+class PeerGather:
+    """Fused output all-gather over peer memory for one decode-attention shape (rfsn_peer_gather).
+
+    Each rank holds ``local_seqs`` consecutive sequences (rank r: [r * local_seqs, (r + 1) *
+    local_seqs)) of the ``world * local_seqs`` in the gathered output ``full`` [total, Q, Hq, D]
+    fp16.  The constructor is collective: every rank allocates its peer-visible buffers
+    (rfsn_peer_alloc), the CUDA IPC handles are exchanged over the process group, and every rank
+    maps the others' (rfsn_peer_open).  Pass the instance as ``gather`` to a decode-attention call:
+    that launch then also leaves the whole batch's output in ``full`` on every rank.  Every rank
+    must make the same sequence of gathered launches, each rank on its own GPU."""
+
+    def __init__(self, local_seqs: int, queries: int, q_heads: int, head_dim: int, rank: int, world: int,
+                 device: torch.device, group=None):
+        import torch.distributed as dist
+        from . import _lib
+        if not 2 <= world <= _lib.RFSN_MAX_PEERS:
+            raise ValueError(f"peer gather needs 2..{_lib.RFSN_MAX_PEERS} ranks, got {world}")
+        self.rank, self.world = rank, world
+        self.total = local_seqs * world
+        self.full = torch.empty((self.total, queries, q_heads, head_dim), dtype=torch.float16, device=device)
+        buf_bytes = 2 * self.full.numel() * 2
+        self._flag_off = (buf_bytes + 255) // 256 * 256
+        self._step_off = self._flag_off + 8 * world
+        lib = _lib.lib()
+        with torch.cuda.device(device):
+            own = C.c_void_p()
+            handle = (C.c_char * 64)()
+            _lib.check("rfsn_peer_alloc", lib.rfsn_peer_alloc(self._step_off + 8, C.byref(own), handle))
+            self._own = own.value
+            handles: List[bytes] = [b""] * world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+            self._opened: List[int] = []
+            bases = []
+            for r in range(world):
+                if r == rank:
+                    bases.append(self._own)
+                    continue
+                ptr = C.c_void_p()
+                _lib.check("rfsn_peer_open", lib.rfsn_peer_open((C.c_char * 64).from_buffer_copy(handles[r]),
+                                                                C.byref(ptr)))
+                self._opened.append(ptr.value)
+                bases.append(ptr.value)
+        st = _lib.PeerGather()
+        st.num_ranks, st.rank = world, rank
+        st.seq_offset, st.total_seqs = rank * local_seqs, self.total
+        for r, base in enumerate(bases):
+            st.buffers[r] = base
+            st.flags[r] = base + self._flag_off
+        st.step = self._own + self._step_off
+        st.out_full = self.full.data_ptr()
+        self.struct = st
+        self.pointer = C.pointer(st)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (after every rank's last gathered launch)."""
+        from . import _lib
+        lib = _lib.lib()
+        for ptr in self._opened:
+            lib.rfsn_peer_close(C.c_void_p(ptr))
+        self._opened = []
+        if self._own:
+            lib.rfsn_peer_free(C.c_void_p(self._own))
+            self._own = None

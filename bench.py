@@ -398,7 +398,7 @@ def public_api_cache(w, dev):
     return cache
 
 
-def e2e_public_api(w, args, dev, world: int = 1, rank: int = 0, shards=None) -> dict:
+def e2e_public_api(w, args, dev, world: int = 1, rank: int = 0, shards=None, peer=None) -> dict:
     """The decode step through the public API: pinned host query in, host output out, every step.
 
     With N ranks each rank runs its own sequences and the outputs are all-gathered
@@ -413,13 +413,14 @@ def e2e_public_api(w, args, dev, world: int = 1, rank: int = 0, shards=None) -> 
         G = CFG["q_heads"] // CFG["kv_heads"]
 
     def step():
-        out = cache.attention_forward(h_q, causal=True)
-        if world > 1:
+        if world > 1 and peer is not None:  # the output all-gather fused into the attention kernel
+            h_full.copy_(cache.attention_forward(h_q, causal=True, gather=peer))
+        elif world > 1:
+            out = cache.attention_forward(h_q, causal=True)
             full = gather_outputs(out.unsqueeze(1), shards, rank, world, G)
             h_full.copy_(full[:, 0])
-            h_out.copy_(out)
         else:
-            h_out.copy_(out)  # device -> host read of the step's result
+            h_out.copy_(cache.attention_forward(h_q, causal=True))  # device -> host read of the result
 
     for _ in range(max(3, args.warmup)):
         step()
@@ -442,13 +443,15 @@ def e2e_public_api(w, args, dev, world: int = 1, rank: int = 0, shards=None) -> 
     from apple_b200 import kernels as K
     K.decode_attention(w["qz"], w["q"], ref, w["segs"], kv_heads=CFG["kv_heads"], qpos=w["qpos"], causal=True,
                        hot=w["hot"], warm=w["warm"])
-    err = float((ref[:, 0].float().cpu() - h_out.float()).abs().max())
+    got = h_full[rank * h_q.shape[0]:(rank + 1) * h_q.shape[0]] if world > 1 else h_out
+    err = float((ref[:, 0].float().cpu() - got.float()).abs().max())
     nb = h_q.numel() * h_q.element_size()
     cache.close()
+    how = "" if world == 1 else (" with the output all-gather fused over peer memory" if peer is not None
+                                 else " + NCCL all-gather of outputs")
     return {"value": world * 1e3 / ms, "unit": UNIT, "h2d_bytes_per_step": nb,
             "d2h_bytes_per_step": nb * (world if world > 1 else 1),
-            "api": "RFSNv10KVCacheMLX.attention_forward" + (" + NCCL all-gather of outputs" if world > 1 else ""),
-            "max_abs_diff_vs_kernel_call": err}
+            "api": "RFSNv10KVCacheMLX.attention_forward" + how, "max_abs_diff_vs_kernel_call": err}
 
 
 def replay_check(w, graph, out, eager_call) -> dict:
@@ -487,10 +490,14 @@ def run_b200(args) -> None:
     shards = plan_shards(CFG["batch"] * world, CFG["kv_heads"], world)
     assert shards[rank].batch == CFG["batch"]
     launches_per_step = 1  # fused decode attention (row merge done in-kernel by the last CTA of each row)
+    peer = None
+    if world > 1 and args.gather == "peer":
+        from apple_b200.sharding import PeerGather
+        peer = PeerGather(CFG["batch"], 1, CFG["q_heads"], CFG["head_dim"], rank, world, dev)
 
-    def attn():
+    def attn(gather=peer):
         K.decode_attention(w["qz"], w["q"], out, w["segs"], kv_heads=CFG["kv_heads"], qpos=w["qpos"], causal=True,
-                           hot=w["hot"], warm=w["warm"])
+                           hot=w["hot"], warm=w["warm"], gather=gather)
 
     for _ in range(max(3, args.warmup)):
         attn()
@@ -507,7 +514,7 @@ def run_b200(args) -> None:
 
     def step():
         graph.replay()
-        if world > 1:
+        if world > 1 and peer is None:
             gather_outputs(out, shards, rank, world, CFG["q_heads"] // CFG["kv_heads"], out=full)
 
     for _ in range(max(3, args.warmup)):
@@ -533,21 +540,32 @@ def run_b200(args) -> None:
     ms_per_step = ms / args.steps
     value = world * 1e3 / ms_per_step
 
-    # kernel-only duration for the roofline: the same graph without the collective
+    # kernel-only duration for the roofline: the attention alone, without the all-gather
+    local_graph = graph
+    if peer is not None:
+        for _ in range(3):
+            attn(None)
+        torch.cuda.synchronize()
+        local_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(local_graph, stream=side):
+            attn(None)
     torch.cuda.synchronize()
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record(stream)
     for _ in range(args.steps):
-        graph.replay()
+        (local_graph.replay() if peer is not None else graph.replay())
     e3.record(stream)
     torch.cuda.synchronize()
     kern_ms = e2.elapsed_time(e3) / args.steps
+    if peer is not None:
+        # the gathered output on this rank holds every rank's shard: this rank's rows equal its own
+        gather_ok = bool(torch.equal(peer.full[rank * CFG["batch"]:(rank + 1) * CFG["batch"]], out))
     replay = replay_check(w, graph, out, lambda o: K.decode_attention(
         w["qz"], w["q"], o, w["segs"], kv_heads=CFG["kv_heads"], qpos=w["qpos"], causal=True, hot=w["hot"],
         warm=w["warm"]))
 
-    e2e = e2e_public_api(w, args, dev, world, rank, shards)
-    del graph
+    e2e = e2e_public_api(w, args, dev, world, rank, shards, peer)
+    del graph, local_graph
     if world > 1:
         dist.barrier()
     if rank == 0:
@@ -567,6 +585,12 @@ def run_b200(args) -> None:
                              "kernel_ms_covers": "fused attention incl. in-kernel LSE merge (one graph replay per step)"},
                 "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "clocks": clocks.summary(),
                 "replay_check": replay}
+        if world > 1:
+            line["gather"] = {"mode": "fused into the attention kernel over NVLink peer memory" if peer is not None
+                              else "NCCL all_gather_into_tensor after each graph replay",
+                              "us_per_step_over_local_kernel": (ms_per_step - kern_ms) * 1e3}
+            if peer is not None:
+                line["gather"]["own_rows_match"] = gather_ok
         if world == 1:
             # the spawned pool starts only after the GPU measurements: its idle workers cost
             # the host-bound e2e loop about 6% when they were alive during it
@@ -578,6 +602,10 @@ def run_b200(args) -> None:
                                     "kind": "port", "sample": cpu.describe() + "; mean of 3 steps"}
         print(json.dumps(line))
     if world > 1:
+        torch.cuda.synchronize()
+        dist.barrier()
+        if peer is not None:
+            peer.close()
         dist.destroy_process_group()
 
 
@@ -1431,6 +1459,9 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
+                    help="decode workload at N > 1: the output all-gather fused into the attention kernel over "
+                         "peer memory (default), or NCCL all_gather_into_tensor after each step")
     ap.add_argument("--layers", type=int, default=0,
                     help="stack workload only: number of layers (default: the 22 of configs[2]); fewer layers "
                          "make a small case for profiling captures")

@@ -149,6 +149,44 @@ typedef struct rfsn_segment {
   int32_t reserved[3];
 } rfsn_segment;
 
+/* Output all-gather fused into decode attention, over NVLink peer memory.
+ *
+ * Work is sharded across the GPUs of one node by sequence (rank r holds sequences
+ * [seq_offset, seq_offset + batch) of total_seqs); the output projection needs every
+ * sequence's attention output on every rank.  Instead of a separate all-gather, the CTA that
+ * merges a row stores its fp16 output straight into every rank's gathered-output buffer (plain
+ * peer stores through IPC-mapped addresses), and the launch's last CTA then signals every rank
+ * and waits (bounded, 1 s) until every rank has signalled the same launch, after which it copies
+ * the complete gathered output into out_full.
+ *
+ * buffers[k]: rank k's gathered-output buffers, 2 x total_seqs x queries x q_heads x head_dim fp16
+ * (two, used by launch parity, so a rank one launch ahead never overwrites a buffer another rank
+ * is still copying); flags[k]: rank k's num_ranks uint64 flag words; step: this rank's uint64
+ * launch counter.  All of buffers[rank], flags[rank] and step live in one allocation made by
+ * rfsn_peer_alloc (zeroed); the other ranks' come from rfsn_peer_open.  Every rank must make the
+ * same sequence of gathered launches.  Ranks must be on distinct GPUs: the wait is on other
+ * GPUs' launches. */
+#define RFSN_MAX_PEERS 8
+typedef struct rfsn_peer_gather {
+  int32_t num_ranks;
+  int32_t rank;
+  int64_t seq_offset;
+  int64_t total_seqs;
+  uint16_t* buffers[RFSN_MAX_PEERS];
+  uint64_t* flags[RFSN_MAX_PEERS];
+  uint64_t* step;
+  uint16_t* out_full;  /* [total_seqs][queries][q_heads][head_dim] fp16 on this device */
+} rfsn_peer_gather;
+
+/* Peer-visible device memory for rfsn_peer_gather: cudaMalloc of `bytes` (zeroed) and its CUDA
+ * IPC handle (64 bytes written to ipc_handle); rfsn_peer_open maps another process's allocation
+ * from its handle on the current device; rfsn_peer_close unmaps it; rfsn_peer_free frees one's
+ * own allocation. */
+int rfsn_peer_alloc(size_t bytes, void** ptr, void* ipc_handle);
+int rfsn_peer_open(const void* ipc_handle, void** ptr);
+int rfsn_peer_close(void* ptr);
+int rfsn_peer_free(void* ptr);
+
 /* Fused decode attention — RFSNv10KVCacheMLX.attention_forward (cache.py:395-428) =
  * materialize_window (:344-393) + _blockwise_exact_attention (attention.py:39-105),
  * without materialising the window: PQ/RVQ/sparse codes are decoded inside a
@@ -184,6 +222,8 @@ typedef struct rfsn_attn_args {
   int64_t q_batch_stride;          /* elements from one sequence's queries to the next (a multiple of 8, at least
                                       queries*q_heads*head_dim); 0 = packed.  Lets q be a view of a wider
                                       projection output. */
+  const rfsn_peer_gather* gather;  /* optional fused output all-gather over peer memory (NULL = none);
+                                      device_status 5 = a peer's signal did not arrive in time */
 } rfsn_attn_args;
 
 /* Bytes of device workspace rfsn_decode_attention needs for these arguments. */
