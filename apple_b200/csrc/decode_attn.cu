@@ -200,9 +200,23 @@ __device__ __noinline__ void gather_finish(const AttnParams& p, int parity, vola
   }
   named_bar_sync(2, threads);
   if (!*ok) return;
+  // the copy is latency-bound in one CTA: every thread keeps 8 loads in flight
   const uint4* src = reinterpret_cast<const uint4*>(p.peer_buf[p.my_rank] + (int64_t)parity * p.full_elems);
   uint4* dst = reinterpret_cast<uint4*>(p.out_full);
-  for (int64_t i = threadIdx.x; i < p.full_elems / 8; i += threads) dst[i] = __ldcg(src + i);
+  const int64_t n = p.full_elems / 8;
+  for (int64_t base = threadIdx.x; base < n; base += 8 * (int64_t)threads) {
+    uint4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int64_t i = base + (int64_t)u * threads;
+      if (i < n) v[u] = __ldcg(src + i);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int64_t i = base + (int64_t)u * threads;
+      if (i < n) dst[i] = v[u];
+    }
+  }
 }
 
 // Gather mode: one output element into every rank's gathered-output buffer of this parity.
@@ -264,6 +278,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
     *abort = 0;
     // gather mode: this launch's buffer parity (the last CTA advances the step afterwards)
     abort[2] = p.npeers ? (int)(*reinterpret_cast<volatile unsigned long long*>(p.step) & 1ull) : 0;
+    abort[3] = 0;  // gather mode: set when this CTA stored a merged row to the peers
     fence_mbar_init();
   }
   __syncthreads();  // barriers initialised; the producer starts streaming at once
@@ -629,6 +644,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
       if (*merge_flag) {  // this CTA finished the row: merge its pieces
         __threadfence();
         merge_row(p, row, threadIdx.x, NW * 32, abort[2]);
+        if (p.npeers && threadIdx.x == 0) abort[3] = 1;
       }
     }
     if (++stage == p.stages) {
@@ -642,8 +658,9 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
   // The done count is a plain counter that is zero between launches (the last CTA
   // resets it): one atomicAdd per CTA, where compare-and-swap tickets retried by
   // 148 CTAs finishing together serialise on round trips.
-  if (p.npeers) {  // every consumer's peer stores are ordered before this CTA counts itself done
-    __threadfence_system();
+  if (p.npeers) {  // a CTA that stored rows to the peers orders them before it counts itself done
+    named_bar_sync(2, NW * 32);
+    if (abort[3]) __threadfence_system();
     named_bar_sync(2, NW * 32);
   }
   if (threadIdx.x == 0) {

@@ -135,7 +135,7 @@ def build_workload(device, seed):
 
 # NVML polling period.  Only rank 0 samples: NVML polling from every rank measurably
 # slowed the per-step NCCL gather at N > 1.
-CLOCK_PERIOD_S = float(os.environ.get("RFSN_CLOCK_PERIOD_MS", "5")) / 1e3
+CLOCK_PERIOD_S = float(os.environ.get("RFSN_CLOCK_PERIOD_MS", "2")) / 1e3
 
 
 class ClockSampler:
@@ -364,15 +364,38 @@ def run_reference(args) -> None:
 # B200 arm
 # ---------------------------------------------------------------------------
 
+KERNEL_SOURCES = ("decode_attn.cu", "rfsn_attn_chunk.cuh", "rfsn_attn_util.cuh", "rfsn_common.cuh", "rfsn_decode.cuh",
+                  "rfsn_layout.h")
+
+
+def kernel_source_hash() -> str:
+    """sha256 (first 16 hex digits) of the fused decode kernel's sources."""
+    import hashlib
+    h = hashlib.sha256()
+    for name in KERNEL_SOURCES:
+        h.update((ROOT / "apple_b200" / "csrc" / name).read_bytes())
+    return h.hexdigest()[:16]
+
+
 def ncu_traffic() -> dict:
-    """DRAM bytes per launch of the fused kernel from the committed ncu summary (None if absent)."""
+    """DRAM bytes per launch of the fused kernel from the committed ncu summary (None if absent).
+    The summary records the hash of the kernel sources it was captured from; when the sources
+    changed since, the figure is reported as stale (null)."""
     p = ROOT / "profiles" / "decode_attn_cfg2.md"
-    out = {"traffic": None, "source": None}
+    out = {"traffic": None, "source": None, "stale": None}
     if p.exists():
+        recorded = None
         for line in p.read_text().splitlines():
-            if line.strip().startswith("dram_bytes_per_launch:"):
-                out["traffic"] = float(line.split(":", 1)[1].strip().split()[0])
+            t = line.strip()
+            if t.startswith("dram_bytes_per_launch:"):
+                out["traffic"] = float(t.split(":", 1)[1].strip().split()[0])
                 out["source"] = "profiles/decode_attn_cfg2.md"
+            elif t.startswith("kernel_source_sha:"):
+                recorded = t.split(":", 1)[1].strip()
+        out["stale"] = recorded != kernel_source_hash()
+        if out["stale"]:
+            out["stale_reason"] = f"captured from sources {recorded}, built from {kernel_source_hash()}"
+            out["traffic"] = None
     return out
 
 
@@ -521,17 +544,22 @@ def run_b200(args) -> None:
         step()
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # one event per step boundary: the K-step total plus the spread of single steps
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     with ClockSampler(dev, active=rank == 0, devices=world) as clocks:
         if world > 1:
             dist.barrier()  # after the sampler started, so every rank enters the timed region together
         torch.cuda.synchronize()
-        e0.record(stream)
-        for _ in range(args.steps):
+        ev[0].record(stream)
+        for i in range(args.steps):
             step()
-        e1.record(stream)
+            ev[i + 1].record(stream)
         torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
+    ms = ev[0].elapsed_time(ev[-1])
+    per = np.array([ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)])
+    spread = {"median_ms": float(np.median(per)), "p10_ms": float(np.percentile(per, 10)),
+              "p90_ms": float(np.percentile(per, 90)), "min_ms": float(per.min()), "max_ms": float(per.max()),
+              "note": "single-step durations between consecutive events on the launch stream"}
     if world > 1:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -580,11 +608,12 @@ def run_b200(args) -> None:
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                              "frac": achieved / peak, "traffic": traffic["traffic"],
                              "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, burst copy)",
-                             "traffic_source": traffic["source"],
+                             "traffic_source": traffic["source"], "traffic_stale": traffic["stale"],
+                             "kernel_source_sha": kernel_source_hash(),
                              "algorithmic_bytes_per_step": nbytes, "kernel_ms": kern_ms,
                              "kernel_ms_covers": "fused attention incl. in-kernel LSE merge (one graph replay per step)"},
                 "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "clocks": clocks.summary(),
-                "replay_check": replay}
+                "replay_check": replay, "step_spread": spread}
         if world > 1:
             line["gather"] = {"mode": "fused into the attention kernel over NVLink peer memory" if peer is not None
                               else "NCCL all_gather_into_tensor after each graph replay",
@@ -1456,7 +1485,7 @@ def main() -> None:
         return
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
