@@ -22,7 +22,7 @@ PKG = CSRC.parent
 ROOT = PKG.parent
 BUILD = CSRC / "_build"
 LIB = PKG / "librfsn_b200.so"
-SOURCES = ["capi.cu", "encode.cu", "encode_tc.cu", "decode_attn.cu", "layer_ops.cu", "route.cu", "codebook_ops.cu"]
+SOURCES = ["capi.cu", "encode.cu", "encode_tc.cu", "decode_attn.cu", "layer_ops.cu", "route.cu", "codebook_ops.cu", "linear.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC,-O2",
          f"-I{ROOT / 'include'}", f"-I{CSRC}"]

@@ -144,24 +144,6 @@ __device__ __forceinline__ int row_pieces(const AttnParams& p, int64_t row, int6
   return (int)(c1 - c0 + 1);
 }
 
-constexpr unsigned long long kTagMask = (1ull << 48) - 1ull;
-
-// Count one arrival on ticket *t for the launch tagged `tag`; returns 1 if it
-// was arrival number `target` of this launch, 0 if not, -1 if the ticket could
-// not be taken.  A ticket holding another launch's tag counts as zero.  Each
-// failed swap means another CTA's succeeded, and at most 0xffff CTAs arrive on
-// one ticket, so the loop bound is never reached in a healthy launch.
-__device__ __forceinline__ int take_ticket(unsigned long long* t, unsigned long long tag, int target) {
-  unsigned long long cur = *reinterpret_cast<volatile unsigned long long*>(t);
-  for (int it = 0; it < 0x10000 + 16; ++it) {
-    const unsigned long long nxt = ((cur >> 16) == tag) ? cur + 1ull : ((tag << 16) | 1ull);
-    const unsigned long long prev = atomicCAS(t, cur, nxt);
-    if (prev == cur) return (int)(nxt & 0xffffull) == target ? 1 : 0;
-    cur = prev;
-  }
-  return -1;
-}
-
 // Log-sum-exp merge of a row's pieces (m in log2 units) and the fp16 output
 // (attention.py:104-105: a row whose every key is masked outputs zeros).
 __device__ __forceinline__ void st_release_sys(unsigned long long* a, unsigned long long v) {

@@ -21,6 +21,7 @@
 
 #include "rfsn_api_internal.h"
 #include "rfsn_common.cuh"
+#include "rfsn_elementwise.cuh"
 
 namespace rfsn {
 
@@ -161,17 +162,6 @@ __global__ void silu_mul_kernel(const uint16_t* __restrict__ g, const uint16_t* 
     const float a = h2f(f2h(__fmul_rn(gv, sg)));
     y[i] = f2h(__fmul_rn(a, h2f(u[i])));
   }
-}
-
-__device__ __forceinline__ float rh(float v) { return __half2float(__float2half_rn(v)); }
-
-__device__ __forceinline__ uint16_t gelu_tanh_f16(uint16_t xh) {
-  const float x = h2f(xh);
-  const float x3 = rh(__fmul_rn(__fmul_rn(x, x), x));
-  const float inner = rh(__fadd_rn(x, rh(__fmul_rn(0.044715f, x3))));
-  const float t = rh(tanhf(rh(__fmul_rn(0.7978845608f, inner))));
-  const float half_x = rh(__fmul_rn(0.5f, x));
-  return f2h(__fmul_rn(half_x, rh(__fadd_rn(1.0f, t))));
 }
 
 __global__ void gelu_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ y, int64_t n, int vec) {

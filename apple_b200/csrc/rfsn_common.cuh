@@ -92,6 +92,24 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 __device__ __forceinline__ uint16_t f2h(float f) { return __half_as_ushort(__float2half_rn(f)); }
 
+constexpr unsigned long long kTagMask = (1ull << 48) - 1ull;
+
+// Count one arrival on ticket *t for the launch tagged `tag` (a launch counter the kernel
+// keeps in its workspace); returns 1 if it was arrival number `target` of this launch, 0 if
+// not, -1 if the ticket could not be taken.  A ticket holding another launch's tag counts as
+// zero.  Each failed swap means another CTA's succeeded, and at most 0xffff CTAs arrive on
+// one ticket, so the loop bound is never reached in a healthy launch.
+__device__ __forceinline__ int take_ticket(unsigned long long* t, unsigned long long tag, int target) {
+  unsigned long long cur = *reinterpret_cast<volatile unsigned long long*>(t);
+  for (int it = 0; it < 0x10000 + 16; ++it) {
+    const unsigned long long nxt = ((cur >> 16) == tag) ? cur + 1ull : ((tag << 16) | 1ull);
+    const unsigned long long prev = atomicCAS(t, cur, nxt);
+    if (prev == cur) return (int)(nxt & 0xffffull) == target ? 1 : 0;
+    cur = prev;
+  }
+  return -1;
+}
+
 // Named barrier among the first `threads` threads of the CTA (id != 0).
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

@@ -445,6 +445,49 @@ def route_topk(q: torch.Tensor, centroids: torch.Tensor, kv_heads: int, k: int,
     return ids[:k], scores[:C]
 
 
+_LIN_WORKSPACE: dict = {}
+LINEAR_NONE, LINEAR_RESIDUAL, LINEAR_GELU = 0, 1, 2
+
+
+def linear_supported(x: torch.Tensor, w: torch.Tensor) -> bool:
+    """Shapes the weight-streaming kernel takes: fp16, M <= 32 rows, N % 64 == 0, K % 256 == 0."""
+    M = x.numel() // x.shape[-1] if x.shape[-1] else 0
+    return (x.is_cuda and x.dtype == torch.float16 and w.dtype == torch.float16 and w.dim() == 2
+            and 0 < M <= 32 and w.shape[0] % 64 == 0 and w.shape[1] % 256 == 0 and x.shape[-1] == w.shape[1])
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = None, gelu: bool = False,
+           out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y = x @ w^T (rfsn_linear_f16): fp16 x [..., K] with at most 32 rows, fp16 w [N, K];
+    residual: y = fp16(fp16(acc) + residual); gelu: y = the layer's fp16 tanh-GELU of fp16(acc)."""
+    _need_cuda(x, "x")
+    K = x.shape[-1]
+    N = w.shape[0]
+    x2 = x.reshape(-1, K)
+    if x2.stride(-1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    w = w if w.is_contiguous() else w.contiguous()
+    y = out if out is not None else torch.empty((M, N), dtype=torch.float16, device=x.device)
+    y2 = y.reshape(M, N)
+    r2 = None
+    if residual is not None:
+        r2 = residual.reshape(M, N)
+        if r2.stride(-1) != 1:
+            r2 = r2.contiguous()
+    nbytes = C.c_size_t(0)
+    call("rfsn_linear_workspace_size", M, N, K, C.byref(nbytes))
+    key = (x.device.index,)
+    ws = _LIN_WORKSPACE.get(key)
+    if ws is None or ws.numel() < nbytes.value:
+        ws = torch.zeros(max(nbytes.value, 1 << 20), dtype=torch.uint8, device=x.device)
+        _LIN_WORKSPACE[key] = ws
+    mode = LINEAR_RESIDUAL if residual is not None else (LINEAR_GELU if gelu else LINEAR_NONE)
+    call("rfsn_linear_f16", _ptr(x2), x2.stride(0), _ptr(w), w.stride(0), _ptr(r2), r2.stride(0) if r2 is not None else N,
+         _ptr(y2), y2.stride(0), M, N, K, mode, _ptr(ws), ws.numel(), None, _stream(x.device.index))
+    return y.reshape(*x.shape[:-1], N) if out is None else y
+
+
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
     """fp16 RMSNorm over the last dim in one launch (fp32 math, fp32 weight)."""
     _need_cuda(x, "x")

@@ -3,9 +3,10 @@
 ``RFSNDecoderLayerMLX`` keeps the reference's structure and API: RMSNorm ->
 q/k/v projections -> cache update -> cache-backed fused decode attention (or
 dense causal attention without a cache) -> o_proj + residual -> RMSNorm ->
-GELU FFN (2x) + residual.  Projections are plain torch GEMMs (cuBLAS); the
-attention, every quantizer operation, the RMSNorms and the GELU run in
-librfsn_b200.so (one launch each).  Extensions:
+GELU FFN (2x) + residual.  Decode-sized projections (at most 32 rows) stream
+their weights with rfsn_linear_f16, the FFN's GELU and residual add fused
+into its epilogues; larger ones (prefill) are cuBLAS GEMMs.  The attention,
+every quantizer operation and the RMSNorms run in librfsn_b200.so too.  Extensions:
 ``num_kv_heads`` (GQA) and ``batch_size`` > 1 sequences per cache.
 """
 from __future__ import annotations
@@ -45,11 +46,25 @@ class _Linear:
         self._cast = None  # weight in the activations' dtype, refreshed when the weight is replaced
         self._src = None
 
-    def __call__(self, x: torch.Tensor) -> torch.Tensor:
-        # like mlx.nn.Linear: the weight is cast to the activations' dtype (fp16 in the layer)
-        if self._cast is None or self._cast.dtype != x.dtype or self._src is not self.weight:
-            self._cast, self._src = self.weight.to(x.dtype), self.weight
-        return torch.nn.functional.linear(x, self._cast)
+    def cast(self, dtype: torch.dtype) -> torch.Tensor:
+        """The weight in the activations' dtype (mlx.nn.Linear casts it to x's dtype), cached."""
+        if self._cast is None or self._cast.dtype != dtype or self._src is not self.weight:
+            self._cast, self._src = self.weight.to(dtype).contiguous(), self.weight
+        return self._cast
+
+    def __call__(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None, gelu: bool = False) -> torch.Tensor:
+        """x @ W^T; decode-sized fp16 products (at most 32 rows) stream W with rfsn_linear_f16, which
+        also fuses the residual add (fp16(fp16(y) + residual)) or the layer's fp16 tanh-GELU; other
+        shapes run the GEMM in cuBLAS and the epilogue separately."""
+        w = self.cast(x.dtype)
+        if K.linear_supported(x, w):
+            return K.linear(x, w, residual=residual, gelu=gelu)
+        y = torch.nn.functional.linear(x, w)
+        if gelu:
+            y = K.gelu_tanh(y) if y.dtype == torch.float16 and y.is_cuda else _gelu(y)
+        if residual is not None:
+            y = residual + y
+        return y
 
 
 class _RMSNorm:
@@ -118,7 +133,8 @@ class RFSNDecoderLayerMLX:
                 or src[0] is not ws[0] or src[1] is not ws[1] or src[2] is not ws[2]):
             self._qkv_w = torch.cat([w.to(a.dtype) for w in ws], 0)
             self._qkv_src = ws
-        y = torch.nn.functional.linear(a, self._qkv_w)
+        y = K.linear(a, self._qkv_w) if K.linear_supported(a, self._qkv_w) else \
+            torch.nn.functional.linear(a, self._qkv_w)
         nq = self.num_heads * self.head_dim
         nk = self.num_kv_heads * self.head_dim
         return y[..., :nq], y[..., nq:nq + nk], y[..., nq + nk:]
@@ -183,10 +199,8 @@ class RFSNDecoderLayerMLX:
         else:
             hidden = residual + attn_out
             ffn_input = self.ffn_norm(hidden).to(torch.float16)
-        up = self.ffn_up(ffn_input)
-        act = K.gelu_tanh(up) if up.dtype == torch.float16 else _gelu(up)  # one launch for the fp16 chain
-        ffn_out = _as(self.ffn_down(act), hidden.dtype)
-        return hidden + ffn_out
+        act = self.ffn_up(ffn_input, gelu=True)  # GELU fused into the projection's epilogue
+        return self.ffn_down(act, residual=hidden)  # residual add fused likewise
 
 
 def calibrate_quantizer(quantizer: HybridQuantizerMLX, calibration_vectors: torch.Tensor, num_iterations: int = 20,

@@ -9,8 +9,10 @@ residual -> RMSNorm -> SwiGLU MLP + residual.
 On this path the RMSNorms (with the residual add folded into the second),
 RoPE and the SwiGLU product are one librfsn_b200.so launch each, in the
 adapter's operation order and rounding points; the q/k/v and gate/up
-projections are one GEMM each over concatenated weights (cuBLAS); decode
-attention is the fused compressed-KV kernel.  The cache stores the KV heads
+projections are one product each over concatenated weights (the weight-
+streaming rfsn_linear_f16 at decode sizes, with the final residual add fused
+into the down projection; cuBLAS otherwise); decode attention is the fused
+compressed-KV kernel.  The cache stores the KV heads
 once (GQA) instead of the reference's _repeat_kv'd copies (llama32_adapter.py:
 380-386, 580-581): attention reads KV head h // group for query head h, the
 same values.  Batch > 1 is an extension (the reference adapter takes batch 1).
@@ -56,6 +58,11 @@ def _position_table(component: Any, seq_len: int, head_dim: int, device) -> torc
     if t.shape[1] != head_dim:
         raise ValueError(f"Expected rotary head dim {head_dim}, got {t.shape[1]}")
     return t.to(device=device, dtype=torch.float16).contiguous()
+
+
+def _linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """llama32_adapter.py:492-494: decode-sized products stream W with rfsn_linear_f16, others cuBLAS."""
+    return K.linear(x, w) if K.linear_supported(x, w) else torch.nn.functional.linear(x, w)
 
 
 class Llama32DecoderLayerMLX:
@@ -148,7 +155,7 @@ class Llama32DecoderLayerMLX:
         """llama32_adapter.py:570-582 (KV heads kept, not repeated)."""
         B, S, _ = hidden.shape
         normed, _ = K.llama_rms_norm(hidden, self.input_layernorm_weight, self.rms_norm_eps)
-        y = torch.nn.functional.linear(normed, self._qkv_w)
+        y = _linear(normed, self._qkv_w)
         nq, nk = self.num_heads * self.head_dim, self.num_key_value_heads * self.head_dim
         q = K.rope(y[..., :nq].unflatten(-1, (self.num_heads, self.head_dim)), cos, sin)
         k = K.rope(y[..., nq:nq + nk].unflatten(-1, (self.num_key_value_heads, self.head_dim)), cos, sin)
@@ -202,11 +209,13 @@ class Llama32DecoderLayerMLX:
             attended = attended.reshape(B, 1, self.num_heads * self.head_dim)
         else:
             attended = _dense_exact_attention(q, k, v, self.scale, causal=True).reshape(B, S, -1)
-        attn_out = torch.nn.functional.linear(attended.to(torch.float16), self.o_proj_weight)
+        attn_out = _linear(attended.to(torch.float16), self.o_proj_weight)
         # hidden = residual + attn_out and the post-attention RMSNorm in one launch
         mlp_in, hidden = K.llama_rms_norm(attn_out, self.post_attention_layernorm_weight, self.rms_norm_eps,
                                           residual=residual)
-        gu = torch.nn.functional.linear(mlp_in, self._gate_up_w)
+        gu = _linear(mlp_in, self._gate_up_w)
         inter = self.gate_proj_weight.shape[0]
         act = K.silu_mul(gu[..., :inter], gu[..., inter:])
+        if K.linear_supported(act, self.down_proj_weight):  # residual add fused into the epilogue
+            return K.linear(act, self.down_proj_weight, residual=hidden)
         return hidden + torch.nn.functional.linear(act, self.down_proj_weight)

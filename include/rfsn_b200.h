@@ -288,6 +288,20 @@ int rfsn_gelu_tanh_f16(const uint16_t* x, uint16_t* y, int64_t n, void* stream);
 int rfsn_add_rmsnorm_f16(const uint16_t* x, const uint16_t* b, uint16_t* sum, const float* weight, uint16_t* y,
                          int64_t rows, int dim, float eps, void* stream);
 
+/* Weight-streaming projection for decode-sized row counts: y[M][N] = x[M][K] W[N][K]^T with fp32
+ * accumulation, fp16 result — the decoder layers' projections (mlx.nn.Linear in RFSNDecoderLayerMLX,
+ * rfsn_v10_mlx_ane_complete.py:114-172; _linear, llama32_adapter.py:492-494), with an optional fused
+ * epilogue: 0 none, 1 y = fp16(fp16(acc) + r) (the residual add after o_proj / ffn_down), 2 y =
+ * gelu_tanh(fp16(acc)) rounded to fp16 after every operation (the FFN activation, attention.py:
+ * 137-138).  M <= 32, N % 64 == 0, K % 256 == 0; row strides in elements, x and W rows 16-byte
+ * aligned.  The workspace (rfsn_linear_workspace_size bytes, 256-byte aligned) holds a launch
+ * counter, per-tile tickets and fp32 partials: zero it once when allocated, reuse it without
+ * clearing, never share it between calls that overlap in time. */
+int rfsn_linear_workspace_size(int M, int N, int K, size_t* bytes);
+int rfsn_linear_f16(const uint16_t* x, int64_t ldx, const uint16_t* w, int64_t ldw, const uint16_t* r, int64_t ldr,
+                    uint16_t* y, int64_t ldy, int M, int N, int K, int epilogue, void* workspace,
+                    size_t workspace_bytes, int32_t* device_status, void* stream);
+
 /* Affine low-bit codebook quantization — the reference's quantize_codebooks_for_ane path
  * (_quantize_matrix / _dequantize_matrix, quantization.py:36-89, used at :159-175 and :277-293),
  * which calls MLX's mx.quantize / mx.dequantize (affine mode).  For each group of `group`
