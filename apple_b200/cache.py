@@ -562,21 +562,23 @@ class RFSNv10KVCacheMLX:
         # a pinned host query is uploaded asynchronously on the current stream (ordered
         # before the attention kernel); keep it unchanged until the call's result is read
         uploaded = not q.is_cuda
-        q = q.to(device=self.device, dtype=torch.float16, non_blocking=bool(uploaded and q.is_pinned()))
+        if uploaded or q.dtype != torch.float16 or self.device.index is None or q.get_device() != self.device.index:
+            q = q.to(device=self.device, dtype=torch.float16, non_blocking=bool(uploaded and q.is_pinned()))
         # a view whose sequences are each packed (e.g. the query heads of a wider projection
         # output) is read in place through the kernel's batch stride; a contiguous upload is a
         # fresh allocation, packed and aligned by construction
-        if uploaded and q.is_contiguous():
-            pack = lambda t: t  # noqa: E731
-        else:
-            pack = lambda t: t if K.queries_packed(t) else t.contiguous()  # noqa: E731
+        check = not (uploaded and q.is_contiguous())
         if self.batch == 1 and q.dim() == 3:
-            return pack(q.unsqueeze(0)), True                 # [1, Q, Hq, D]
-        if q.dim() == 3 and q.shape[0] == self.batch:
-            return pack(q.unsqueeze(1)), False                # [B, 1, Hq, D]
-        if q.dim() == 4 and q.shape[0] == self.batch:
-            return pack(q), False
-        raise ValueError(f"q must be [Q, H, D] (batch 1), [B, H, D] or [B, Q, H, D]; got {tuple(q.shape)}")
+            qb, squeeze = q.unsqueeze(0), True                # [1, Q, Hq, D]
+        elif q.dim() == 3 and q.shape[0] == self.batch:
+            qb, squeeze = q.unsqueeze(1), False               # [B, 1, Hq, D]
+        elif q.dim() == 4 and q.shape[0] == self.batch:
+            qb, squeeze = q, False
+        else:
+            raise ValueError(f"q must be [Q, H, D] (batch 1), [B, H, D] or [B, Q, H, D]; got {tuple(q.shape)}")
+        if check and not K.queries_packed(qb):
+            qb = qb.contiguous()
+        return qb, squeeze
 
     def _qpos(self, query_positions, start, end, qb: torch.Tensor) -> Optional[torch.Tensor]:
         """Per-query last visible positions [B, Q, Hq] int32, or None when every query sits at
@@ -617,7 +619,11 @@ class RFSNv10KVCacheMLX:
 
         gather (extension, multi-GPU): a sharding.PeerGather whose ranks each hold an equal batch
         shard; the kernel then also all-gathers the outputs over peer memory and the call returns
-        the whole batch's output (gather.full, [total, Q, Hq, D], as [total, Hq, D] for one query)."""
+        the whole batch's output (gather.full, [total, Q, Hq, D], as [total, Hq, D] for one query).
+
+        out (extension): a contiguous fp16 tensor with q's element count to write the result to.
+        A pinned host tensor is written by the kernel itself over the bus (no separate copy), and
+        the call then waits for the stream, so the host holds the result when it returns."""
         del pq_codebook, rvq_codebook  # ignored by the reference too (cache.py:406)
         if self.quantizer is None:
             raise RuntimeError("Cache cannot run attention before update() provides a quantizer")
@@ -648,8 +654,15 @@ class RFSNv10KVCacheMLX:
                 self._plan_cache[key] = (segs, dict(stats), shape)
         stats["query_tokens"] = int(qb.shape[1])  # queries per sequence (q.shape[0] for one sequence)
         self.last_access_stats = stats
+        host_out = out is not None and not out.is_cuda
+        if host_out and not out.is_pinned():
+            raise ValueError("a host out must be pinned memory: the kernel writes it over the bus")
         if out is None:
             out = torch.empty(qb.shape, dtype=torch.float16, device=qb.device)
+        elif out.shape != qb.shape:
+            if out.numel() != qb.numel() or not out.is_contiguous():
+                raise ValueError(f"out must be contiguous with {qb.numel()} elements; got {tuple(out.shape)}")
+            out = out.view(qb.shape)
         qpos = self._qpos(query_positions, start, end, qb) if causal else None
         # without a cold tier or router, a prepared call is reused across steps: its key is
         # the segments' stores and slots plus the shapes and buffers, and each step patches
@@ -672,6 +685,8 @@ class RFSNv10KVCacheMLX:
                     self._attn_calls.clear()
                 self._attn_calls[ck] = entry
         K.run_attention(entry, qb, out, qpos)
+        if host_out:  # the kernel's stores to host memory are complete and visible
+            torch.cuda.current_stream(qb.device).synchronize()
         if gather is not None:
             full = gather.full
             return full[:, 0] if (q.dim() == 3 and not squeeze) else full

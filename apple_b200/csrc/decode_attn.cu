@@ -247,6 +247,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
   uint16_t* s_pq = reinterpret_cast<uint16_t*>(smem + p.smem_pq);
   uint16_t* s_pqsw = reinterpret_cast<uint16_t*>(smem + p.smem_pqsw);  // 4-dim presets; PQ-only: 3 V copies
   uint16_t* s_rvq = reinterpret_cast<uint16_t*>(smem + p.smem_rvq);
+  griddep_launch();  // a projection launched after this kernel may start streaming its weights
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;

@@ -54,6 +54,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const uint16_t* x
                                                                uint16_t* __restrict__ y, int dim, float eps,
                                                                int vec) {
   __shared__ float s_part[kNormThreads / 32];
+  griddep_launch();  // a projection launched after this kernel may start streaming its weights
   const int64_t row = blockIdx.x;
   const uint16_t* xr = x + row * dim;
   uint16_t* yr = y + row * dim;

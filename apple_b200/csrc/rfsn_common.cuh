@@ -110,6 +110,13 @@ __device__ __forceinline__ int take_ticket(unsigned long long* t, unsigned long 
   return -1;
 }
 
+// Programmatic dependent launch.  griddep_wait: this thread waits until the grids this launch
+// depends on have completed and their memory is visible (a no-op for a launch without that
+// dependency).  griddep_launch: this CTA lets dependent launches be scheduled early; they still
+// wait in griddep_wait before touching memory this grid writes.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Named barrier among the first `threads` threads of the CTA (id != 0).
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

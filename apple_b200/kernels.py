@@ -449,11 +449,24 @@ _LIN_WORKSPACE: dict = {}
 LINEAR_NONE, LINEAR_RESIDUAL, LINEAR_GELU = 0, 1, 2
 
 
+# Whether the decoder layers run their decode-sized projections on rfsn_linear_f16 (with the
+# residual add and the GELU fused into its epilogue) instead of cuBLAS.  Off: at the config-3
+# layer shapes (M = 32, 8-23 MB weights) the kernel measures 9.6-12.8 us per launch inside CUDA
+# graphs against cuBLAS's 5.2-9.9 us, because the cross-CTA reduction of its split-K tiles
+# costs about 5 us per launch; the 22-layer step is faster on cuBLAS (2.08 ms against 2.64 ms).
+LAYER_LINEAR = False
+
+
+def use_linear(x: torch.Tensor, w: torch.Tensor) -> bool:
+    """True when a layer should call linear() for x @ w^T: LAYER_LINEAR and a supported shape."""
+    return LAYER_LINEAR and linear_supported(x, w)
+
+
 def linear_supported(x: torch.Tensor, w: torch.Tensor) -> bool:
-    """Shapes the weight-streaming kernel takes: fp16, M <= 32 rows, N % 64 == 0, K % 256 == 0."""
+    """Shapes the weight-streaming kernel takes: fp16, M <= 32 rows, N % 64 == 0, K % 128 == 0."""
     M = x.numel() // x.shape[-1] if x.shape[-1] else 0
     return (x.is_cuda and x.dtype == torch.float16 and w.dtype == torch.float16 and w.dim() == 2
-            and 0 < M <= 32 and w.shape[0] % 64 == 0 and w.shape[1] % 256 == 0 and x.shape[-1] == w.shape[1])
+            and 0 < M <= 32 and w.shape[0] % 64 == 0 and w.shape[1] % 128 == 0 and x.shape[-1] == w.shape[1])
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = None, gelu: bool = False,

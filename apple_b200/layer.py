@@ -57,7 +57,7 @@ class _Linear:
         also fuses the residual add (fp16(fp16(y) + residual)) or the layer's fp16 tanh-GELU; other
         shapes run the GEMM in cuBLAS and the epilogue separately."""
         w = self.cast(x.dtype)
-        if K.linear_supported(x, w):
+        if K.use_linear(x, w):
             return K.linear(x, w, residual=residual, gelu=gelu)
         y = torch.nn.functional.linear(x, w)
         if gelu:
@@ -133,7 +133,7 @@ class RFSNDecoderLayerMLX:
                 or src[0] is not ws[0] or src[1] is not ws[1] or src[2] is not ws[2]):
             self._qkv_w = torch.cat([w.to(a.dtype) for w in ws], 0)
             self._qkv_src = ws
-        y = K.linear(a, self._qkv_w) if K.linear_supported(a, self._qkv_w) else \
+        y = K.linear(a, self._qkv_w) if K.use_linear(a, self._qkv_w) else \
             torch.nn.functional.linear(a, self._qkv_w)
         nq = self.num_heads * self.head_dim
         nk = self.num_kv_heads * self.head_dim

@@ -62,7 +62,7 @@ def _position_table(component: Any, seq_len: int, head_dim: int, device) -> torc
 
 def _linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     """llama32_adapter.py:492-494: decode-sized products stream W with rfsn_linear_f16, others cuBLAS."""
-    return K.linear(x, w) if K.linear_supported(x, w) else torch.nn.functional.linear(x, w)
+    return K.linear(x, w) if K.use_linear(x, w) else torch.nn.functional.linear(x, w)
 
 
 class Llama32DecoderLayerMLX:
@@ -216,6 +216,6 @@ class Llama32DecoderLayerMLX:
         gu = _linear(mlp_in, self._gate_up_w)
         inter = self.gate_proj_weight.shape[0]
         act = K.silu_mul(gu[..., :inter], gu[..., inter:])
-        if K.linear_supported(act, self.down_proj_weight):  # residual add fused into the epilogue
+        if K.use_linear(act, self.down_proj_weight):  # residual add fused into the epilogue
             return K.linear(act, self.down_proj_weight, residual=hidden)
         return hidden + torch.nn.functional.linear(act, self.down_proj_weight)

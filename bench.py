@@ -442,8 +442,8 @@ def e2e_public_api(w, args, dev, world: int = 1, rank: int = 0, shards=None, pee
             out = cache.attention_forward(h_q, causal=True)
             full = gather_outputs(out.unsqueeze(1), shards, rank, world, G)
             h_full.copy_(full[:, 0])
-        else:
-            h_out.copy_(cache.attention_forward(h_q, causal=True))  # device -> host read of the result
+        else:  # the kernel writes the result into pinned host memory; the call returns once it is there
+            cache.attention_forward(h_q, causal=True, out=h_out)
 
     for _ in range(max(3, args.warmup)):
         step()
@@ -470,8 +470,9 @@ def e2e_public_api(w, args, dev, world: int = 1, rank: int = 0, shards=None, pee
     err = float((ref[:, 0].float().cpu() - got.float()).abs().max())
     nb = h_q.numel() * h_q.element_size()
     cache.close()
-    how = "" if world == 1 else (" with the output all-gather fused over peer memory" if peer is not None
-                                 else " + NCCL all-gather of outputs")
+    how = (" (out= pinned host buffer: the kernel stores the result there, the call waits for the stream)"
+           if world == 1 else (" with the output all-gather fused over peer memory" if peer is not None
+                               else " + NCCL all-gather of outputs"))
     return {"value": world * 1e3 / ms, "unit": UNIT, "h2d_bytes_per_step": nb,
             "d2h_bytes_per_step": nb * (world if world > 1 else 1),
             "api": "RFSNv10KVCacheMLX.attention_forward" + how, "max_abs_diff_vs_kernel_call": err}
@@ -917,7 +918,7 @@ def longctx_setup(dev, **overrides):
     from apple_b200.quantization import HybridQuantizerMLX
     from apple_b200.storage import RFSNConfig
     c = LONG
-    g = torch.Generator(device=dev).manual_seed(c["seed"])
+    g = torch.Generator(device=dev).manual_seed(c["seed"] + int(overrides.pop("seed_offset", 0)))
     B, Hkv, D, T, ch = c["batch"], c["kv_heads"], c["head_dim"], c["context"], c["chunk"]
     nchunks = T // ch
     steps_walk = torch.randn((B, nchunks, Hkv, D), generator=g, device=dev) * 0.05
@@ -991,10 +992,16 @@ def run_longctx(args) -> None:
     import torch
     from apple_b200 import kernels as K
     from apple_b200.storage import AsyncHierarchicalRouterMLX
+    import torch.distributed as dist
     c = LONG
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
     torch.cuda.set_device(dev)
-    cfg, cache, q = longctx_setup(dev)
+    if world > 1:  # weak scaling: each rank holds its own batch of 4 sequences (global batch 4 x world)
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    cfg, cache, q = longctx_setup(dev, seed_offset=rank)
     B, Hkv, T = c["batch"], c["kv_heads"], c["context"]
     router = AsyncHierarchicalRouterMLX(cfg, layer_idx=0)
     # first pass: the router prefetches, misses copy chunk images host -> device
@@ -1028,35 +1035,69 @@ def run_longctx(args) -> None:
         graph.replay()
     steps = max(10, args.steps)
     stream = torch.cuda.current_stream()
+    full = torch.empty((world * B,) + tuple(out.shape[1:]), dtype=out.dtype, device=dev) if world > 1 else None
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(dev) as clocks:
+    with ClockSampler(dev, active=rank == 0, devices=world) as clocks:
+        if world > 1:
+            dist.barrier()
         torch.cuda.synchronize()
         e0.record(stream)
         for _ in range(steps):
             graph.replay()
+            if world > 1:  # the one exchange: every rank's output rows to every rank
+                dist.all_gather_into_tensor(full, out)
         e1.record(stream)
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
     err = float((out[:, 0].float() - out_api.float()).abs().max())
     # e2e: public API with the router every step, pinned host query in, host output out
     hqh = q.cpu().pin_memory()
     hout = torch.empty_like(hqh).pin_memory()
+    hfull = torch.empty((world * B,) + tuple(hqh.shape[1:]), dtype=hqh.dtype).pin_memory() if world > 1 else None
+
+    def e2e_step():
+        y = cache.attention_forward(hqh, causal=True, router=router, current_position=T - 1, context_window=T)
+        if world > 1:
+            dist.all_gather_into_tensor(full[:, 0], y.contiguous())
+            hfull.copy_(full[:, 0])
+        else:
+            hout.copy_(y)
+
     for _ in range(2):
-        hout.copy_(cache.attention_forward(hqh, causal=True, router=router, current_position=T - 1, context_window=T))
+        e2e_step()
     torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
     t0 = time.perf_counter()
     n_e2e = 10
     for _ in range(n_e2e):
-        hout.copy_(cache.attention_forward(hqh, causal=True, router=router, current_position=T - 1, context_window=T))
+        e2e_step()
+    torch.cuda.synchronize()
     e2e_s = (time.perf_counter() - t0) / n_e2e
+    if world > 1:
+        t = torch.tensor([e2e_s], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
     nbytes = long_bytes()
     peak, _ = measured_peak()
     del graph
+    cache.close()
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
     print(json.dumps({
-        "metric": "long-context decode attn steps/s (131K ctx, three tiers)", "value": 1e3 / ms, "unit": "steps/s",
-        "n_gpus": 1, "steps": steps, "warmup": 3, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f16 operands, f32 accumulate", "data": "synthetic",
+        "metric": "long-context decode attn steps/s (131K ctx, three tiers)", "value": world * 1e3 / ms,
+        "unit": "steps/s", "n_gpus": world, "steps": steps, "warmup": 3, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16 operands, f32 accumulate", "data": "synthetic",
         "config": {"workload": "BASELINE configs[3]: batch 4, 131072 ctx, hot 2048 / warm 32768 / cold 188 x 512",
+                   "global_batch": world * B, "batch_per_gpu": B,
+                   "parallelism": f"batch-shard dp{world}" + (", NCCL all-gather of the outputs every step"
+                                                              if world > 1 else ""),
                    "segments": len(segs), "cold_pool": "all 188 chunks device-resident after the first pass"},
         "roofline": {"bound": "hbm", "achieved": nbytes / (ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
                      "frac": nbytes / (ms * 1e-3) / 1e9 / peak, "traffic": None, "algorithmic_bytes_per_step": nbytes},
@@ -1064,11 +1105,12 @@ def run_longctx(args) -> None:
                       "h2d_gbs": cold_fill_bytes / cold_fill_s / 1e9 if cold_fill_s > 0 else None,
                       "stats": {k2: stats[k2] for k2 in ("cold_chunks_touched", "cold_chunk_cache_hits",
                                                           "cold_chunk_cache_misses", "cold_tokens_materialized")}},
-        "e2e": {"value": 1.0 / e2e_s, "unit": "steps/s", "h2d_bytes_per_step": hqh.numel() * 2,
-                "d2h_bytes_per_step": hqh.numel() * 2, "api": "RFSNv10KVCacheMLX.attention_forward with router"},
+        "e2e": {"value": world / e2e_s, "unit": "steps/s", "h2d_bytes_per_step": hqh.numel() * 2,
+                "d2h_bytes_per_step": hqh.numel() * 2 * world, "api": "RFSNv10KVCacheMLX.attention_forward with router"},
         "max_abs_diff_api_vs_graph": err, "gpu_launches": steps, "clocks": clocks.summary(),
-        "cpu_baseline": longctx_cpu_baseline()}))
-    cache.close()
+        **({"cpu_baseline": longctx_cpu_baseline()} if world == 1 else {})}))
+    if world > 1:
+        dist.destroy_process_group()
 
 
 # ---------------------------------------------------------------------------

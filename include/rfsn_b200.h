@@ -194,6 +194,8 @@ int rfsn_peer_free(void* ptr);
  * log-sum-exp.  Also covers RFSNHybridAttentionMLX.__call__ (attention.py:150-170).
  *
  * q / out: fp16 [batch][queries][q_heads][D]; query head hq reads KV head hq / (q_heads/kv_heads).
+ *       out may be device memory or pinned (mapped) host memory, which the kernel then writes
+ *       over the bus: the caller synchronizes the stream before reading it.
  * qpos: int32 [batch][queries][q_heads] global positions; key at position p is visible
  *       iff p <= qpos (causal); ignored when causal == 0.
  * segments: host array in window (position) order; their token counts sum to the window.
@@ -293,10 +295,14 @@ int rfsn_add_rmsnorm_f16(const uint16_t* x, const uint16_t* b, uint16_t* sum, co
  * rfsn_v10_mlx_ane_complete.py:114-172; _linear, llama32_adapter.py:492-494), with an optional fused
  * epilogue: 0 none, 1 y = fp16(fp16(acc) + r) (the residual add after o_proj / ffn_down), 2 y =
  * gelu_tanh(fp16(acc)) rounded to fp16 after every operation (the FFN activation, attention.py:
- * 137-138).  M <= 32, N % 64 == 0, K % 256 == 0; row strides in elements, x and W rows 16-byte
- * aligned.  The workspace (rfsn_linear_workspace_size bytes, 256-byte aligned) holds a launch
- * counter, per-tile tickets and fp32 partials: zero it once when allocated, reuse it without
- * clearing, never share it between calls that overlap in time. */
+ * 137-138).  M <= 32, N % 64 == 0, K % 128 == 0; row strides in elements, x and W rows 16-byte
+ * aligned.  The workspace (rfsn_linear_workspace_size bytes, 256-byte aligned) holds per-tile
+ * tickets, which every completed launch leaves at zero, and fp32 partials: zero it once when
+ * allocated (and again after a launch that set a device status), reuse it without clearing,
+ * never share it between calls that overlap in time (consecutive calls on one stream, of any
+ * shapes, may share it).  The kernel is launched as a programmatic dependent launch: it may begin
+ * streaming W while the previous kernel on the stream finishes, and reads x, r, the workspace
+ * and writes y only after that kernel has completed. */
 int rfsn_linear_workspace_size(int M, int N, int K, size_t* bytes);
 int rfsn_linear_f16(const uint16_t* x, int64_t ldx, const uint16_t* w, int64_t ldw, const uint16_t* r, int64_t ldr,
                     uint16_t* y, int64_t ldy, int M, int N, int K, int epilogue, void* workspace,

@@ -112,6 +112,12 @@ def test_gqa_batch_cache_golden(tmp_path):
         out = cache.attention_forward(q, causal=True, query_positions=[int(qpos)], context_window=win)
         assert [cache.last_access_stats[k] for k in STAT_KEYS] == list(g["stats"][i, 0]), i
         close(out.cpu().numpy(), g["out"][i], f"case {i}")
+        # a pinned host query in, and a pinned host output that the kernel writes itself
+        hq = q.cpu().pin_memory()
+        hout = torch.full(q.shape, float("nan"), dtype=torch.float16).pin_memory()
+        got = cache.attention_forward(hq, causal=True, query_positions=[int(qpos)], context_window=win, out=hout)
+        assert got.data_ptr() == hout.data_ptr()
+        assert torch.equal(hout, out.cpu()), i
     cache.close()
 
 
@@ -316,11 +322,15 @@ def test_reference_chunk_file_into_device_store():
         np.testing.assert_array_equal(u16(out[0]), u16(oq.decode(codes)))
 
 
-def test_llama_layer_golden(tmp_path):
+@pytest.mark.parametrize("layer_linear", [False, True])
+def test_llama_layer_golden(tmp_path, monkeypatch, layer_linear):
     """Llama32DecoderLayerMLX (llama32_adapter.py:417-662) against the reference run through the
-    shim: prefill, 20 cache-backed decode steps through hot, warm and cold, and the dense path.
-    fp16 outputs up to ~5 in magnitude: within one fp16 step (atol 4e-3) plus 2e-3 relative."""
+    shim: prefill, 20 cache-backed decode steps through hot, warm and cold, and the dense path;
+    projections on cuBLAS and on rfsn_linear_f16.  fp16 outputs up to ~5 in magnitude: within
+    one fp16 step (atol 4e-3) plus 2e-3 relative."""
+    from apple_b200 import kernels as Kmod
     from apple_b200.llama import Llama32DecoderLayerMLX
+    monkeypatch.setattr(Kmod, "LAYER_LINEAR", layer_linear)
     g = dict(np.load(GOLDEN / "llama_layer.npz"))
     D = 64
     hidden = g["x"].shape[-1]
@@ -476,9 +486,13 @@ def test_decoder_layer_cached_decode_matches_dense(tmp_path):
     assert layer.cache_tokens == 40
 
 
-def test_decoder_layer_golden(tmp_path):
+@pytest.mark.parametrize("layer_linear", [False, True])
+def test_decoder_layer_golden(tmp_path, monkeypatch, layer_linear):
     """RFSNDecoderLayerMLX vs the reference layer (rfsn_v10_mlx_ane_complete.py:55-172): prefill 40
-    tokens, 24 cache-backed decode steps through hot, warm and cold tiers, and the dense path."""
+    tokens, 24 cache-backed decode steps through hot, warm and cold tiers, and the dense path;
+    projections on cuBLAS, and on rfsn_linear_f16 with the GELU and residual add fused."""
+    from apple_b200 import kernels as Kmod
+    monkeypatch.setattr(Kmod, "LAYER_LINEAR", layer_linear)
     g = dict(np.load(GOLDEN / "decoder_layer.npz"))
     cfg = RFSNConfig(hidden_dim=256, num_heads=4, head_dim=64, num_subspaces=8, subspace_dim=8, num_rvq_layers=1,
                      rvq_codebook_size=64, rvq_sparsity_threshold=0.3, hot_capacity=16, warm_capacity=24,

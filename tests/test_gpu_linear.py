@@ -1,18 +1,24 @@
 """Weight-streaming projection (rfsn_linear_f16) against a torch fp32 reference.
 
-y = fp16(x32 @ w32^T) (+ the fused epilogues: residual add, tanh-GELU in fp16
-steps).  The kernel sums in a different order than the reference, so an
-element may differ where the fp32 value sits on an fp16 rounding boundary: at
-most one fp16 step, and equal in most elements.
+y = fp16(x32 @ w32^T).  The kernel sums in its own fixed order (per-chunk MMA
+sums, then the K-chunk shares in order), so it is compared with the float64
+product through the error bound of fp32 summation: |y - ref| <= 2^-11 |ref| (the
+fp16 rounding) + K 2^-24 sum|x||w| (fp32 accumulation of K products).  Most
+elements round to the same fp16 value as the float64 product.  The fused
+epilogues are checked exactly against the kernel's own plain product: residual
+y = fp16(fp16(acc) + r), and the layer's fp16 tanh-GELU chain within one fp16
+step (tanhf's last bit).
 """
-import numpy as np
 import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
 
 if torch.cuda.is_available():
-    from apple_b200 import kernels as K
+    from apple_b200 import kernels as kern
+
+SHAPES = [(1, 64, 128), (7, 192, 512), (32, 2560, 2048), (32, 2048, 4096), (17, 4096, 768), (32, 2048, 5632),
+          (32, 5632, 2048), (3, 128, 384)]
 
 
 def _ulps(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
@@ -33,24 +39,65 @@ def _gelu_chain(h: torch.Tensor) -> torch.Tensor:
     return (r(0.5 * x) * r(1.0 + t)).to(torch.float16)
 
 
-@pytest.mark.parametrize("M,N,K", [(1, 64, 256), (7, 192, 512), (32, 2560, 2048), (32, 2048, 4096), (17, 4096, 768)])
-@pytest.mark.parametrize("mode", ["none", "residual", "gelu"])
-def test_linear_vs_fp32_reference(M, N, K, mode):
-    g = torch.Generator(device="cuda").manual_seed(M * 7 + N + K)
+def _inputs(M, N, K, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
     wide = torch.randn((M, K + 64), generator=g, device="cuda").half()
     x = wide[:, 32:32 + K]  # strided rows: the layer passes views of wider activations
     w = (torch.randn((N, K), generator=g, device="cuda") / K ** 0.5).half()
     r = torch.randn((M, N), generator=g, device="cuda").half()
-    y = K.linear(x, w, residual=r if mode == "residual" else None, gelu=mode == "gelu")
-    ref = (x.float() @ w.float().T).half()
-    if mode == "residual":
-        ref = (ref.float() + r.float()).half()
-    elif mode == "gelu":
-        ref = _gelu_chain(ref)
+    return x, w, r
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_linear_vs_fp32_reference(M, N, K):
+    x, w, r = _inputs(M, N, K, M * 7 + N + K)
+    y = kern.linear(x, w)
+    ref = x.double() @ w.double().T
+    bound = 2.0 ** -11 * ref.abs() + K * 2.0 ** -24 * (x.double().abs() @ w.double().abs().T)
+    err = (y.double() - ref).abs()
+    assert bool((err <= bound).all()), float((err / bound).max())
+    assert float((y == ref.half()).float().mean()) > 0.9
+    # fused epilogues on the same sums
+    y_res = kern.linear(x, w, residual=r)
+    assert torch.equal(y_res, (y.float() + r.float()).half())
+    y_gelu = kern.linear(x, w, gelu=True)
+    dg = _ulps(y_gelu, _gelu_chain(y))
+    assert int(dg.max()) <= 1 and int((dg != 0).sum()) <= max(2, dg.numel() // 1000), (int(dg.max()), int((dg != 0).sum()))
+    # the sum order is fixed: a second call is bit-identical
+    assert torch.equal(kern.linear(x, w), y)
+
+
+def test_linear_chain_in_graph_replays():
+    """Two projections back to back on one stream (the second starts early under programmatic
+    dependent launch and shares the workspace), captured once and replayed on new inputs."""
+    M, H, F = 32, 2048, 5632
+    g = torch.Generator(device="cuda").manual_seed(5)
+    w1 = (torch.randn((F, H), generator=g, device="cuda") / H ** 0.5).half()
+    w2 = (torch.randn((H, F), generator=g, device="cuda") / F ** 0.5).half()
+    x = torch.randn((M, H), generator=g, device="cuda").half()
+    res = torch.randn((M, H), generator=g, device="cuda").half()
+
+    def chain():
+        a = kern.linear(x, w1, gelu=True)
+        return kern.linear(a, w2, residual=res)
+
+    for _ in range(2):
+        chain()
     torch.cuda.synchronize()
-    d = _ulps(y, ref)
-    assert int(d.max()) <= 1 if mode != "gelu" else int(d.max()) <= 2, (int(d.max()), mode)
-    assert float((d == 0).float().mean()) > 0.95
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        out = chain()
+    for i in range(4):
+        x.copy_(torch.randn((M, H), generator=g, device="cuda").half())
+        res.copy_(torch.randn((M, H), generator=g, device="cuda").half())
+        out.fill_(float("nan"))
+        graph.replay()
+        want = chain()
+        torch.cuda.synchronize()
+        assert torch.equal(out, want), i
+    del graph
 
 
 def test_linear_rejects_unsupported_shapes():
@@ -58,6 +105,6 @@ def test_linear_rejects_unsupported_shapes():
     w = torch.zeros((64, 256), dtype=torch.float16, device="cuda")
     from apple_b200 import RFSNError
     with pytest.raises(RFSNError):
-        K.linear(x, w)  # more than 32 rows
+        kern.linear(x, w)  # more than 32 rows
     with pytest.raises(RFSNError):
-        K.linear(x[:4, :200].contiguous(), w[:, :200].contiguous())  # K not a multiple of 256
+        kern.linear(x[:4, :200].contiguous(), w[:, :200].contiguous())  # K not a multiple of 128
