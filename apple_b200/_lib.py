@@ -91,6 +91,8 @@ SIGNATURES = {
                                                 C.POINTER(C.c_size_t)]),
     "rfsn_decode_attention": (C.c_int, [C.POINTER(AttnArgs), C.POINTER(Quantizer), C.c_void_p]),
     "rfsn_decode_attention_noalloc": (C.c_int, [C.POINTER(AttnArgs), C.POINTER(Quantizer), C.c_void_p]),
+    "rfsn_decode_attention_host": (C.c_int, [C.POINTER(AttnArgs), C.POINTER(Quantizer), C.c_void_p, C.c_void_p,
+                                             C.c_int, C.c_void_p]),
     "rfsn_route_topk": (C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                                   C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "rfsn_peer_alloc": (C.c_int, [C.c_size_t, C.POINTER(C.c_void_p), C.c_void_p]),

@@ -85,6 +85,7 @@ class RFSNv10KVCacheMLX:
         self._cold: Optional[ColdTier] = None
         self._cold_root: Optional[Path] = None
         self._plan_cache: Dict[Tuple, Tuple[List, Dict[str, int], Tuple]] = {}
+        self._q_stage: Dict[Tuple, torch.Tensor] = {}  # device staging buffers of host queries, by shape
         # prepared attention calls for cached plans; _store_epoch changes whenever a store
         # buffer or the quantizer is replaced, which retires the calls that point at them
         self._attn_calls: Dict[Tuple, Any] = {}
@@ -580,6 +581,24 @@ class RFSNv10KVCacheMLX:
             qb = qb.contiguous()
         return qb, squeeze
 
+    def _staged_queries(self, q: torch.Tensor) -> Tuple[torch.Tensor, bool]:
+        """The device staging buffer a host query is copied into, shaped as _queries shapes an
+        upload ([1, Q, Hq, D], [B, 1, Hq, D] or [B, Q, Hq, D]); its contents are written by the
+        library call that uses it, on the stream, after every earlier call's kernels."""
+        if self.batch == 1 and q.dim() == 3:
+            shape, squeeze = (1,) + tuple(q.shape), True
+        elif q.dim() == 3 and q.shape[0] == self.batch:
+            shape, squeeze = (q.shape[0], 1) + tuple(q.shape[1:]), False
+        elif q.dim() == 4 and q.shape[0] == self.batch:
+            shape, squeeze = tuple(q.shape), False
+        else:
+            raise ValueError(f"q must be [Q, H, D] (batch 1), [B, H, D] or [B, Q, H, D]; got {tuple(q.shape)}")
+        stage = self._q_stage.get(shape)
+        if stage is None:
+            stage = torch.empty(shape, dtype=torch.float16, device=self.device)
+            self._q_stage[shape] = stage
+        return stage, squeeze
+
     def _qpos(self, query_positions, start, end, qb: torch.Tensor) -> Optional[torch.Tensor]:
         """Per-query last visible positions [B, Q, Hq] int32, or None when every query sits at
         the window's last position end - 1: then causal masking hides no key of the window
@@ -627,7 +646,12 @@ class RFSNv10KVCacheMLX:
         del pq_codebook, rvq_codebook  # ignored by the reference too (cache.py:406)
         if self.quantizer is None:
             raise RuntimeError("Cache cannot run attention before update() provides a quantizer")
-        qb, squeeze = self._queries(q)
+        # pinned host query and pinned host output: one library call uploads the query into a
+        # device staging buffer, runs the attention, whose kernel stores the result straight into
+        # the host buffer, and waits for the stream (rfsn_decode_attention_host)
+        host_call = (out is not None and gather is None and not q.is_cuda and not out.is_cuda
+                     and q.dtype == torch.float16 and q.is_contiguous() and q.is_pinned() and out.is_pinned())
+        qb, squeeze = self._staged_queries(q) if host_call else self._queries(q)
         start, end, _ = self._window_bounds(query_positions, context_window, current_position, adjusted=False)
         # without a cold tier or router the plan depends only on the window and the tier
         # layout, so a decode loop that reads the same window reuses it
@@ -684,9 +708,12 @@ class RFSNv10KVCacheMLX:
                 if len(self._attn_calls) > 32:
                     self._attn_calls.clear()
                 self._attn_calls[ck] = entry
-        K.run_attention(entry, qb, out, qpos)
-        if host_out:  # the kernel's stores to host memory are complete and visible
-            torch.cuda.current_stream(qb.device).synchronize()
+        if host_call:
+            K.run_attention_host(entry, q, qb, out, qpos, synchronize=True)
+        else:
+            K.run_attention(entry, qb, out, qpos)
+            if host_out:  # the kernel's stores to host memory are complete and visible
+                torch.cuda.current_stream(qb.device).synchronize()
         if gather is not None:
             full = gather.full
             return full[:, 0] if (q.dim() == 3 and not squeeze) else full

@@ -967,6 +967,30 @@ extern "C" int rfsn_decode_attention(const rfsn_attn_args* args, const rfsn_quan
   return check_cuda(launch(pl, s));
 }
 
+// rfsn_decode_attention_host: the call with the query in host memory.  The query's
+// bytes are copied into the caller's device staging buffer on the stream, the
+// attention reads them from there, and with `synchronize` the call returns once
+// the stream has finished, so an output in pinned (mapped) host memory, which the
+// kernel writes over the bus, is then ready to read.
+extern "C" int rfsn_decode_attention_host(const rfsn_attn_args* args, const rfsn_quantizer* qz,
+                                          const uint16_t* q_host, uint16_t* q_stage, int synchronize, void* stream) {
+  if (!args || !q_host || !q_stage) return RFSN_ERR_INVALID_ARGUMENT;
+  if (args->batch <= 0 || args->queries <= 0 || args->q_heads <= 0 || args->head_dim <= 0)
+    return RFSN_ERR_INVALID_ARGUMENT;
+  if (args->q_batch_stride != 0 &&
+      args->q_batch_stride != (int64_t)args->queries * args->q_heads * args->head_dim)
+    return RFSN_ERR_INVALID_ARGUMENT;  // the staged query is packed
+  const size_t bytes = (size_t)args->batch * args->queries * args->q_heads * args->head_dim * sizeof(uint16_t);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(q_stage, q_host, bytes, cudaMemcpyHostToDevice, s);
+  if (e != cudaSuccess) return check_cuda(e);
+  rfsn_attn_args a = *args;
+  a.q = q_stage;
+  const int st = rfsn_decode_attention(&a, qz, stream);
+  if (st != RFSN_OK || !synchronize) return st;
+  return check_cuda(cudaStreamSynchronize(s));
+}
+
 // ---------------------------------------------------------------------------
 // rfsn_decode_attention_noalloc: the same attention with partials kept in a
 // fixed module-scope buffer instead of a caller-provided workspace.

@@ -336,6 +336,25 @@ def run_attention(entry: "_AttnCall", q: torch.Tensor, out: torch.Tensor, qpos: 
     _lib.check("rfsn_decode_attention", status)
 
 
+def run_attention_host(entry: "_AttnCall", q_host: torch.Tensor, stage: torch.Tensor, out: torch.Tensor,
+                       qpos: Optional[torch.Tensor] = None, synchronize: bool = True) -> None:
+    """Launch a prepared call with the query in pinned host memory (rfsn_decode_attention_host):
+    the library copies q_host into `stage` (a contiguous device tensor shaped like the prepared
+    call's q) on the stream and runs the attention; with synchronize it returns once the stream
+    has finished, so a pinned host `out`, which the kernel writes over the bus, holds the result."""
+    a = entry.args
+    a.out = out.data_ptr()
+    a.qpos = qpos.data_ptr() if qpos is not None else None
+    a.device_status = None
+    stream = _stream(stage.device.index)
+    args = (C.byref(a), C.byref(entry.qs), q_host.data_ptr(), stage.data_ptr(), int(bool(synchronize)), stream)
+    status = lib().rfsn_decode_attention_host(*args)
+    if status == _lib.RFSN_ERR_WORKSPACE_TOO_SMALL:
+        _size_workspace(entry, stage.device)
+        status = lib().rfsn_decode_attention_host(*args)
+    _lib.check("rfsn_decode_attention_host", status)
+
+
 def _size_workspace(entry: "_AttnCall", device: torch.device) -> None:
     a = entry.args
     nbytes = C.c_size_t(0)

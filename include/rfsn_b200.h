@@ -233,6 +233,16 @@ int rfsn_attention_workspace_size(const rfsn_attn_args* args, const rfsn_quantiz
 
 int rfsn_decode_attention(const rfsn_attn_args* args, const rfsn_quantizer* qz, void* stream);
 
+/* rfsn_decode_attention with the query in HOST memory (the reference-facing call with host
+ * buffers).  q_host: the packed fp16 query [batch][queries][q_heads][D] (pinned memory lets the
+ * copy run asynchronously); q_stage: a device buffer of the same size the call copies it into on
+ * the stream (args->q is ignored; args->q_batch_stride must be 0 or the packed stride).  args->out
+ * may be device memory or pinned (mapped) host memory.  synchronize != 0: return after the stream
+ * has finished, so a host out holds the result.  Replaces the upload + attention_forward + read of
+ * cache.py:395-428 driven from a host caller. */
+int rfsn_decode_attention_host(const rfsn_attn_args* args, const rfsn_quantizer* qz, const uint16_t* q_host,
+                               uint16_t* q_stage, int synchronize, void* stream);
+
 /* Allocation-free decode attention.  No counterpart in the reference: it is an
  * addition for callers that cannot allocate device memory when they run
  * attention (a host binding that holds only q/out/store pointers, a runtime

@@ -80,6 +80,12 @@ def test_cache_tiers_golden(tmp_path):
         out = cache.attention_forward(q, causal=True, query_positions=[int(qpos)], context_window=win)
         assert [cache.last_access_stats[k] for k in STAT_KEYS] == list(g[f"{tag}_stats"]), tag
         close(out.cpu().numpy(), g[f"{tag}_out"], tag)
+        # the same call from pinned host buffers (one library call: upload, attention, wait)
+        hq = q.cpu().pin_memory()
+        hout = torch.full(q.shape, float("nan"), dtype=torch.float16).pin_memory()
+        cache.attention_forward(hq, causal=True, query_positions=[int(qpos)], context_window=win, out=hout)
+        assert torch.equal(hout, out.cpu()), tag
+        assert [cache.last_access_stats[k] for k in STAT_KEYS] == list(g[f"{tag}_stats"]), tag
         kw, vw, adj = cache.materialize_window([int(qpos)], win)
         np.testing.assert_array_equal(u16(kw), u16(g[f"{tag}_keys"]))
         np.testing.assert_array_equal(u16(vw), u16(g[f"{tag}_values"]))
