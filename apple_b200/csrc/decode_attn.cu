@@ -201,13 +201,55 @@ __device__ __noinline__ void gather_finish(const AttnParams& p, int parity, vola
   }
 }
 
-// Gather mode: one output element into every rank's gathered-output buffer of this parity.
-__device__ __noinline__ void push_to_peers(const AttnParams& p, int parity, int b, int qi, int h, int d, uint16_t v) {
-  const int64_t gi = (int64_t)parity * p.full_elems + (((p.seq_offset + b) * p.Q + qi) * p.Hq + h) * (int64_t)p.D + d;
-  for (int k = 0; k < p.npeers; ++k) p.peer_buf[k][gi] = v;
+// Gather mode: merge 8 consecutive dims of one query row per thread (the same fp32 operations
+// per element, in the same order, as the scalar loop below) and store them as one 16-byte
+// write to the local output and one to every rank's gathered-output buffer of this parity.
+__device__ __noinline__ void merge_row_push(const AttnParams& p, int64_t row, int tid, int nthr, int parity) {
+  int64_t c0;
+  const int np = row_pieces(p, row, &c0);
+  const int b = (int)(row / p.Hkv), kvh = (int)(row % p.Hkv);
+  const float NEG_INF = __int_as_float(0xff800000);
+  const int D8 = p.D / 8;
+  for (int idx = tid; idx < p.R * D8; idx += nthr) {
+    const int r = idx / D8, d = (idx - r * D8) * 8;
+    float M = NEG_INF;
+    for (int k = 0; k < np; ++k) M = fmaxf(M, __ldcg(&p.ws_ml[((row * p.max_pieces + k) * p.R + r) * 2]));
+    float O[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, L = 0.f;
+    if (M != NEG_INF) {
+      for (int k = 0; k < np; ++k) {
+        const int64_t pb = (row * p.max_pieces + k) * p.R + r;
+        const float mk = __ldcg(&p.ws_ml[pb * 2]);
+        if (mk == NEG_INF) continue;
+        const float sc = ex2_approx(mk - M);
+        const float4 o0 = __ldcg(reinterpret_cast<const float4*>(&p.ws_o[pb * p.D + d]));
+        const float4 o1 = __ldcg(reinterpret_cast<const float4*>(&p.ws_o[pb * p.D + d + 4]));
+        O[0] = __fmaf_rn(o0.x, sc, O[0]); O[1] = __fmaf_rn(o0.y, sc, O[1]);
+        O[2] = __fmaf_rn(o0.z, sc, O[2]); O[3] = __fmaf_rn(o0.w, sc, O[3]);
+        O[4] = __fmaf_rn(o1.x, sc, O[4]); O[5] = __fmaf_rn(o1.y, sc, O[5]);
+        O[6] = __fmaf_rn(o1.z, sc, O[6]); O[7] = __fmaf_rn(o1.w, sc, O[7]);
+        L = __fmaf_rn(__ldcg(&p.ws_ml[pb * 2 + 1]), sc, L);
+      }
+    }
+    uint32_t h[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const uint32_t lo = f2h(L > 0.f ? O[2 * e] / L : 0.f), hi = f2h(L > 0.f ? O[2 * e + 1] / L : 0.f);
+      h[e] = lo | (hi << 16);
+    }
+    const uint4 v = make_uint4(h[0], h[1], h[2], h[3]);
+    const int qi = r / p.G, g = r - qi * p.G;
+    *reinterpret_cast<uint4*>(&p.out[(((size_t)b * p.Q + qi) * p.Hq + kvh * p.G + g) * p.D + d]) = v;
+    const int64_t gi = (int64_t)parity * p.full_elems +
+                       (((p.seq_offset + b) * p.Q + qi) * p.Hq + kvh * p.G + g) * (int64_t)p.D + d;
+    for (int k = 0; k < p.npeers; ++k) *reinterpret_cast<uint4*>(p.peer_buf[k] + gi) = v;
+  }
 }
 
 __device__ __forceinline__ void merge_row(const AttnParams& p, int64_t row, int tid, int nthr, int parity) {
+  if (p.npeers) {
+    merge_row_push(p, row, tid, nthr, parity);
+    return;
+  }
   int64_t c0;
   const int np = row_pieces(p, row, &c0);
   const int b = (int)(row / p.Hkv), kvh = (int)(row % p.Hkv);
@@ -231,7 +273,6 @@ __device__ __forceinline__ void merge_row(const AttnParams& p, int64_t row, int 
     const int qi = r / p.G, g = r - qi * p.G;
     const uint16_t h = f2h(o);
     p.out[(((size_t)b * p.Q + qi) * p.Hq + kvh * p.G + g) * p.D + d] = h;
-    if (p.npeers) push_to_peers(p, parity, b, qi, kvh * p.G + g, d, h);
   }
 }
 
@@ -641,9 +682,12 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) rfsn_decode_attn_kernel(cons
   // The done count is a plain counter that is zero between launches (the last CTA
   // resets it): one atomicAdd per CTA, where compare-and-swap tickets retried by
   // 148 CTAs finishing together serialise on round trips.
-  if (p.npeers) {  // a CTA that stored rows to the peers orders them before it counts itself done
+  if (p.npeers) {
+    // A CTA that stored rows to the peers orders them before it counts itself done.  GPU scope
+    // is enough here: the launch's last CTA observes this count, fences at system scope and then
+    // releases the peers' flags, and that release carries every store ordered before it.
     named_bar_sync(2, NW * 32);
-    if (abort[3]) __threadfence_system();
+    if (abort[3]) __threadfence();
     named_bar_sync(2, NW * 32);
   }
   if (threadIdx.x == 0) {
@@ -857,7 +901,10 @@ static int make_plan(const rfsn_attn_args* a, const rfsn_quantizer* qz, Plan& pl
     if (g.num_ranks < 2 || g.num_ranks > RFSN_MAX_PEERS || g.rank < 0 || g.rank >= g.num_ranks || !g.step ||
         !g.out_full || g.seq_offset < 0 || g.seq_offset + a->batch > g.total_seqs)
       return RFSN_ERR_INVALID_ARGUMENT;
-    if (reinterpret_cast<uintptr_t>(g.out_full) & 15) return RFSN_ERR_ALIGNMENT;
+    // the merge stores 8 dims at a time: the local output and the buffers 16-byte aligned
+    if ((reinterpret_cast<uintptr_t>(g.out_full) & 15) || (reinterpret_cast<uintptr_t>(a->out) & 15) ||
+        (a->head_dim % 8))
+      return RFSN_ERR_ALIGNMENT;
     for (int k = 0; k < g.num_ranks; ++k) {
       if (!g.buffers[k] || !g.flags[k]) return RFSN_ERR_INVALID_ARGUMENT;
       if ((reinterpret_cast<uintptr_t>(g.buffers[k]) & 15) || (reinterpret_cast<uintptr_t>(g.flags[k]) & 7))
