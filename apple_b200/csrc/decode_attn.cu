@@ -146,13 +146,17 @@ __device__ __forceinline__ int row_pieces(const AttnParams& p, int64_t row, int6
 
 // Log-sum-exp merge of a row's pieces (m in log2 units) and the fp16 output
 // (attention.py:104-105: a row whose every key is masked outputs zeros).
-__device__ __forceinline__ void st_release_sys(unsigned long long* a, unsigned long long v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
+// Flag words shared between GPUs.  The signalling thread fences once at system scope and then
+// stores every rank's flag relaxed (a fence followed by relaxed stores releases everything
+// before the fence); the waiting thread polls relaxed and fences once after it has seen every
+// flag (relaxed loads followed by a fence acquire what the flags' writers released).
+__device__ __forceinline__ void st_relaxed_sys(unsigned long long* a, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
 }
 
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* a) {
+__device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned long long* a) {
   unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
   return v;
 }
 
@@ -165,18 +169,19 @@ __device__ __noinline__ void gather_finish(const AttnParams& p, int parity, vola
     __threadfence_system();
     const unsigned long long s = *reinterpret_cast<volatile unsigned long long*>(p.step) + 1ull;
     *reinterpret_cast<volatile unsigned long long*>(p.step) = s;
-    for (int k = 0; k < p.npeers; ++k) st_release_sys(p.peer_flags[k] + p.my_rank, s);
+    for (int k = 0; k < p.npeers; ++k) st_relaxed_sys(p.peer_flags[k] + p.my_rank, s);  // after the fence above
     int good = 1;
     const unsigned long long* mine = p.peer_flags[p.my_rank];
     const uint64_t t0 = global_timer_ns();
     for (int r = 0; r < p.npeers && good; ++r) {
-      for (uint32_t it = 0; ld_acquire_sys(mine + r) < s; ++it) {
+      for (uint32_t it = 0; ld_relaxed_sys(mine + r) < s; ++it) {
         if ((it & 63u) == 63u && global_timer_ns() - t0 > kWaitLimitNs) {
           good = 0;
           break;
         }
       }
     }
+    if (good) __threadfence_system();  // acquires the peers' rows their flags released
     if (!good && p.dev_status) atomicExch(p.dev_status, kDevStatusPeerTimeout);
     *ok = good;
   }
