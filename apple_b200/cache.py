@@ -86,6 +86,7 @@ class RFSNv10KVCacheMLX:
         self._cold_root: Optional[Path] = None
         self._plan_cache: Dict[Tuple, Tuple[List, Dict[str, int], Tuple]] = {}
         self._q_stage: Dict[Tuple, torch.Tensor] = {}  # device staging buffers of host queries, by shape
+        self._host_memo: Optional[Tuple] = None  # the last host call: its key and what it reuses
         # prepared attention calls for cached plans; _store_epoch changes whenever a store
         # buffer or the quantizer is replaced, which retires the calls that point at them
         self._attn_calls: Dict[Tuple, Any] = {}
@@ -651,6 +652,22 @@ class RFSNv10KVCacheMLX:
         # the host buffer, and waits for the stream (rfsn_decode_attention_host)
         host_call = (out is not None and gather is None and not q.is_cuda and not out.is_cuda
                      and q.dtype == torch.float16 and q.is_contiguous() and q.is_pinned() and out.is_pinned())
+        # a decode loop that calls again from the same host buffers against an unchanged cache
+        # (the same window, tiers and stores) reuses the last host call's plan, prepared
+        # arguments, staging buffer, positions and statistics
+        memo_key = None
+        if host_call and router is None and not self.cold_chunk_metadata:
+            qp = None if query_positions is None else _int_list(query_positions)
+            if query_positions is None or qp is not None:
+                memo_key = (q.data_ptr(), tuple(q.shape), out.data_ptr(), tuple(out.shape), bool(causal),
+                            None if qp is None else tuple(qp), context_window, current_position, self.total_tokens,
+                            self.num_hot, self.num_warm, self._hot_start, self._warm_start, self._store_epoch)
+                memo = self._host_memo
+                if memo is not None and memo[0] == memo_key:
+                    _, entry, stage, qpos, stats, ret = memo
+                    self.last_access_stats = dict(stats)
+                    K.run_attention_host(entry, q, stage, out, qpos, synchronize=True)
+                    return ret
         qb, squeeze = self._staged_queries(q) if host_call else self._queries(q)
         start, end, _ = self._window_bounds(query_positions, context_window, current_position, adjusted=False)
         # without a cold tier or router the plan depends only on the window and the tier
@@ -717,9 +734,10 @@ class RFSNv10KVCacheMLX:
         if gather is not None:
             full = gather.full
             return full[:, 0] if (q.dim() == 3 and not squeeze) else full
-        if squeeze:
-            return out[0]
-        return out.reshape(q.shape) if q.dim() == 3 else out
+        ret = out[0] if squeeze else (out.reshape(q.shape) if q.dim() == 3 else out)
+        if memo_key is not None and ck is not None:
+            self._host_memo = (memo_key, entry, qb, qpos, dict(stats), ret)
+        return ret
 
     def memory_usage_bytes(self) -> Dict[str, int]:
         """cache.py:430-440 (same formulas: hot K+V fp16, PQ 2 bytes per code, RVQ 2 bytes per code)."""

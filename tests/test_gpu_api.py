@@ -127,6 +127,38 @@ def test_gqa_batch_cache_golden(tmp_path):
     cache.close()
 
 
+def test_host_buffer_calls_repeat_and_advance(tmp_path):
+    """Decode-loop use of the host-buffer path: the same pinned buffers with new query values
+    each call (the cache reuses the last call's plan), then a token appended to the cache (the
+    next call plans again); every output equals the device-resident call on the same query."""
+    g = dict(np.load(GOLDEN / "gqa_batch_cache.npz"))
+    B, T, Hkv, D = g["keys"].shape
+    Hq = g["q"].shape[1]
+    # hot and warm tiers hold every token (no cold tier: the case the reuse applies to)
+    cfg = tiers_config(tmp_path, hidden_dim=Hq * D, num_heads=Hq, head_dim=D, num_subspaces=16, subspace_dim=4,
+                       num_rvq_layers=1, rvq_sparsity_threshold=-1.0, num_kv_heads=Hkv, batch_size=B,
+                       warm_capacity=int(T) + 16)
+    qz = golden_quantizer(cfg, g)
+    cache = RFSNv10KVCacheMLX(cfg, layer_idx=0)
+    keys, values = torch.from_numpy(g["keys"]).cuda(), torch.from_numpy(g["values"]).cuda()
+    cache.update(keys[:, :T - 2], values[:, :T - 2], qz)
+    gen = torch.Generator().manual_seed(3)
+    hq = torch.empty((B, Hq, D), dtype=torch.float16).pin_memory()
+    hout = torch.empty((B, Hq, D), dtype=torch.float16).pin_memory()
+    for step in range(6):
+        if step == 3:
+            cache.update(keys[:, T - 2:T - 1], values[:, T - 2:T - 1], qz)
+        hq.copy_(torch.randn((B, Hq, D), generator=gen).half())
+        hout.fill_(float("nan"))
+        cache.attention_forward(hq, causal=True, out=hout)
+        host_stats = dict(cache.last_access_stats)
+        want = cache.attention_forward(hq.cuda(), causal=True)
+        assert torch.equal(hout, want.cpu()), step
+        assert host_stats == cache.last_access_stats, step
+    assert cache.num_cold == 0 and cache._host_memo is not None
+    cache.close()
+
+
 def test_cache_tiers_with_router(tmp_path):
     """Router-driven prefetch: same outputs, hit/miss statistics as the oracle with the router's loads."""
     g = dict(np.load(GOLDEN / "cache_tiers.npz"))
