@@ -36,6 +36,8 @@
 // rescaled only when a row's running max grows.  All waits are bounded
 // (rfsn_common.cuh).
 #include <cuda_runtime.h>
+
+#include <atomic>
 #include <math.h>
 
 #include <mutex>
@@ -950,8 +952,21 @@ static size_t workspace_layout(AttnParams& p, void* base) {
 template <int D, int RMAX, int NW, int LP>
 static cudaError_t launch_variant(const Plan& pl, cudaStream_t s) {
   auto kern = rfsn_decode_attn_kernel<D, RMAX, NW, LP>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
-  if (e != cudaSuccess) return e;
+  // the dynamic shared-memory limit is raised once per device to the largest size launched
+  // (a per-launch attribute call costs host time on every decode step)
+  static std::atomic<int> limit[64];
+  int dev = -1;
+  cudaGetDevice(&dev);
+  const int need = (int)pl.smem;
+  if (dev < 0 || dev >= 64 || need > limit[dev].load(std::memory_order_relaxed)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, need);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) {
+      int cur = limit[dev].load(std::memory_order_relaxed);
+      while (need > cur && !limit[dev].compare_exchange_weak(cur, need)) {
+      }
+    }
+  }
   kern<<<pl.grid, (NW + 1) * 32, pl.smem, s>>>(pl.p);
   return cudaGetLastError();
 }
